@@ -1,0 +1,96 @@
+"""ctypes binding of the C ABI in `include/bp_kernels.h` (libbp_kernels.so, built in-tree).
+
+The library is loaded once per process. A missing library or a non-zero status raises: there is no
+fallback path. Every call passes torch's current CUDA stream of the tensor's device, so launches
+are ordered with the surrounding torch work and can be captured in CUDA graphs.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import c_float, c_int, c_longlong, c_void_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libbp_kernels.so"
+
+BP_OK = 0
+BP_DTYPE_BF16, BP_DTYPE_F32, BP_DTYPE_INT8 = 0, 1, 2
+_DTYPE_CODE = {torch.bfloat16: BP_DTYPE_BF16, torch.float32: BP_DTYPE_F32, torch.int8: BP_DTYPE_INT8}
+
+# name -> (restype, argtypes); must match include/bp_kernels.h
+_SIGNATURES = {
+    "bp_abi_version": (c_int, []),
+    "bp_status_string": (ctypes.c_char_p, [c_int]),
+    "bp_last_error": (ctypes.c_char_p, []),
+    "bp_skinny_mm": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_void_p, c_longlong, c_int,
+                             c_int, c_int, c_int, c_void_p]),
+    "bp_gemv_int8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
+    "bp_mlstm_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                              c_int, c_int, c_int, c_int, c_longlong, c_longlong, c_longlong, c_longlong,
+                              c_int, c_int, c_float, c_float, c_void_p]),
+    "bp_mlstm_accept": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+class KernelError(RuntimeError):
+    """A kernel entry point returned a non-zero status."""
+
+    def __init__(self, name: str, status: int, message: str):
+        super().__init__(f"{name}: {message or 'status ' + str(status)} (status {status})")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded library; raises if it has not been built (`python -m byteprof_b200.build`)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m byteprof_b200.build` "
+                               "(there is no fallback implementation)")
+        cdll = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(cdll, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = cdll
+    return _lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def call(name: str, *args) -> None:
+    """Calls an entry point and raises KernelError on a non-zero status."""
+    L = lib()
+    st = getattr(L, name)(*args)
+    if st != BP_OK:
+        msg = L.bp_last_error().decode(errors="replace")
+        raise KernelError(name, st, msg)
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DTYPE_CODE[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}") from None
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t: torch.Tensor) -> int:
+    """torch's current stream on the tensor's device, as a raw cudaStream_t."""
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def require_cuda(*tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if t is not None and not t.is_cuda:
+            raise ValueError("the byteprof B200 kernels take CUDA tensors only (there is no CPU path)")

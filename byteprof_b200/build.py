@@ -1,0 +1,90 @@
+"""Builds the sm_100a kernel library `byteprof_b200/_lib/libbp_kernels.so` in-tree with nvcc.
+
+Each `csrc/*.cu` file is compiled to an object in parallel (`-gencode arch=compute_100a,code=sm_100a`,
+`-lineinfo`, `-O3`), then linked into one shared library that exports the C ABI declared in
+`include/bp_kernels.h`. The CUDA runtime is linked statically, so the library does not depend on
+which libcudart torch loaded. The build is skipped when the library is newer than every source.
+
+    python -m byteprof_b200.build [--force]
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+INCLUDE = ROOT / "include"
+LIB_DIR = PKG / "_lib"
+LIB_PATH = LIB_DIR / "libbp_kernels.so"
+OBJ_DIR = ROOT / "_build" / "obj"
+
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+              "-I", str(INCLUDE)]
+
+
+def nvcc() -> str:
+    cand = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(cand):
+        raise RuntimeError("nvcc not found (needed to build the sm_100a kernels)")
+    return cand
+
+
+def sources() -> list[Path]:
+    return sorted(CSRC.glob("*.cu"))
+
+
+def _stale() -> bool:
+    if not LIB_PATH.exists():
+        return True
+    t = LIB_PATH.stat().st_mtime
+    deps = sources() + sorted(CSRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h")) + [Path(__file__)]
+    return any(p.stat().st_mtime > t for p in deps)
+
+
+def _compile(src: Path) -> Path:
+    obj = OBJ_DIR / (src.stem + ".o")
+    cmd = [nvcc(), *ARCH_FLAGS, *NVCC_FLAGS, "-c", str(src), "-o", str(obj)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed on {src.name}:\n{r.stdout}\n{r.stderr}")
+    return obj
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    """Compile every kernel source for sm_100a and link the C-ABI library; returns its path."""
+    if not force and not _stale():
+        return LIB_PATH
+    OBJ_DIR.mkdir(parents=True, exist_ok=True)
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 1)) as ex:
+        objs = list(ex.map(_compile, sources()))
+    tmp = LIB_PATH.with_suffix(".so.tmp")
+    cmd = [nvcc(), *ARCH_FLAGS, "-shared", "-Xcompiler", "-fPIC", "-o", str(tmp), *map(str, objs)]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(tmp, LIB_PATH)
+    if verbose:
+        print(f"built {LIB_PATH}")
+    return LIB_PATH
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    a = ap.parse_args(argv)
+    build(force=a.force, verbose=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,389 @@
+// Fused mLSTM recurrence over T positions with the (C, n, m) state kept on chip, plus the draft
+// acceptance kernel.
+//
+// Reference: byteprof/optim/mlstm_multistep.py:20-146 (_gates, multistep_fw_kernel,
+// lazy_commit_kernel, accept_kernel) and the library step it restates (mlstm_kernels 2.0.6
+// recurrent_step_fw_kernel, called at byteprof/optim/draft_core.py:114-141).
+//
+// Per position t and head (reference math, mlstm_multistep.py:20-30, 64-85):
+//   f_log = log(sigmoid(f_t)),  m_t = max(f_log + m_{t-1}, i_t)
+//   f_act = exp(f_log + m_{t-1} - m_t),  i_act = exp(i_t - m_t),  max_val = exp(-m_t)
+//   C_t = f_act * C_{t-1} + i_act * (k_t v_t^T),  n_t = f_act * n_{t-1} + i_act * k_t
+//   h_t = (q_t * qk_scale)^T C_t / (max(|(q_t * qk_scale)^T n_t|, max_val) + eps)
+// With bf16 inputs the reference rounds to bf16: f_act, i_act, max_val (.to(DTYPE)), k*v and
+// i_act*(k*v) (bf16 x bf16 stays bf16 under Triton's promotion rules), q*qk_scale (the scalar is
+// cast to bf16 first), C and n before the output dot products and each product q*C, q*n. This
+// kernel applies the same roundings. It accumulates the two dot products in fp32 (the reference
+// reduces the bf16 products in bf16, in an order that depends on its register layout).
+// The gate values are evaluated in double precision and rounded to fp32 at each point where the
+// reference holds an fp32 value, so the bf16 gate values are the correctly rounded ones.
+//
+// B200 design: grid (DV / 16, NH); each CTA owns 16 value columns of one head and keeps that
+// [DQ x 16] fp32 slice of C in registers for all T positions (no per-position HBM round trip of the
+// 4 MiB state). TPC threads share one column (RPT rows each, in 8-row chunks so that q and k are
+// read from shared memory with 16-byte loads). One extra producer warp per CTA
+//   - prefetches q, k, v of position t + 7 with cp.async into an 8-deep shared-memory ring,
+//   - evaluates the gate recurrence 32 positions at a time (double buffered),
+//   - updates n and the q.n denominator, and finishes h_t one position later.
+// One __syncthreads per position. (head, column-block) CTAs are independent: no inter-CTA waits.
+#include "bp_common.cuh"
+
+namespace bp {
+namespace {
+
+constexpr int kBV = 16;    // value columns per CTA
+constexpr int kDepth = 8;  // shared-memory ring depth (positions)
+constexpr int kGC = 32;    // gate chunk (positions)
+
+struct ScanArgs {
+  const float* c_in;
+  const float* n_in;
+  const float* m_in;
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* ig;
+  const void* fg;
+  void* h;
+  float* c_out;
+  float* n_out;
+  float* m_out;
+  float* n_save;
+  float* m_save;
+  const int64_t* steps_dev;
+  int T, NH, DV;
+  long long str_qk, str_v, str_if, str_h;
+  int gate_f32;
+  float qk_scale, eps;
+};
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+// Rounds to the input dtype (the reference's `.to(DTYPE)`): bf16 rounds, fp32 is the identity.
+template <typename T>
+__device__ __forceinline__ float rnd(float v) {
+  if constexpr (sizeof(T) == 2) return round_bf16(v);
+  return v;
+}
+
+template <int DQ, typename T>
+struct ScanCfg {
+  static constexpr int TPC = DQ >= 128 ? 16 : 8;  // threads per value column
+  static constexpr int RPT = DQ / TPC;            // rows of C per thread
+  static constexpr int CH = RPT / 8;              // 8-row chunks per thread
+  static constexpr int NCOMP = kBV * TPC;         // compute threads
+  static constexpr int NTHREADS = NCOMP + 32;     // + one producer warp
+  static constexpr int RPL = DQ / 32;             // rows of n per producer lane
+  static constexpr int STAGE = 2 * DQ + kBV;      // elements of q, k, v for one position
+  static constexpr int CHUNKS16 = STAGE * static_cast<int>(sizeof(T)) / 16;
+};
+
+__device__ __forceinline__ float load_gate(const void* p, long long idx, int is_f32) {
+  if (is_f32) return static_cast<const float*>(p)[idx];
+  return __bfloat162float(static_cast<const __nv_bfloat16*>(p)[idx]);
+}
+
+// Gate values of positions [32 j, 32 j + 32) of one head into slot (position & 63) of the gate
+// buffers. `m_run` is the stabiliser after position 32 j - 1 on entry and after the last valid
+// position of the chunk on exit (identical in every lane).
+template <typename T>
+__device__ void gate_chunk(const ScanArgs& a, int head, int j, int n_steps, float& m_run, float* g_f, float* g_i,
+                           float* g_mx) {
+  const int lane = threadIdx.x & 31;
+  const int s = j * kGC + lane;
+  float fl = 0.0f, iv = 0.0f;
+  if (s < n_steps) {
+    const float fv = load_gate(a.fg, s * a.str_if + head, a.gate_f32);
+    iv = load_gate(a.ig, s * a.str_if + head, a.gate_f32);
+    // sigmoid(x) = 1 / (1 + exp(-x)) with fp32 intermediates, then log.
+    const float e = static_cast<float>(exp(-static_cast<double>(fv)));
+    const float d = __fadd_rn(1.0f, e);
+    const float sig = __fdiv_rn(1.0f, d);
+    fl = static_cast<float>(log(static_cast<double>(sig)));
+  }
+  // The stabiliser recurrence is sequential (each fp32 add rounds): every lane runs it.
+  float m_prev = m_run, my_m = 0.0f, my_a = 0.0f;
+  for (int t = 0; t < kGC; ++t) {
+    const float flt = __shfl_sync(0xffffffffu, fl, t);
+    const float ivt = __shfl_sync(0xffffffffu, iv, t);
+    if (j * kGC + t < n_steps) {
+      const float sum = __fadd_rn(flt, m_prev);
+      const float mn = fmaxf(sum, ivt);
+      if (lane == t) {
+        my_m = mn;
+        my_a = __fsub_rn(sum, mn);
+      }
+      m_prev = mn;
+    }
+  }
+  m_run = m_prev;
+  if (s < n_steps) {
+    const int slot = s & 63;
+    g_mx[slot] = rnd<T>(static_cast<float>(exp(-static_cast<double>(my_m))));
+    g_f[slot] = rnd<T>(static_cast<float>(exp(static_cast<double>(my_a))));
+    g_i[slot] = rnd<T>(static_cast<float>(exp(static_cast<double>(__fsub_rn(iv, my_m)))));
+  }
+}
+
+template <int DQ, typename T>
+__global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(const ScanArgs a) {
+  using Cfg = ScanCfg<DQ, T>;
+  __shared__ __align__(16) T ring[kDepth][Cfg::STAGE];
+  __shared__ float g_f[64], g_i[64], g_mx[64];
+  __shared__ float hb[2][kBV];
+
+  const int head = blockIdx.y;
+  const int c0 = blockIdx.x * kBV;
+  const int tid = threadIdx.x;
+  const bool producer = tid >= Cfg::NCOMP;
+  const int lane = tid & 31;
+  const bool want_h = a.h != nullptr;
+
+  int n_steps = a.T;
+  if (a.steps_dev != nullptr) {
+    long long L = *a.steps_dev + 1;
+    n_steps = static_cast<int>(L < 0 ? 0 : (L > a.T ? a.T : L));
+  }
+
+  const T* qg = static_cast<const T*>(a.q);
+  const T* kg = static_cast<const T*>(a.k);
+  const T* vg = static_cast<const T*>(a.v);
+
+  // Producer: issue the copies of position s into ring slot s % kDepth (one commit group per call).
+  auto issue = [&](int s) {
+    if (s < n_steps) {
+      T* dst = ring[s % kDepth];
+      for (int c = lane; c < Cfg::CHUNKS16; c += 32) {
+        constexpr int per_row = DQ * static_cast<int>(sizeof(T)) / 16;  // 16-byte chunks of q (or k)
+        const char* src;
+        if (c < per_row)
+          src = reinterpret_cast<const char*>(qg + s * a.str_qk + static_cast<long long>(head) * DQ) + 16 * c;
+        else if (c < 2 * per_row)
+          src = reinterpret_cast<const char*>(kg + s * a.str_qk + static_cast<long long>(head) * DQ) + 16 * (c - per_row);
+        else
+          src = reinterpret_cast<const char*>(vg + s * a.str_v + static_cast<long long>(head) * a.DV + c0) +
+                16 * (c - 2 * per_row);
+        cp_async16(reinterpret_cast<char*>(dst) + 16 * c, src);
+      }
+    }
+    cp_async_commit();
+  };
+
+  // ---- prologue --------------------------------------------------------------------------------
+  float creg[Cfg::RPT];                 // compute threads: C[rows, col]
+  float nreg[Cfg::RPL];                 // producer: n[lane + 32 r]
+  float m_run = a.m_in[head];
+  const int col = tid / Cfg::TPC;       // compute threads: value column in the block
+  const int l = tid % Cfg::TPC;
+  const float* cbase = a.c_in + static_cast<long long>(head) * DQ * a.DV + c0;
+
+  if (producer) {
+#pragma unroll
+    for (int r = 0; r < Cfg::RPL; ++r) nreg[r] = a.n_in[head * DQ + lane + 32 * r];
+    if (blockIdx.x == 0) {
+      if (a.n_save != nullptr)
+#pragma unroll
+        for (int r = 0; r < Cfg::RPL; ++r) a.n_save[head * DQ + lane + 32 * r] = nreg[r];
+      if (a.m_save != nullptr && lane == 0) a.m_save[head] = m_run;
+    }
+    for (int s = 0; s < kDepth - 1; ++s) issue(s);
+    gate_chunk<T>(a, head, 0, n_steps, m_run, g_f, g_i, g_mx);
+  } else {
+#pragma unroll
+    for (int ch = 0; ch < Cfg::CH; ++ch)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) creg[ch * 8 + e] = cbase[static_cast<long long>((l + Cfg::TPC * ch) * 8 + e) * a.DV + col];
+  }
+
+  // bf16(qk_scale) in bf16 mode (Triton casts the scalar to the tensor's dtype).
+  const float qsc = rnd<T>(a.qk_scale);
+  float qn_prev = 0.0f;
+
+  // ---- positions ---------------------------------------------------------------------------------
+  for (int t = 0; t < n_steps; ++t) {
+    if (producer) cp_async_wait<kDepth - 2>();
+    __syncthreads();
+    const T* st = ring[t % kDepth];
+    const float fa = g_f[t & 63], ia = g_i[t & 63];
+    if (producer) {
+      if (want_h && t > 0 && lane < kBV) {
+        const float den = __fadd_rn(fmaxf(fabsf(qn_prev), g_mx[(t - 1) & 63]), a.eps);
+        static_cast<T*>(a.h)[(t - 1) * a.str_h + static_cast<long long>(head) * a.DV + c0 + lane] =
+            from_f<T>(__fdiv_rn(hb[(t - 1) & 1][lane], den));
+      }
+      issue(t + kDepth - 1);
+      float qn = 0.0f;
+#pragma unroll
+      for (int r = 0; r < Cfg::RPL; ++r) {
+        const int row = lane + 32 * r;
+        const float kf = to_f<T>(st[DQ + row]);
+        nreg[r] = fmaf(fa, nreg[r], rnd<T>(ia * kf));
+        if (want_h) {
+          const float qs = rnd<T>(to_f<T>(st[row]) * qsc);
+          qn += rnd<T>(qs * rnd<T>(nreg[r]));
+        }
+      }
+      if (want_h) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) qn += __shfl_xor_sync(0xffffffffu, qn, o);
+        qn_prev = qn;
+      }
+      __syncwarp();
+      if ((t & (kGC - 1)) == 0) gate_chunk<T>(a, head, t / kGC + 1, n_steps, m_run, g_f, g_i, g_mx);
+    } else {
+      const float vf = to_f<T>(st[2 * DQ + col]);
+      float hs = 0.0f;
+#pragma unroll
+      for (int ch = 0; ch < Cfg::CH; ++ch) {
+        const int rb = (l + Cfg::TPC * ch) * 8;
+        float kf[8], qf[8];
+        if constexpr (sizeof(T) == 2) {
+          const uint4 kv4 = *reinterpret_cast<const uint4*>(st + DQ + rb);
+          const uint4 qv4 = *reinterpret_cast<const uint4*>(st + rb);
+          kf[0] = bf16lo(kv4.x); kf[1] = bf16hi(kv4.x); kf[2] = bf16lo(kv4.y); kf[3] = bf16hi(kv4.y);
+          kf[4] = bf16lo(kv4.z); kf[5] = bf16hi(kv4.z); kf[6] = bf16lo(kv4.w); kf[7] = bf16hi(kv4.w);
+          qf[0] = bf16lo(qv4.x); qf[1] = bf16hi(qv4.x); qf[2] = bf16lo(qv4.y); qf[3] = bf16hi(qv4.y);
+          qf[4] = bf16lo(qv4.z); qf[5] = bf16hi(qv4.z); qf[6] = bf16lo(qv4.w); qf[7] = bf16hi(qv4.w);
+        } else {
+          const float4* kp = reinterpret_cast<const float4*>(st + DQ + rb);
+          const float4* qp = reinterpret_cast<const float4*>(st + rb);
+          const float4 k0 = kp[0], k1 = kp[1], q0 = qp[0], q1 = qp[1];
+          kf[0] = k0.x; kf[1] = k0.y; kf[2] = k0.z; kf[3] = k0.w; kf[4] = k1.x; kf[5] = k1.y; kf[6] = k1.z; kf[7] = k1.w;
+          qf[0] = q0.x; qf[1] = q0.y; qf[2] = q0.z; qf[3] = q0.w; qf[4] = q1.x; qf[5] = q1.y; qf[6] = q1.z; qf[7] = q1.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float& c = creg[ch * 8 + e];
+          c = fmaf(fa, c, rnd<T>(ia * rnd<T>(kf[e] * vf)));
+          if (want_h) hs += rnd<T>(rnd<T>(qf[e] * qsc) * rnd<T>(c));
+        }
+      }
+      if (want_h) {
+#pragma unroll
+        for (int o = Cfg::TPC / 2; o > 0; o >>= 1) hs += __shfl_xor_sync(0xffffffffu, hs, o);
+        if (l == 0) hb[t & 1][col] = hs;
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // ---- epilogue -----------------------------------------------------------------------------------
+  if (producer) {
+    if (want_h && n_steps > 0 && lane < kBV) {
+      const int t = n_steps - 1;
+      const float den = __fadd_rn(fmaxf(fabsf(qn_prev), g_mx[t & 63]), a.eps);
+      static_cast<T*>(a.h)[t * a.str_h + static_cast<long long>(head) * a.DV + c0 + lane] =
+          from_f<T>(__fdiv_rn(hb[t & 1][lane], den));
+    }
+    if (blockIdx.x == 0) {
+      if (a.n_out != nullptr)
+#pragma unroll
+        for (int r = 0; r < Cfg::RPL; ++r) a.n_out[head * DQ + lane + 32 * r] = nreg[r];
+      if (a.m_out != nullptr && lane == 0) a.m_out[head] = m_run;
+    }
+  } else if (a.c_out != nullptr) {
+    float* obase = a.c_out + static_cast<long long>(head) * DQ * a.DV + c0;
+#pragma unroll
+    for (int ch = 0; ch < Cfg::CH; ++ch)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) obase[static_cast<long long>((l + Cfg::TPC * ch) * 8 + e) * a.DV + col] = creg[ch * 8 + e];
+  }
+}
+
+__global__ void accept_kernel(const int64_t* ids, const int64_t* tok, int64_t* out, int S, int smax) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int64_t alive = 1, n = 0;
+  for (int j = 0; j < S - 1; ++j) {
+    alive = alive && (ids[1 + j] == tok[j]);
+    n += alive;
+  }
+  for (int j = 0; j < S; ++j) out[j] = tok[j];
+  out[smax] = n;
+}
+
+template <int DQ, typename T>
+int launch_scan(const ScanArgs& a, cudaStream_t s) {
+  using Cfg = ScanCfg<DQ, T>;
+  dim3 grid(a.DV / kBV, a.NH, 1);
+  mlstm_scan_kernel<DQ, T><<<grid, Cfg::NTHREADS, 0, s>>>(a);
+  return check_launch("mlstm scan launch");
+}
+
+template <typename T>
+int dispatch_dq(const ScanArgs& a, int DQ, cudaStream_t s) {
+  switch (DQ) {
+    case 64: return launch_scan<64, T>(a, s);
+    case 128: return launch_scan<128, T>(a, s);
+    case 256: return launch_scan<256, T>(a, s);
+    case 512: return launch_scan<512, T>(a, s);
+    default: return fail(BP_ERR_UNSUPPORTED, "head dim DQ = %d is not one of 64, 128, 256, 512", DQ);
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+}  // namespace bp
+
+extern "C" int bp_mlstm_scan(const float* c_in, const float* n_in, const float* m_in, const void* q, const void* k,
+                             const void* v, const void* i_gate, const void* f_gate, void* h, float* c_out, float* n_out,
+                             float* m_out, float* n_save, float* m_save, const int64_t* steps_dev, int T, int NH, int DQ,
+                             int DV, long long str_t_qk, long long str_t_v, long long str_t_if, long long str_t_h,
+                             int dtype, int gate_dtype, float qk_scale, float eps, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (T < 0 || NH <= 0 || DQ <= 0 || DV <= 0) return fail(BP_ERR_INVALID_ARGUMENT, "bad sizes T=%d NH=%d DQ=%d DV=%d", T, NH, DQ, DV);
+  if (dtype != BP_DTYPE_BF16 && dtype != BP_DTYPE_F32) return fail(BP_ERR_INVALID_ARGUMENT, "dtype %d is not bf16 or fp32", dtype);
+  if (gate_dtype != BP_DTYPE_BF16 && gate_dtype != BP_DTYPE_F32)
+    return fail(BP_ERR_INVALID_ARGUMENT, "gate dtype %d is not bf16 or fp32", gate_dtype);
+  if (DV % kBV != 0) return fail(BP_ERR_UNSUPPORTED, "DV = %d is not a multiple of %d", DV, kBV);
+  if (c_in == nullptr || n_in == nullptr || m_in == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "start state is NULL");
+  if (T > 0 && (q == nullptr || k == nullptr || v == nullptr || i_gate == nullptr || f_gate == nullptr))
+    return fail(BP_ERR_INVALID_ARGUMENT, "q, k, v, i or f is NULL");
+  if ((n_out != nullptr && n_out == n_in) || (m_out != nullptr && m_out == m_in))
+    return fail(BP_ERR_INVALID_ARGUMENT, "n_out / m_out must not alias n_in / m_in (other CTAs still read them)");
+  const int vec_elems = dtype == BP_DTYPE_BF16 ? 8 : 4;
+  if (!al16(q) || !al16(k) || !al16(v) || str_t_qk % vec_elems || str_t_v % vec_elems)
+    return fail(BP_ERR_MISALIGNED, "q/k/v need 16-byte aligned bases and position strides that are multiples of %d elements",
+                vec_elems);
+  if (T > 0 && (str_t_qk < static_cast<long long>(NH) * DQ || str_t_v < static_cast<long long>(NH) * DV || str_t_if < NH ||
+                (h != nullptr && str_t_h < static_cast<long long>(NH) * DV)))
+    return fail(BP_ERR_INVALID_ARGUMENT, "a position stride is smaller than one position");
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  ScanArgs a;
+  a.c_in = c_in; a.n_in = n_in; a.m_in = m_in;
+  a.q = q; a.k = k; a.v = v; a.ig = i_gate; a.fg = f_gate; a.h = h;
+  a.c_out = c_out; a.n_out = n_out; a.m_out = m_out; a.n_save = n_save; a.m_save = m_save;
+  a.steps_dev = steps_dev;
+  a.T = T; a.NH = NH; a.DV = DV;
+  a.str_qk = str_t_qk; a.str_v = str_t_v; a.str_if = str_t_if; a.str_h = str_t_h;
+  a.gate_f32 = gate_dtype == BP_DTYPE_F32;
+  a.qk_scale = qk_scale; a.eps = eps;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return dtype == BP_DTYPE_BF16 ? dispatch_dq<__nv_bfloat16>(a, DQ, s) : dispatch_dq<float>(a, DQ, s);
+}
+
+extern "C" int bp_mlstm_accept(const int64_t* ids, const int64_t* tok, int64_t* out, int S, int smax, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (S < 0 || smax < S) return fail(BP_ERR_INVALID_ARGUMENT, "need 0 <= S <= smax (S=%d smax=%d)", S, smax);
+  if (ids == nullptr || tok == nullptr || out == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "NULL pointer");
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  accept_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ids, tok, out, S, smax);
+  return check_launch("accept launch");
+}

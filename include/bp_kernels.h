@@ -1,0 +1,114 @@
+/*
+ * bp_kernels.h -- C ABI of the B200 (sm_100a) kernels behind byteprof's decode hot path.
+ *
+ * Every entry point takes caller-owned device pointers, plain integer sizes and strides, and a
+ * cudaStream_t passed as `void*` (NULL = the legacy default stream). Nothing here allocates device
+ * memory, synchronises the host or aborts: each call returns a status (BP_OK = 0), and
+ * bp_last_error() returns a message for the last failing call on the calling thread. All launches
+ * go to the given stream, so the calls can be captured in a CUDA graph.
+ *
+ * Reference interfaces replaced (paths inside the byteprof project):
+ *   bp_skinny_mm        byteprof/optim/skinny.py:136-166   skinny_mm (bf16 and int8 weight kinds)
+ *                       byteprof/optim/skinny.py:111-129   _launch (+ _split_reduce, skinny.py:83-90)
+ *   bp_gemv_int8        byteprof/quant/triton_int8.py:40-47 gemv_int8
+ *   bp_mlstm_scan       byteprof/optim/mlstm_multistep.py:33-85  multistep_fw_kernel
+ *                       byteprof/optim/mlstm_multistep.py:89-133 lazy_commit_kernel
+ *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
+ *   bp_mlstm_accept     byteprof/optim/mlstm_multistep.py:136-146 accept_kernel
+ */
+#ifndef BP_KERNELS_H
+#define BP_KERNELS_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------------------------- */
+enum {
+  BP_OK = 0,
+  BP_ERR_INVALID_ARGUMENT = 1, /* a size, stride, pointer or dtype is not accepted */
+  BP_ERR_UNSUPPORTED = 2,      /* a valid request this build has no kernel for (e.g. head dim) */
+  BP_ERR_MISALIGNED = 3,       /* a pointer or stride breaks the alignment the kernel needs */
+  BP_ERR_CUDA = 4,             /* the CUDA runtime reported an error (launch or device) */
+  BP_ERR_NO_DEVICE = 5         /* no sm_100 device is current */
+};
+
+/* ---- element types ------------------------------------------------------------------------ */
+enum {
+  BP_DTYPE_BF16 = 0,
+  BP_DTYPE_F32 = 1,
+  BP_DTYPE_INT8 = 2
+};
+
+/* Version of this ABI (major * 100 + minor). */
+int bp_abi_version(void);
+
+/* Human-readable name of a status code (static storage). */
+const char* bp_status_string(int status);
+
+/* Message describing the last failing call on this thread ("" when none). */
+const char* bp_last_error(void);
+
+/*
+ * Skinny linear  y[M, N] = x[M, K] . W[N, K]^T  (fp32 accumulation).
+ *   x      bf16, row stride ldx elements (ldx >= K); rows beyond M are never read
+ *   w      w_dtype = BP_DTYPE_BF16: bf16 [N, K] contiguous
+ *          w_dtype = BP_DTYPE_INT8: int8 [N, K] contiguous, w_scale = bf16 [N]; y = scale[n] * sum_k x*q
+ *   y      y_dtype BP_DTYPE_BF16 or BP_DTYPE_F32 (the fp32 store is the un-rounded accumulator), row
+ *          stride ldy elements; exactly the M x N block is written
+ * M = 0 or N = 0 writes nothing; K = 0 writes zeros. Any M is accepted; rows are processed in
+ * chunks of 16 per launch (the weights are re-read per chunk, as the reference re-reads per 64 rows).
+ * Replaces skinny_mm / _launch / _skinny_kernel MODE 0 and 1 (byteprof/optim/skinny.py:35-166).
+ */
+int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale,
+                 void* y, long long ldy, int y_dtype, int M, int N, int K, void* stream);
+
+/*
+ * int8 weight-only GEMV for one activation row: y[1, N] = scale[n] * sum_k x[k] * q[n, k].
+ * Same kernel family as bp_skinny_mm with M = 1 (byteprof/quant/triton_int8.py:15-47).
+ */
+int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,
+                 void* stream);
+
+/*
+ * Fused mLSTM recurrence over T positions (exponential gating with the max stabiliser m), one head
+ * per group of CTAs, the (C, n, m) state kept on chip across all positions.
+ *   c_in [NH, DQ, DV], n_in [NH, DQ], m_in [NH]  fp32, contiguous: the state before position 0
+ *   q, k [T, NH, DQ] (row stride str_t_qk), v [T, NH, DV] (str_t_v), elements of `dtype`
+ *   i_gate, f_gate [T, NH] pre-activations (str_t_if), elements of `gate_dtype`
+ *   h      [T, NH, DV] (str_t_h), `dtype`; NULL = do not compute the outputs
+ *   c_out, n_out, m_out  the state after the last applied position; NULL = not written.
+ *          c_out may equal c_in (each CTA reads its tile before writing it); n_out / m_out must not
+ *          alias n_in / m_in.
+ *   n_save, m_save  receive a copy of n_in / m_in (the lazy-commit start copy); NULL = skipped
+ *   steps_dev  NULL: apply all T positions. Otherwise a device int64 L: apply positions 0..L
+ *          (clamped to T), read on the device so the count can change between graph replays.
+ * qk_scale multiplies q (the reference passes DQ^-0.5); eps is added to the denominator.
+ * dtype BP_DTYPE_BF16 follows the reference's bf16 casts of the gates, products and C for the
+ * output dot product; BP_DTYPE_F32 keeps everything in fp32.
+ * Supported: DQ in {64, 128, 256, 512}, DV a multiple of 16; vector strides multiples of 8 elements
+ * and 16-byte aligned bases.
+ * Replaces multistep_fw_kernel (h only, save n/m) and lazy_commit_kernel (state only, steps_dev),
+ * byteprof/optim/mlstm_multistep.py:33-133, and the library step of draft_core.py:114-141 (T = 1).
+ */
+int bp_mlstm_scan(const float* c_in, const float* n_in, const float* m_in, const void* q, const void* k,
+                  const void* v, const void* i_gate, const void* f_gate, void* h, float* c_out, float* n_out,
+                  float* m_out, float* n_save, float* m_save, const int64_t* steps_dev, int T, int NH, int DQ,
+                  int DV, long long str_t_qk, long long str_t_v, long long str_t_if, long long str_t_h,
+                  int dtype, int gate_dtype, float qk_scale, float eps, void* stream);
+
+/*
+ * Draft acceptance on the device: out[0:S] <- tok[0:S]; out[smax] <- L, the number of leading
+ * drafts ids[1 + j] equal to tok[j] (j < S - 1). ids, tok, out int64.
+ * Replaces accept_kernel (byteprof/optim/mlstm_multistep.py:136-146).
+ */
+int bp_mlstm_accept(const int64_t* ids, const int64_t* tok, int64_t* out, int S, int smax, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BP_KERNELS_H */

@@ -1,0 +1,42 @@
+"""pytest setup: the `gpu` marker, the repo root on sys.path, and the in-tree kernel library.
+
+Tests marked `gpu` need an sm_100 device; they fail (not skip) when selected without one, so a run
+on a GPU box can never pass by skipping. Everything else runs on the CPU.
+"""
+
+from __future__ import annotations
+
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a CUDA sm_100 device (B200)")
+
+
+@pytest.fixture(scope="session", autouse=True)
+def _kernel_library():
+    """Builds libbp_kernels.so if a source is newer than it (no-op when the prebuilt library is current)."""
+    from byteprof_b200 import build
+
+    try:
+        build.build()
+    except RuntimeError:
+        if not build.LIB_PATH.exists():
+            raise
+    yield
+
+
+@pytest.fixture(autouse=True)
+def _gpu_required(request):
+    if request.node.get_closest_marker("gpu") is not None:
+        import torch
+
+        assert torch.cuda.is_available(), "this test needs a CUDA device"
+    yield

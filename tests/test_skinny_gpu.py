@@ -1,0 +1,163 @@
+"""GPU parity of the skinny linear (bp_skinny_mm through byteprof_b200.optim.skinny) against the CPU
+oracle, following the reference's tests/test_skinny.py (componentwise error < 4e-3 for every M = 1..33
+on the real and odd shapes, empty and many rows, row independence, validation, the sentinel buffer)
+plus the BASELINE bars: bf16 max-abs error <= 1e-2 x output RMS on every OLMo-2-1B shape at
+M in {1, 2, 4, 8, 16}, int8 within 1e-3 relative on the fp32 accumulator."""
+
+import numpy as np
+import pytest
+import torch
+
+from byteprof_b200.optim import skinny as S
+from helpers import deq_np, make_weights, to_np
+from oracle import skinny_ref
+
+pytestmark = pytest.mark.gpu
+
+TOL = skinny_ref.TOL_COMPONENTWISE  # 4e-3, the reference's componentwise tolerance
+REAL = [(2048, 2048), (8192, 2048), (2048, 8192), (1024, 2048), (2816, 2048), (2048, 2816)]
+ODD = [(37, 256), (1, 128), (50, 384), (129, 640)]
+OLMO = [(2048, 2048), (8192, 2048), (2048, 8192), (100352, 2048)]
+
+
+def x_rows(m, k, seed):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+@pytest.mark.parametrize("n,k", REAL + ODD)
+def test_matches_oracle_for_every_m(kind, n, k):
+    _, args = make_weights(kind, n, k)
+    wd = deq_np(kind, args)
+    worst = 0.0
+    for m in range(1, 34):
+        x = x_rows(m, k, seed=m)
+        y = S.skinny_mm(x, *args)
+        assert y.shape == (m, n) and y.dtype == torch.bfloat16
+        worst = max(worst, skinny_ref.nerr(to_np(y), to_np(x), wd))
+    assert worst < TOL, worst
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+@pytest.mark.parametrize("n,k", [(37, 1000), (3, 129), (16, 2047), (7, 5000), (1025, 2049)])
+def test_unaligned_k_takes_the_elementwise_path(kind, n, k):
+    _, args = make_weights(kind, n, k, seed=5)
+    wd = deq_np(kind, args)
+    for m in (1, 3, 16, 17):
+        x = x_rows(m, k, seed=m)
+        assert skinny_ref.nerr(to_np(S.skinny_mm(x, *args)), to_np(x), wd) < TOL
+
+
+@pytest.mark.parametrize("n,k", OLMO)
+@pytest.mark.parametrize("m", [1, 2, 4, 8, 16])
+def test_bf16_baseline_bar_max_abs_within_1e2_of_rms(n, k, m):
+    _, args = make_weights("bf16", n, k, seed=n + k)
+    x = x_rows(m, k, seed=100 + m)
+    y = S.skinny_mm(x, *args)
+    ref = skinny_ref.linear_ref(to_np(x), deq_np("bf16", args))
+    assert skinny_ref.rms_bound_ratio(to_np(y), ref) <= 1e-2
+
+
+@pytest.mark.parametrize("n,k", OLMO)
+@pytest.mark.parametrize("m", [1, 4, 16])
+def test_int8_baseline_bar_fp32_within_1e3_relative(n, k, m):
+    _, args = make_weights("int8", n, k, seed=n + k)
+    x = x_rows(m, k, seed=200 + m)
+    ref = skinny_ref.linear_ref(to_np(x), deq_np("int8", args), exact=n < 50000)
+    y32 = S.skinny_mm(x, *args, out=torch.empty(m, n, device="cuda", dtype=torch.float32))
+    assert skinny_ref.rel_normwise(to_np(y32), ref) <= 1e-3
+    # the bf16 output is that accumulator rounded once: within one bf16 step of the reference
+    yb = to_np(S.skinny_mm(x, *args))
+    assert (np.abs(yb - ref) <= np.abs(ref) * 2.0**-7 + 1e-4 * np.abs(ref).max()).all()
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+def test_empty_input_and_many_rows(kind):
+    _, args = make_weights(kind, 64, 256)
+    wd = deq_np(kind, args)
+    assert S.skinny_mm(torch.empty(0, 256, device="cuda", dtype=torch.bfloat16), *args).shape == (0, 64)
+    x = x_rows(150, 256, seed=1)  # more than MAX_M rows: processed in chunks
+    assert skinny_ref.nerr(to_np(S.skinny_mm(x, *args)), to_np(x), wd) < TOL
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+def test_cfg_is_accepted_and_ignored(kind):
+    _, args = make_weights(kind, 192, 1024)
+    wd = deq_np(kind, args)
+    for m in (1, 5, 17, 33):
+        x = x_rows(m, 1024, seed=m)
+        assert skinny_ref.nerr(to_np(S.skinny_mm(x, *args, cfg=(32, 128, 4, 3, 4))), to_np(x), wd) < TOL
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+def test_rows_do_not_depend_on_the_other_rows(kind):
+    """Output row i is bit-identical whatever the number of rows in the same 16-row launch."""
+    _, args = make_weights(kind, 2048, 2048)
+    x = x_rows(16, 2048, seed=9)
+    full = S.skinny_mm(x, *args)
+    for m in (1, 3, 9):
+        assert torch.equal(S.skinny_mm(x[:m].contiguous(), *args), full[:m])
+
+
+def test_results_are_deterministic():
+    _, args = make_weights("bf16", 2048, 8192)
+    x = x_rows(4, 8192, seed=2)
+    a = S.skinny_mm(x, *args)
+    for _ in range(3):
+        assert torch.equal(S.skinny_mm(x, *args), a)
+
+
+def test_input_validation():
+    w = torch.zeros(8, 128, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        S.skinny_mm(torch.zeros(2, 64, device="cuda", dtype=torch.bfloat16), w)
+    with pytest.raises(ValueError):
+        S.skinny_mm(torch.zeros(2, 128, device="cuda", dtype=torch.bfloat16)[:, ::2], w)
+    with pytest.raises(ValueError):
+        S.skinny_mm(torch.zeros(2, 128, device="cuda", dtype=torch.bfloat16),
+                    torch.zeros(8, 128, device="cuda", dtype=torch.int8))
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+@pytest.mark.parametrize("m", [1, 3, 17])
+def test_kernel_writes_only_the_output_block(kind, m):
+    n, k = 70, 384
+    _, args = make_weights(kind, n, k)
+    x = x_rows(m, k, seed=4)
+    flat = torch.full((m * n + 4096,), 777.0, device="cuda", dtype=torch.bfloat16)
+    out = flat[:m * n].view(m, n)
+    S.skinny_mm(x, *args, out=out)
+    assert torch.equal(flat[m * n:], torch.full_like(flat[m * n:], 777.0))
+    assert not (out == 777.0).any()
+    assert skinny_ref.nerr(to_np(out), to_np(x), deq_np(kind, args)) < TOL
+
+
+def test_strided_output_rows_leave_the_gaps_untouched():
+    n, k, m = 96, 512, 5
+    _, args = make_weights("bf16", n, k)
+    x = x_rows(m, k, seed=8)
+    big = torch.full((m, n + 40), -5.0, device="cuda", dtype=torch.bfloat16)
+    S.skinny_mm(x, *args, out=big[:, :n])
+    assert (big[:, n:] == -5.0).all()
+    assert skinny_ref.nerr(to_np(big[:, :n]), to_np(x), deq_np("bf16", args)) < TOL
+
+
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+def test_cuda_graph_replay_equals_eager(kind):
+    _, args = make_weights(kind, 2048, 2048)
+    x = x_rows(4, 2048, seed=1)
+    S.skinny_mm(x, *args)
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        S.skinny_mm(x, *args)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y = S.skinny_mm(x, *args)
+    x.copy_(x_rows(4, 2048, seed=2))
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, S.skinny_mm(x, *args))
