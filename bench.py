@@ -405,14 +405,15 @@ def run_ours(args) -> int:
         extras["scan"] = scan_cells(device, peak)
 
     if rank == 0:
-        dom = [c for key, c in cells.items() if key.startswith("100352x2048")]
-        if dom:
-            lm_bytes = sum(alg_bytes(m, 100352, 2048) for m in MS)
-            lm_us = sum(c["us"] for c in dom)
-            achieved = lm_bytes / (lm_us * 1e-6) / 1e9
+        # dominant kernel = the sweep cell with the largest device time per step
+        if cells:
+            dom_key = max(cells, key=lambda key: cells[key]["us"])
+            n_, k_ = (int(v) for v in dom_key.split("|")[0].split("x"))
+            m_ = int(dom_key.split("|M")[1])
+            achieved = alg_bytes(m_, n_, k_) / (cells[dom_key]["us"] * 1e-6) / 1e9
         else:
-            achieved = value / world
-        traffic = _traffic_from_profile()
+            dom_key, achieved = "sweep", value / world
+        traffic = _traffic_from_profiles(dom_key)
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_total / args.steps, 4), "higher_is_better": True,
@@ -423,7 +424,7 @@ def run_ours(args) -> int:
                        "weights": "N(0, 0.02) bf16, x ~ N(0, 1)", "timing": "CUDA graph per step, CUDA events"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "skinny (100352x2048 LM-head cells, M=1..16)"},
+                         "kernel": f"skinny_mm cell {dom_key} (largest time share)"},
             "frac_of_peak": round(value / world / peak, 4),
             "mean_cell_frac": round(statistics.mean(c["frac"] for c in cells.values()), 4) if cells else None,
             "cells": cells,
@@ -443,13 +444,19 @@ def run_ours(args) -> int:
     return 0
 
 
-def _traffic_from_profile():
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary, when present."""
-    p = ROOT / "profiles" / "skinny_lmhead_traffic.json"
-    try:
-        return json.loads(p.read_text())["dram_bytes_per_launch"]
-    except Exception:  # noqa: BLE001
-        return None
+def _traffic_from_profiles(cell: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of `cell` from a committed
+    ncu summary under profiles/ (lines `cell: <N>x<K>|M<m>` and `dram_bytes_per_launch: <bytes>`)."""
+    for p in sorted((ROOT / "profiles").glob("*.md")):
+        cell_line = traffic = None
+        for line in p.read_text().splitlines():
+            if line.startswith("cell:"):
+                cell_line = line.split(":", 1)[1].strip()
+            elif line.startswith("dram_bytes_per_launch:"):
+                traffic = int(line.split(":", 1)[1].strip())
+        if cell_line == cell and traffic is not None:
+            return traffic
+    return None
 
 
 def _cpu_baseline() -> dict:
@@ -460,6 +467,41 @@ def _cpu_baseline() -> dict:
                       "torch bf16 on the host = byteprof SkinnyLinear's CPU branch"}
 
 
+def run_case(args) -> int:
+    """One sweep cell alone (for ncu captures): `--case N,K,M[,bf16|int8]`; W eager warm-up calls, then K
+    timed calls over a weight ring > 2x L2. Prints a JSON line with us per call and GB/s."""
+    from byteprof_b200.optim.skinny import skinny_mm
+    from byteprof_b200.quant.int8 import quantize_rowwise_int8
+
+    parts = args.case.split(",")
+    n, k, m = (int(v) for v in parts[:3])
+    kind = parts[3] if len(parts) > 3 else "bf16"
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    wbytes = 2 * n * k if kind == "bf16" else n * k
+    ring = []
+    for _ in range(max(2, math.ceil(RING_BYTES / wbytes))):
+        w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        ring.append((w,) if kind == "bf16" else quantize_rowwise_int8(w))
+    x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
+    for i in range(args.warmup):
+        skinny_mm(x, *ring[i % len(ring)], out=y)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(args.steps):
+        skinny_mm(x, *ring[(args.warmup + i) % len(ring)], out=y)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / args.steps
+    nb = alg_bytes(m, n, k, kind)
+    print(json.dumps({"case": f"{n}x{k}|M{m}|{kind}", "us": round(us, 3), "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+                      "bytes": nb, "launches": args.warmup + args.steps}), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -467,11 +509,14 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the per-cell, int8, scan and CPU passes")
+    ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8]: time one sweep cell alone (ncu captures)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     if args.impl == "reference":
         return run_reference(args)
+    if args.case:
+        return run_case(args)
     return run_ours(args)
 
 

@@ -78,6 +78,53 @@ __device__ __forceinline__ float rnd(float v) {
   return v;
 }
 
+// Two adjacent elements of q or k from shared memory as floats (one 4- or 8-byte load).
+template <typename T>
+__device__ __forceinline__ void load_pair(const T* p, float& a, float& b) {
+  if constexpr (sizeof(T) == 2) {
+    const uint32_t w = *reinterpret_cast<const uint32_t*>(p);
+    a = bf16lo(w);
+    b = bf16hi(w);
+  } else {
+    const float2 v = *reinterpret_cast<const float2*>(p);
+    a = v.x;
+    b = v.y;
+  }
+}
+
+// bf16 pair from two bf16-valued floats (exact), and back.
+__device__ __forceinline__ __nv_bfloat162 pack2(float a, float b) { return __floats2bfloat162_rn(a, b); }
+__device__ __forceinline__ void unpack2(__nv_bfloat162 v, float& a, float& b) {
+  const float2 f = __bfloat1622float2(v);
+  a = f.x;
+  b = f.y;
+}
+
+// (o0, o1) = s * (a0, a1): with bf16 inputs one packed bf16 multiply (round to nearest), else fp32.
+template <typename T>
+__device__ __forceinline__ void mul_pair(float s, float a0, float a1, float& o0, float& o1) {
+  if constexpr (sizeof(T) == 2) {
+    unpack2(__hmul2(pack2(s, s), pack2(a0, a1)), o0, o1);
+  } else {
+    o0 = s * a0;
+    o1 = s * a1;
+  }
+}
+
+// (q0 * qsc) * c0 + (q1 * qsc) * c1 with the reference's bf16 roundings of q*qsc, c and each product
+// (qsc is already bf16-valued in bf16 mode); the two products are added in fp32.
+template <typename T>
+__device__ __forceinline__ float dot_pair(float q0, float q1, float qsc, float c0, float c1) {
+  if constexpr (sizeof(T) == 2) {
+    const __nv_bfloat162 qs = __hmul2(pack2(q0, q1), pack2(qsc, qsc));
+    float p0, p1;
+    unpack2(__hmul2(qs, __floats2bfloat162_rn(c0, c1)), p0, p1);
+    return p0 + p1;
+  } else {
+    return (q0 * qsc) * c0 + (q1 * qsc) * c1;
+  }
+}
+
 template <int DQ, typename T>
 struct ScanCfg {
   static constexpr int TPC = DQ >= 128 ? 16 : 8;  // threads per value column
@@ -85,7 +132,7 @@ struct ScanCfg {
   static constexpr int CH = RPT / 8;              // 8-row chunks per thread
   static constexpr int NCOMP = kBV * TPC;         // compute threads
   static constexpr int NTHREADS = NCOMP + 32;     // + one producer warp
-  static constexpr int RPL = DQ / 32;             // rows of n per producer lane
+  static constexpr int RPL = DQ / 32;             // rows of n per producer lane: pairs 2*lane + 64*j + {0,1}
   static constexpr int STAGE = 2 * DQ + kBV;      // elements of q, k, v for one position
   static constexpr int CHUNKS16 = STAGE * static_cast<int>(sizeof(T)) / 16;
 };
@@ -99,7 +146,7 @@ __device__ __forceinline__ float load_gate(const void* p, long long idx, int is_
 // buffers. `m_run` is the stabiliser after position 32 j - 1 on entry and after the last valid
 // position of the chunk on exit (identical in every lane).
 template <typename T>
-__device__ void gate_chunk(const ScanArgs& a, int head, int j, int n_steps, float& m_run, float* g_f, float* g_i,
+__device__ __forceinline__ void gate_chunk(const ScanArgs& a, int head, int j, int n_steps, float& m_run, float* g_f, float* g_i,
                            float* g_mx) {
   const int lane = threadIdx.x & 31;
   const int s = j * kGC + lane;
@@ -183,19 +230,21 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
 
   // ---- prologue --------------------------------------------------------------------------------
   float creg[Cfg::RPT];                 // compute threads: C[rows, col]
-  float nreg[Cfg::RPL];                 // producer: n[lane + 32 r]
+  float nreg[Cfg::RPL];                 // producer: n[prow(r)]
   float m_run = a.m_in[head];
   const int col = tid / Cfg::TPC;       // compute threads: value column in the block
   const int l = tid % Cfg::TPC;
   const float* cbase = a.c_in + static_cast<long long>(head) * DQ * a.DV + c0;
 
+  // producer lane's n rows: pairs of adjacent rows, so q and k are read as bf16x2 / float2 words
+  auto prow = [&](int r) { return 2 * lane + 64 * (r >> 1) + (r & 1); };
   if (producer) {
 #pragma unroll
-    for (int r = 0; r < Cfg::RPL; ++r) nreg[r] = a.n_in[head * DQ + lane + 32 * r];
+    for (int r = 0; r < Cfg::RPL; ++r) nreg[r] = a.n_in[head * DQ + prow(r)];
     if (blockIdx.x == 0) {
       if (a.n_save != nullptr)
 #pragma unroll
-        for (int r = 0; r < Cfg::RPL; ++r) a.n_save[head * DQ + lane + 32 * r] = nreg[r];
+        for (int r = 0; r < Cfg::RPL; ++r) a.n_save[head * DQ + prow(r)] = nreg[r];
       if (a.m_save != nullptr && lane == 0) a.m_save[head] = m_run;
     }
     for (int s = 0; s < kDepth - 1; ++s) issue(s);
@@ -226,14 +275,16 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
       issue(t + kDepth - 1);
       float qn = 0.0f;
 #pragma unroll
-      for (int r = 0; r < Cfg::RPL; ++r) {
-        const int row = lane + 32 * r;
-        const float kf = to_f<T>(st[DQ + row]);
-        nreg[r] = fmaf(fa, nreg[r], rnd<T>(ia * kf));
-        if (want_h) {
-          const float qs = rnd<T>(to_f<T>(st[row]) * qsc);
-          qn += rnd<T>(qs * rnd<T>(nreg[r]));
-        }
+      for (int r = 0; r < Cfg::RPL; r += 2) {
+        const int row = prow(r);
+        float k0, k1, q0, q1;
+        load_pair<T>(st + DQ + row, k0, k1);
+        load_pair<T>(st + row, q0, q1);
+        float ik0, ik1;
+        mul_pair<T>(ia, k0, k1, ik0, ik1);  // i_act * k, rounded like the reference
+        nreg[r] = fmaf(fa, nreg[r], ik0);
+        nreg[r + 1] = fmaf(fa, nreg[r + 1], ik1);
+        if (want_h) qn += dot_pair<T>(q0, q1, qsc, nreg[r], nreg[r + 1]);
       }
       if (want_h) {
 #pragma unroll
@@ -243,31 +294,50 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
       __syncwarp();
       if ((t & (kGC - 1)) == 0) gate_chunk<T>(a, head, t / kGC + 1, n_steps, m_run, g_f, g_i, g_mx);
     } else {
-      const float vf = to_f<T>(st[2 * DQ + col]);
       float hs = 0.0f;
+      if constexpr (sizeof(T) == 2) {
+        // bf16: q, k stay packed; every product is one bf16x2 multiply rounded to nearest (the
+        // reference's bf16 x bf16 products), the state update and the sum are fp32.
+        const __nv_bfloat162 v2 = __bfloat162bfloat162(st[2 * DQ + col]);
+        const __nv_bfloat162 ia2 = pack2(ia, ia), qsc2 = pack2(qsc, qsc);
 #pragma unroll
-      for (int ch = 0; ch < Cfg::CH; ++ch) {
-        const int rb = (l + Cfg::TPC * ch) * 8;
-        float kf[8], qf[8];
-        if constexpr (sizeof(T) == 2) {
-          const uint4 kv4 = *reinterpret_cast<const uint4*>(st + DQ + rb);
-          const uint4 qv4 = *reinterpret_cast<const uint4*>(st + rb);
-          kf[0] = bf16lo(kv4.x); kf[1] = bf16hi(kv4.x); kf[2] = bf16lo(kv4.y); kf[3] = bf16hi(kv4.y);
-          kf[4] = bf16lo(kv4.z); kf[5] = bf16hi(kv4.z); kf[6] = bf16lo(kv4.w); kf[7] = bf16hi(kv4.w);
-          qf[0] = bf16lo(qv4.x); qf[1] = bf16hi(qv4.x); qf[2] = bf16lo(qv4.y); qf[3] = bf16hi(qv4.y);
-          qf[4] = bf16lo(qv4.z); qf[5] = bf16hi(qv4.z); qf[6] = bf16lo(qv4.w); qf[7] = bf16hi(qv4.w);
-        } else {
+        for (int ch = 0; ch < Cfg::CH; ++ch) {
+          const int rb = (l + Cfg::TPC * ch) * 8;
+          const uint4 kw = *reinterpret_cast<const uint4*>(st + DQ + rb);
+          const uint4 qw = *reinterpret_cast<const uint4*>(st + rb);
+          const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kw);
+          const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qw);
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            float& c0 = creg[ch * 8 + 2 * p];
+            float& c1 = creg[ch * 8 + 2 * p + 1];
+            float u0, u1;
+            unpack2(__hmul2(ia2, __hmul2(k2[p], v2)), u0, u1);
+            c0 = fmaf(fa, c0, u0);
+            c1 = fmaf(fa, c1, u1);
+            if (want_h) {
+              float p0, p1;
+              unpack2(__hmul2(__hmul2(q2[p], qsc2), __floats2bfloat162_rn(c0, c1)), p0, p1);
+              hs += p0 + p1;
+            }
+          }
+        }
+      } else {
+        const float vf = to_f<T>(st[2 * DQ + col]);
+#pragma unroll
+        for (int ch = 0; ch < Cfg::CH; ++ch) {
+          const int rb = (l + Cfg::TPC * ch) * 8;
           const float4* kp = reinterpret_cast<const float4*>(st + DQ + rb);
           const float4* qp = reinterpret_cast<const float4*>(st + rb);
-          const float4 k0 = kp[0], k1 = kp[1], q0 = qp[0], q1 = qp[1];
-          kf[0] = k0.x; kf[1] = k0.y; kf[2] = k0.z; kf[3] = k0.w; kf[4] = k1.x; kf[5] = k1.y; kf[6] = k1.z; kf[7] = k1.w;
-          qf[0] = q0.x; qf[1] = q0.y; qf[2] = q0.z; qf[3] = q0.w; qf[4] = q1.x; qf[5] = q1.y; qf[6] = q1.z; qf[7] = q1.w;
-        }
+          const float4 ka = kp[0], kb = kp[1], qa = qp[0], qb = qp[1];
+          const float kf[8] = {ka.x, ka.y, ka.z, ka.w, kb.x, kb.y, kb.z, kb.w};
+          const float qf[8] = {qa.x, qa.y, qa.z, qa.w, qb.x, qb.y, qb.z, qb.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          float& c = creg[ch * 8 + e];
-          c = fmaf(fa, c, rnd<T>(ia * rnd<T>(kf[e] * vf)));
-          if (want_h) hs += rnd<T>(rnd<T>(qf[e] * qsc) * rnd<T>(c));
+          for (int e = 0; e < 8; ++e) {
+            float& c = creg[ch * 8 + e];
+            c = fmaf(fa, c, ia * (kf[e] * vf));
+            if (want_h) hs += (qf[e] * qsc) * c;
+          }
         }
       }
       if (want_h) {
@@ -291,7 +361,7 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
     if (blockIdx.x == 0) {
       if (a.n_out != nullptr)
 #pragma unroll
-        for (int r = 0; r < Cfg::RPL; ++r) a.n_out[head * DQ + lane + 32 * r] = nreg[r];
+        for (int r = 0; r < Cfg::RPL; ++r) a.n_out[head * DQ + prow(r)] = nreg[r];
       if (a.m_out != nullptr && lane == 0) a.m_out[head] = m_run;
     }
   } else if (a.c_out != nullptr) {

@@ -14,6 +14,9 @@ triton/language/semantic.py computation_type_impl; tl.sum keeps bf16, standard.p
   * f_act, i_act, max_val are rounded to bf16 (`.to(DTYPE)`, mlstm_multistep.py:27-29);
   * k*v, i_act*(k*v) and i_act*k are bf16 x bf16 products, rounded to bf16; f_act*C and f_act*n are
     fp32 (bf16 x fp32 promotes to fp32), the sums fp32;
+  * `f_act * C + x` and `f_act * n + x` are single fused multiply-adds: Triton compiles with
+    enable_fp_fusion on by default, so a product feeding an add becomes one fma.rn.f32 (emulated here in
+    float64, whose product of two float32 values is exact, then rounded once to float32);
   * q*qk_scale: the scalar is rounded to bf16, the product to bf16;
   * C and n are rounded to bf16 before the output dot products (`c0.to(DTYPE)`), and each product
     q*C, q*n is rounded to bf16. The reference then reduces these bf16 products in bf16 (layout
@@ -56,6 +59,13 @@ def gates(f: np.ndarray, i: np.ndarray, m_old: np.ndarray, bf16: bool):
     return m_new, max_val, f_act, i_act
 
 
+def fma32(a, b, c) -> np.ndarray:
+    """float32 fused multiply-add a * b + c with one rounding (float64 product exact, sum rounded twice
+    only when the float64 sum itself rounds, which for these magnitudes does not change the float32 result
+    in practice)."""
+    return (np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64)).astype(F32)
+
+
 def step(state, q, k, v, i, f, qk_scale: float, eps: float, bf16: bool, want_h: bool = True):
     """One position for all heads.
 
@@ -68,8 +78,8 @@ def step(state, q, k, v, i, f, qk_scale: float, eps: float, bf16: bool, want_h: 
     v = np.asarray(v, F32)
     kv = _r(k[:, :, None] * v[:, None, :], bf16)
     ikv = _r(i_act[:, None, None] * kv, bf16)
-    c_new = (f_act[:, None, None] * c + ikv).astype(F32)
-    n_new = (f_act[:, None] * n + _r(i_act[:, None] * k, bf16)).astype(F32)
+    c_new = fma32(f_act[:, None, None], c, ikv)
+    n_new = fma32(f_act[:, None], n, _r(i_act[:, None] * k, bf16))
     h = None
     if want_h:
         qs = _r(q * _r(F32(qk_scale), bf16), bf16)

@@ -52,11 +52,18 @@ def test_unaligned_k_takes_the_elementwise_path(kind, n, k):
 @pytest.mark.parametrize("n,k", OLMO)
 @pytest.mark.parametrize("m", [1, 2, 4, 8, 16])
 def test_bf16_baseline_bar_max_abs_within_1e2_of_rms(n, k, m):
+    """The bar (max-abs error <= 1e-2 x RMS of the fp32 F.linear) on the fp32 accumulator, and the bf16
+    output bit-equal to that accumulator rounded to nearest even. (On bf16 outputs the bar is below the
+    output resolution: with RMS ~0.9 an output >= 4 has a bf16 step of 2^-5, so correct rounding alone
+    can miss it by up to 0.017 x RMS, for any bf16-output implementation.)"""
     _, args = make_weights("bf16", n, k, seed=n + k)
     x = x_rows(m, k, seed=100 + m)
-    y = S.skinny_mm(x, *args)
-    ref = skinny_ref.linear_ref(to_np(x), deq_np("bf16", args))
-    assert skinny_ref.rms_bound_ratio(to_np(y), ref) <= 1e-2
+    y32 = S.skinny_mm(x, *args, out=torch.empty(m, n, device="cuda", dtype=torch.float32))
+    yb = S.skinny_mm(x, *args)
+    ref = skinny_ref.linear_ref(to_np(x), deq_np("bf16", args), exact=n < 50000)
+    assert skinny_ref.rms_bound_ratio(to_np(y32), ref) <= 1e-2
+    assert skinny_ref.rel_normwise(to_np(y32), ref) <= 1e-5
+    assert torch.equal(yb, y32.to(torch.bfloat16))
 
 
 @pytest.mark.parametrize("n,k", OLMO)
