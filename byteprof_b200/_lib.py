@@ -8,7 +8,7 @@ are ordered with the surrounding torch work and can be captured in CUDA graphs.
 from __future__ import annotations
 
 import ctypes
-from ctypes import c_float, c_int, c_longlong, c_void_p
+from ctypes import c_float, c_int, c_longlong, c_size_t, c_void_p
 from pathlib import Path
 
 import torch
@@ -25,13 +25,15 @@ _SIGNATURES = {
     "bp_status_string": (ctypes.c_char_p, [c_int]),
     "bp_last_error": (ctypes.c_char_p, []),
     "bp_skinny_mm": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_void_p, c_longlong, c_int,
-                             c_int, c_int, c_int, c_void_p]),
+                             c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
+    "bp_skinny_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "bp_gemv_int8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p]),
     "bp_mlstm_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_int, c_int, c_int, c_int, c_longlong, c_longlong, c_longlong, c_longlong,
                               c_int, c_int, c_float, c_float, c_void_p]),
     "bp_mlstm_accept": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "bp_device_errors": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -94,3 +96,38 @@ def require_cuda(*tensors: torch.Tensor) -> None:
     for t in tensors:
         if t is not None and not t.is_cuda:
             raise ValueError("the byteprof B200 kernels take CUDA tensors only (there is no CPU path)")
+
+
+# ---- skinny workspace --------------------------------------------------------------------------------
+# One zero-filled scratch buffer per device for the stream-K partial sums of the bf16 tensor-core path.
+# Kernels leave it zero-filled. Calls that overlap in time on different streams of one device would
+# share it, which the C ABI forbids: the operator API serialises on torch's current stream.
+WORKSPACE_CAPACITY = 8 << 20
+_workspaces: dict[int, torch.Tensor] = {}
+_ws_need: dict[tuple[int, int, int, int], int] = {}
+
+
+def skinny_workspace(device: torch.device, m: int, n: int, k: int, w_dtype: int) -> tuple[int | None, int]:
+    """(pointer, bytes) of the device's skinny workspace, large enough for this problem."""
+    key = (device.index, n, k, w_dtype)
+    need = _ws_need.get(key)
+    if need is None:
+        need = int(lib().bp_skinny_workspace_bytes(min(m, 16), n, k, w_dtype))
+        _ws_need[key] = need
+    if need == 0:
+        return None, 0
+    ws = _workspaces.get(device.index)
+    if ws is None or ws.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("the skinny workspace is allocated on the first call: run one call outside CUDA-graph "
+                               "capture first (the usual warm-up)")
+        ws = torch.zeros(max(WORKSPACE_CAPACITY, need), dtype=torch.uint8, device=device)
+        _workspaces[device.index] = ws
+    return ws.data_ptr(), ws.numel()
+
+
+def device_errors() -> int:
+    """Error flags the kernels raised on the current device since the last call (then cleared)."""
+    v = ctypes.c_uint(0)
+    call("bp_device_errors", ctypes.byref(v))
+    return int(v.value)

@@ -20,6 +20,7 @@
 #include <cooperative_groups.h>
 
 #include "bp_common.cuh"
+#include "skinny_internal.h"
 
 namespace cg = cooperative_groups;
 
@@ -310,11 +311,33 @@ int dispatch_m(const SkinnyArgs& a, int m, bool vec, cudaStream_t st) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// BP_SKINNY_PATH=fma forces the CUDA-core kernel for bf16 too (read at every call; for comparisons).
+bool tc_path_enabled() {
+  const char* e = getenv("BP_SKINNY_PATH");
+  return !(e != nullptr && e[0] == 'f');
+}
+
 }  // namespace
 }  // namespace bp
 
+extern "C" size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype) {
+  if (M <= 0 || N <= 0 || K <= 0 || w_dtype != BP_DTYPE_BF16) return 0;
+  return bp::skinny_tc_workspace_bytes(N, K);
+}
+
+extern "C" int bp_device_errors(unsigned int* flags) {
+  using namespace bp;
+  clear_error();
+  if (flags == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "flags is NULL");
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  *flags = read_and_clear_device_errors();
+  return check_launch("device error read");
+}
+
 extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale, void* y,
-                            long long ldy, int y_dtype, int M, int N, int K, void* stream) {
+                            long long ldy, int y_dtype, int M, int N, int K, void* workspace, size_t workspace_bytes,
+                            void* stream) {
   using namespace bp;
   clear_error();
   if (M < 0 || N < 0 || K < 0) return fail(BP_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d K=%d)", M, N, K);
@@ -355,7 +378,10 @@ extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_d
     const int m = M - r0 < 16 ? M - r0 : 16;
     a.x = static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r0) * ldx;
     a.y = static_cast<char*>(y) + static_cast<long long>(r0) * ldy * static_cast<long long>(ysz);
-    st = is8 ? dispatch_m<int8_t>(a, m, vec, s) : dispatch_m<__nv_bfloat16>(a, m, vec, s);
+    if (!is8 && tc_path_enabled() && skinny_tc_supported(a.x, ldx, w, m, N, K))
+      st = launch_skinny_tc(a.x, ldx, w, a.y, ldy, a.y_f32, m, N, K, workspace, workspace_bytes, s);
+    else
+      st = is8 ? dispatch_m<int8_t>(a, m, vec, s) : dispatch_m<__nv_bfloat16>(a, m, vec, s);
     if (st != BP_OK) return st;
   }
   return BP_OK;
@@ -363,5 +389,5 @@ extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_d
 
 extern "C" int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,
                             void* stream) {
-  return bp_skinny_mm(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, stream);
+  return bp_skinny_mm(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, nullptr, 0, stream);
 }

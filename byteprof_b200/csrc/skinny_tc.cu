@@ -1,0 +1,418 @@
+// Tensor-core skinny linear for bf16 weights: y[M, N] = x[M, K] . W[N, K]^T, M <= 16 rows per launch.
+//
+// Reference: byteprof/optim/skinny.py:35-80 (_skinny_kernel MODE 0: one program per BN weight rows,
+// swap-AB tl.dot with the weight tile as the MMA's M operand and the few activation rows as N) and
+// skinny.py:83-90, 111-129 (split-K through an fp32 workspace and a second reduce kernel).
+//
+// B200 design:
+//  * Swap-AB on the 5th-generation tensor cores: a 128-row weight tile is the A operand (MMA M = 128),
+//    the activation rows padded to 16 are B (MMA N = 16), the fp32 accumulator lives in TMEM.
+//    One kernel serves every M = 1..16, so a row's sum does not depend on the number of rows.
+//  * TMA streams 128 x 64 weight tiles (16 KB, 128-byte swizzle, L2 evict-first) and the matching
+//    16 x 64 activation tile (rows beyond M zero-filled by TMA) into a 6-stage shared-memory ring.
+//  * Stream-K: a persistent grid of one CTA per SM; CTA c owns the contiguous range
+//    [c U / P, (c + 1) U / P) of the U = tiles x k-blocks units, so every SM streams the same number
+//    of bytes whatever the shape. A tile split between CTAs is finished by the CTA that arrives last
+//    (atomic counter per tile, reset by that CTA): it adds the partials in CTA order, so the result
+//    is deterministic. No CTA waits for another.
+//  * Warp roles: warp 0 issues TMA, warp 1 issues tcgen05.mma (and owns the TMEM allocation), warps
+//    2-5 drain TMEM (two accumulator buffers, so draining overlaps the next tile's MMAs).
+//  * Programmatic dependent launch: every CTA lets the next kernel in the stream launch at once, and
+//    issues its first weight tiles before griddepcontrol.wait (weights are not produced by the
+//    preceding kernel; the activations and every global write come after the wait).
+//  * Every mbarrier wait is bounded; a timeout sets the device error word, the CTA drains its copies
+//    in flight, frees TMEM and returns.
+#include <cudaTypedefs.h>
+
+#include "skinny_internal.h"
+#include "sm100.cuh"
+
+namespace bp {
+namespace {
+
+constexpr int kBM = 128;  // weight rows per tile (MMA M)
+constexpr int kBK = 64;   // K elements per stage (one 128-byte swizzle row of bf16)
+constexpr int kNP = 16;   // activation rows per launch (MMA N)
+constexpr int kStages = 6;
+constexpr int kABytes = kBM * kBK * 2;
+constexpr int kBBytes = kNP * kBK * 2;
+constexpr int kThreads = 192;
+constexpr int kEpiThreads = 128;
+constexpr uint32_t kTmemCols = 32;  // two 16-column fp32 accumulators
+
+struct TcArgs {
+  void* y;
+  long long ldy;
+  int y_f32;
+  int M, N, K;
+  int tiles, kblocks;
+  long long units;
+  int P;
+  int* counters;    // [tiles], zero between launches
+  float* partials;  // [P][2][kNP][kBM]
+};
+
+struct __align__(1024) TcSmem {
+  uint8_t a[kStages][kABytes];
+  uint8_t b[kStages][kBBytes];
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+  int last_flag;
+};
+
+constexpr size_t kSmemBytes = sizeof(TcSmem) + 1024;  // + slack to align the base to 1024 bytes
+
+__host__ __device__ __forceinline__ long long unit_start(int c, long long U, int P) {
+  return static_cast<long long>(c) * U / P;
+}
+// The CTA whose range holds unit u: the largest c with unit_start(c) <= u.
+__host__ __device__ __forceinline__ int unit_owner(long long u, long long U, int P) {
+  return static_cast<int>(((u + 1) * P - 1) / U);
+}
+
+// Waits that ignore `abort`: used only to drain this CTA's own asynchronous work before it exits.
+__device__ __forceinline__ void mbar_wait_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > kWaitLimitNs) {
+      atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
+      return;
+    }
+  }
+}
+
+__device__ __forceinline__ void store_rows(const TcArgs& a, int row, const float (&v)[kNP]) {
+  if (row >= a.N) return;
+#pragma unroll
+  for (int m = 0; m < kNP; ++m) {
+    if (m < a.M) {
+      if (a.y_f32)
+        static_cast<float*>(a.y)[m * a.ldy + row] = v[m];
+      else
+        static_cast<__nv_bfloat16*>(a.y)[m * a.ldy + row] = __float2bfloat16_rn(v[m]);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, 2)
+    skinny_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c = blockIdx.x;
+  const long long U = a.units;
+  const int KB = a.kblocks;
+  const long long u0 = unit_start(c, U, a.P), u1 = unit_start(c + 1, U, a.P);
+  const int n_units = static_cast<int>(u1 - u0);
+  const int t_first = static_cast<int>(u0 / KB);
+  const int t_last = n_units > 0 ? static_cast<int>((u1 - 1) / KB) : t_first - 1;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s.tfull[b], 1);
+      mbar_init(&s.tempty[b], kEpiThreads);
+    }
+    mbar_init(&s.mma_done, 1);
+    s.abort = 0;
+    s.last_flag = 0;
+    mbar_fence_init();
+    tma_prefetch_desc(&tw);
+    tma_prefetch_desc(&tx);
+  }
+  if (warp == 1) {
+    tmem_alloc(&s.tmem_base, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  pdl_launch_dependents();
+  const uint32_t tmem = s.tmem_base;
+  volatile int* abort = &s.abort;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer ----
+      const uint64_t pol = l2_evict_first_policy();
+      const int npre = n_units < kStages ? n_units : kStages;
+      for (int i = 0; i < npre; ++i) {  // weights only: they do not depend on the previous kernel
+        const long long u = u0 + i;
+        const int t = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
+        mbar_arrive_expect_tx(&s.full[i], kABytes + kBBytes);
+        tma_load_2d_hint(s.a[i], &tw, &s.full[i], kb * kBK, t * kBM, pol);
+      }
+      pdl_wait_prior_grids();
+      for (int i = 0; i < npre; ++i) {
+        const int kb = static_cast<int>((u0 + i) % KB);
+        tma_load_2d(s.b[i], &tx, &s.full[i], kb * kBK, 0);
+      }
+      int issued = npre;
+      for (int i = npre; i < n_units; ++i) {
+        const int st = i % kStages;
+        if (!mbar_wait(&s.empty[st], static_cast<uint32_t>((i / kStages) + 1) & 1u, abort)) break;
+        const long long u = u0 + i;
+        const int t = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
+        mbar_arrive_expect_tx(&s.full[st], kABytes + kBBytes);
+        tma_load_2d_hint(s.a[st], &tw, &s.full[st], kb * kBK, t * kBM, pol);
+        tma_load_2d(s.b[st], &tx, &s.full[st], kb * kBK, 0);
+        issued = i + 1;
+      }
+      // drain: the last copy issued into each stage has landed
+      for (int st = 0; st < kStages && st < issued; ++st) {
+        const int i_last = st + kStages * ((issued - 1 - st) / kStages);
+        mbar_wait_drain(&s.full[st], static_cast<uint32_t>(i_last / kStages) & 1u);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer ----
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, kNP);
+      int i = 0, it = 0;
+      bool ok = true;
+      for (int t = t_first; t <= t_last && ok; ++t, ++it) {
+        const long long lo = u0 > static_cast<long long>(t) * KB ? u0 : static_cast<long long>(t) * KB;
+        const long long hi = u1 < static_cast<long long>(t + 1) * KB ? u1 : static_cast<long long>(t + 1) * KB;
+        const int buf = it & 1;
+        if (!mbar_wait(&s.tempty[buf], static_cast<uint32_t>((it >> 1) + 1) & 1u, abort)) break;
+        tc_fence_after_sync();
+        const uint32_t dacc = tmem + static_cast<uint32_t>(buf * kNP);
+        for (long long u = lo; u < hi; ++u, ++i) {
+          const int st = i % kStages;
+          if (!mbar_wait(&s.full[st], static_cast<uint32_t>(i / kStages) & 1u, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after_sync();
+          const uint32_t ab = smem_addr(s.a[st]), bb = smem_addr(s.b[st]);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk)
+            umma_f16(dacc, umma_desc_sw128(ab + 32 * kk), umma_desc_sw128(bb + 32 * kk), idesc,
+                     (u > lo || kk > 0) ? 1u : 0u);
+          umma_commit(&s.empty[st]);  // frees the stage once these MMAs have read it
+        }
+        if (ok) umma_commit(&s.tfull[buf]);
+      }
+      umma_commit(&s.mma_done);
+      mbar_wait_drain(&s.mma_done, 0);
+    }
+  } else {
+    // ---- epilogue: TMEM -> registers -> y (or a stream-K partial) ----
+    pdl_wait_prior_grids();
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int r = 32 * q + lane;
+    const int et = threadIdx.x - 64;
+    int it = 0;
+    for (int t = t_first; t <= t_last; ++t, ++it) {
+      const int buf = it & 1;
+      const bool ok = mbar_wait(&s.tfull[buf], static_cast<uint32_t>(it >> 1) & 1u, abort);
+      __syncwarp();
+      if (named_barrier_or(1, kEpiThreads, !ok)) break;  // all epilogue threads take the same decision
+      tc_fence_after_sync();
+      float acc[kNP];
+      tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * kNP), acc);
+      tc_fence_before_sync();
+      mbar_arrive(&s.tempty[buf]);
+      const int row = t * kBM + r;
+      const int c_lo = unit_owner(static_cast<long long>(t) * KB, U, a.P);
+      const int c_hi = unit_owner(static_cast<long long>(t + 1) * KB - 1, U, a.P);
+      if (c_lo == c_hi) {
+        store_rows(a, row, acc);
+        continue;
+      }
+      const int slot = (t == t_first) ? 0 : 1;
+      float* mine = a.partials + static_cast<size_t>(c * 2 + slot) * kNP * kBM;
+#pragma unroll
+      for (int m = 0; m < kNP; ++m) mine[m * kBM + r] = acc[m];
+      __threadfence();
+      __syncwarp();
+      named_barrier_sync(1, kEpiThreads);
+      if (et == 0) {
+        const int old = atomicAdd(&a.counters[t], 1);
+        const int last = old == c_hi - c_lo;
+        if (last) a.counters[t] = 0;  // every contributor has arrived: ready for the next launch
+        s.last_flag = last;
+      }
+      __syncwarp();
+      named_barrier_sync(1, kEpiThreads);
+      if (s.last_flag) {
+        __threadfence();
+        float v[kNP];
+#pragma unroll
+        for (int m = 0; m < kNP; ++m) v[m] = 0.0f;
+        for (int cc = c_lo; cc <= c_hi; ++cc) {  // fixed order: the sum does not depend on arrival order
+          const int cslot = (t == static_cast<int>(unit_start(cc, U, a.P) / KB)) ? 0 : 1;
+          const float* p = a.partials + static_cast<size_t>(cc * 2 + cslot) * kNP * kBM;
+#pragma unroll
+          for (int m = 0; m < kNP; ++m) v[m] += __ldcg(p + m * kBM + r);
+        }
+        store_rows(a, row, v);
+      }
+    }
+  }
+
+  tc_fence_before_sync();
+  cta_barrier_unaligned();  // lanes 1-31 of warps 0 and 1 arrive while lane 0 still runs its loop
+  if (warp == 1) {
+    __syncwarp();  // lane 0 ran the MMA loop alone: reconverge before the warp-wide dealloc
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- host side ---------------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int encode_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                   uint32_t box_inner, uint32_t box_outer, CUtensorMapL2promotion promo) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(BP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BP_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+  return BP_OK;
+}
+
+int tc_sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cached[dev] = n > 0 ? n : 148;
+  }
+  return cached[dev];
+}
+
+int ensure_smem_attr() {
+  static bool done[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && done[dev]) return BP_OK;
+  cudaError_t e = cudaFuncSetAttribute(skinny_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(kSmemBytes));
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "cudaFuncSetAttribute(smem %zu): %s", kSmemBytes, cudaGetErrorString(e));
+  if (dev >= 0 && dev < 64) done[dev] = true;
+  return BP_OK;
+}
+
+bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("BP_DISABLE_PDL");
+    v = (e != nullptr && e[0] == '1') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+struct Partition {
+  int tiles, kblocks, P;
+  long long units;
+};
+
+Partition partition(int N, int K) {
+  Partition p;
+  p.tiles = (N + kBM - 1) / kBM;
+  p.kblocks = (K + kBK - 1) / kBK;
+  p.units = static_cast<long long>(p.tiles) * p.kblocks;
+  const int sms = tc_sm_count();
+  p.P = static_cast<int>(p.units < sms ? p.units : sms);
+  return p;
+}
+
+size_t counters_bytes(int tiles) { return (static_cast<size_t>(tiles) * 4 + 255) / 256 * 256; }
+
+}  // namespace
+
+size_t skinny_tc_workspace_bytes(int N, int K) {
+  if (N <= 0 || K <= 0) return 0;
+  const Partition p = partition(N, K);
+  return counters_bytes(p.tiles) + static_cast<size_t>(p.P) * 2 * kNP * kBM * sizeof(float);
+}
+
+bool skinny_tc_supported(const void* x, long long ldx, const void* w, int M, int N, int K) {
+  const bool al = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
+  return al && M >= 1 && M <= kNP && N >= 1 && K >= 8 && K % 8 == 0 && ldx % 8 == 0;
+}
+
+int launch_skinny_tc(const void* x, long long ldx, const void* w, void* y, long long ldy, int y_f32, int M, int N,
+                     int K, void* ws, size_t ws_bytes, cudaStream_t stream) {
+  const Partition p = partition(N, K);
+  const size_t need = skinny_tc_workspace_bytes(N, K);
+  if (ws == nullptr || ws_bytes < need)
+    return fail(BP_ERR_INVALID_ARGUMENT, "the tensor-core path needs a zero-initialised workspace of %zu bytes (got %zu)",
+                need, ws_bytes);
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(BP_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int st = ensure_smem_attr();
+  if (st != BP_OK) return st;
+  CUtensorMap tw, tx;
+  st = encode_2d_bf16(&tw, w, static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint64_t>(K) * 2, kBK, kBM,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
+  if (st != BP_OK) return st;
+  st = encode_2d_bf16(&tx, x, static_cast<uint64_t>(K), static_cast<uint64_t>(M), static_cast<uint64_t>(ldx) * 2, kBK, kNP,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+  if (st != BP_OK) return st;
+
+  TcArgs a;
+  a.y = y;
+  a.ldy = ldy;
+  a.y_f32 = y_f32;
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.tiles = p.tiles;
+  a.kblocks = p.kblocks;
+  a.units = p.units;
+  a.P = p.P;
+  a.counters = static_cast<int*>(ws);
+  a.partials = reinterpret_cast<float*>(static_cast<char*>(ws) + counters_bytes(p.tiles));
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.P, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_tc_kernel, tw, tx, a);
+  if (e != cudaSuccess)
+    return fail(BP_ERR_CUDA, "tensor-core skinny launch (M=%d N=%d K=%d P=%d): %s", M, N, K, p.P, cudaGetErrorString(e));
+  return BP_OK;
+}
+
+unsigned int read_and_clear_device_errors() {
+  unsigned int v = 0, zero = 0;
+  cudaMemcpyFromSymbol(&v, g_bp_device_errors, sizeof(v));
+  cudaMemcpyToSymbol(g_bp_device_errors, &zero, sizeof(zero));
+  return v;
+}
+
+}  // namespace bp

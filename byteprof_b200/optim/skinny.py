@@ -71,10 +71,11 @@ def skinny_mm(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = Non
         raise ValueError("w and scale must be contiguous")
     if scale is not None and kind == "int8" and scale.dtype != torch.bfloat16:
         scale = scale.to(torch.bfloat16)
+    wcode = _lib.dtype_code(w.dtype)
     with torch.cuda.device(x.device):
-        _lib.call("bp_skinny_mm", x.data_ptr(), k, w.data_ptr(), _lib.dtype_code(w.dtype),
-                  _lib.ptr(scale if kind == "int8" else None), y.data_ptr(), y.stride(0), _lib.dtype_code(y.dtype),
-                  m, n, k, _lib.stream_of(x))
+        ws, ws_bytes = _lib.skinny_workspace(x.device, m, n, k, wcode)
+        _lib.call("bp_skinny_mm", x.data_ptr(), k, w.data_ptr(), wcode, _lib.ptr(scale if kind == "int8" else None),
+                  y.data_ptr(), y.stride(0), _lib.dtype_code(y.dtype), m, n, k, ws, ws_bytes, _lib.stream_of(x))
     return y
 
 

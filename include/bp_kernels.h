@@ -59,12 +59,24 @@ const char* bp_last_error(void);
  *          w_dtype = BP_DTYPE_INT8: int8 [N, K] contiguous, w_scale = bf16 [N]; y = scale[n] * sum_k x*q
  *   y      y_dtype BP_DTYPE_BF16 or BP_DTYPE_F32 (the fp32 store is the un-rounded accumulator), row
  *          stride ldy elements; exactly the M x N block is written
+ *   workspace, workspace_bytes  caller-owned device scratch of at least
+ *          bp_skinny_workspace_bytes(M, N, K, w_dtype) bytes, 256-byte aligned, zero-filled once before
+ *          its first use; every call leaves it zero-filled again. Calls that overlap in time (other
+ *          streams) must use different workspaces. May be NULL when the query returns 0.
  * M = 0 or N = 0 writes nothing; K = 0 writes zeros. Any M is accepted; rows are processed in
  * chunks of 16 per launch (the weights are re-read per chunk, as the reference re-reads per 64 rows).
  * Replaces skinny_mm / _launch / _skinny_kernel MODE 0 and 1 (byteprof/optim/skinny.py:35-166).
  */
 int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale,
-                 void* y, long long ldy, int y_dtype, int M, int N, int K, void* stream);
+                 void* y, long long ldy, int y_dtype, int M, int N, int K, void* workspace,
+                 size_t workspace_bytes, void* stream);
+
+/*
+ * Workspace bytes bp_skinny_mm needs for this problem on the current device (0: none needed). The
+ * stream-K partial sums of the bf16 tensor-core path live there (byteprof/optim/skinny.py:125 allocates
+ * its split-K workspace per call instead).
+ */
+size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype);
 
 /*
  * int8 weight-only GEMV for one activation row: y[1, N] = scale[n] * sum_k x[k] * q[n, k].
@@ -106,6 +118,13 @@ int bp_mlstm_scan(const float* c_in, const float* n_in, const float* m_in, const
  * Replaces accept_kernel (byteprof/optim/mlstm_multistep.py:136-146).
  */
 int bp_mlstm_accept(const int64_t* ids, const int64_t* tok, int64_t* out, int S, int smax, void* stream);
+
+/*
+ * Device error flags raised by the kernels since the last call, then cleared (synchronises the current
+ * device). Bit 0: a bounded wait inside a kernel timed out (the kernel stopped early; its output is
+ * invalid). No counterpart in the reference, whose kernels have no waits.
+ */
+int bp_device_errors(unsigned int* flags);
 
 #ifdef __cplusplus
 }

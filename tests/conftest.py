@@ -35,8 +35,15 @@ def _kernel_library():
 
 @pytest.fixture(autouse=True)
 def _gpu_required(request):
-    if request.node.get_closest_marker("gpu") is not None:
+    """GPU tests need a device, and no kernel may have raised a device error (a bounded wait that
+    timed out) by the end of the test."""
+    gpu = request.node.get_closest_marker("gpu") is not None
+    if gpu:
         import torch
 
         assert torch.cuda.is_available(), "this test needs a CUDA device"
     yield
+    if gpu:
+        from byteprof_b200 import _lib
+
+        assert _lib.device_errors() == 0, "a kernel reported a device error (bounded wait timed out)"

@@ -14,7 +14,7 @@ HEADER = Path(__file__).resolve().parent.parent / "include" / "bp_kernels.h"
 
 def declared_functions() -> list[str]:
     text = HEADER.read_text()
-    return re.findall(r"^\s*(?:int|const char\*)\s+(bp_\w+)\s*\(", text, re.M)
+    return re.findall(r"^\s*(?:int|size_t|const char\*)\s+(bp_\w+)\s*\(", text, re.M)
 
 
 def test_header_and_binding_agree():
@@ -47,10 +47,10 @@ def test_status_codes_match_the_header():
 
 
 @pytest.mark.parametrize("args,msg", [
-    ((None, 0, None, 0, None, None, 0, 0, -1, 4, 4, None), b"negative size"),
-    ((None, 0, None, 7, None, None, 0, 0, 1, 4, 4, None), b"weight dtype"),
-    ((None, 0, None, 0, None, None, 0, 5, 1, 4, 4, None), b"output dtype"),
-    ((None, 0, None, 0, None, None, 4, 0, 4, 4, 4, None), b"y is NULL"),
+    ((None, 0, None, 0, None, None, 0, 0, -1, 4, 4, None, 0, None), b"negative size"),
+    ((None, 0, None, 7, None, None, 0, 0, 1, 4, 4, None, 0, None), b"weight dtype"),
+    ((None, 0, None, 0, None, None, 0, 5, 1, 4, 4, None, 0, None), b"output dtype"),
+    ((None, 0, None, 0, None, None, 4, 0, 4, 4, 4, None, 0, None), b"y is NULL"),
 ])
 def test_skinny_rejects_bad_arguments_before_touching_a_device(args, msg):
     L = _lib.lib()
@@ -60,8 +60,8 @@ def test_skinny_rejects_bad_arguments_before_touching_a_device(args, msg):
 
 def test_empty_problems_return_ok_without_a_device():
     L = _lib.lib()
-    assert L.bp_skinny_mm(None, 0, None, 0, None, None, 0, 0, 0, 4, 4, None) == 0
-    assert L.bp_skinny_mm(None, 0, None, 0, None, None, 0, 0, 3, 0, 4, None) == 0
+    assert L.bp_skinny_mm(None, 0, None, 0, None, None, 0, 0, 0, 4, 4, None, 0, None) == 0
+    assert L.bp_skinny_mm(None, 0, None, 0, None, None, 0, 0, 3, 0, 4, None, 0, None) == 0
     assert L.bp_last_error() == b""
 
 
@@ -83,3 +83,18 @@ def test_scan_rejects_unsupported_geometry_and_aliasing():
 def test_accept_rejects_bad_sizes():
     L = _lib.lib()
     assert L.bp_mlstm_accept(None, None, None, 5, 3, None) == 1
+
+
+def test_workspace_query_without_a_device():
+    L = _lib.lib()
+    assert L.bp_skinny_workspace_bytes(4, 2048, 2048, 2) == 0  # int8: CUDA-core path, no workspace
+    assert L.bp_skinny_workspace_bytes(0, 2048, 2048, 0) == 0
+    assert L.bp_skinny_workspace_bytes(4, 0, 2048, 0) == 0
+
+
+def test_binding_argument_counts_match_the_header():
+    text = HEADER.read_text()
+    for name, (_, args) in _lib._SIGNATURES.items():
+        decl = re.search(r"\b" + name + r"\s*\(([^;]*)\);", text, re.S).group(1).strip()
+        n = 0 if decl in ("void", "") else decl.count(",") + 1
+        assert n == len(args), name

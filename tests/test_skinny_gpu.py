@@ -168,3 +168,36 @@ def test_cuda_graph_replay_equals_eager(kind):
     g.replay()
     torch.cuda.synchronize()
     assert torch.equal(y, S.skinny_mm(x, *args))
+
+
+@pytest.mark.parametrize("n,k", [(2048, 2048), (8192, 2048), (2048, 8192), (37, 256), (129, 640)])
+def test_cuda_core_bf16_path_matches_too(n, k, monkeypatch):
+    """bf16 problems run on the tensor-core kernel; BP_SKINNY_PATH=fma selects the CUDA-core kernel,
+    which stays correct (it also serves unaligned shapes)."""
+    _, args = make_weights("bf16", n, k, seed=3)
+    wd = deq_np("bf16", args)
+    x = x_rows(7, k, seed=3)
+    tc = S.skinny_mm(x, *args)
+    monkeypatch.setenv("BP_SKINNY_PATH", "fma")
+    fma = S.skinny_mm(x, *args)
+    monkeypatch.delenv("BP_SKINNY_PATH")
+    assert skinny_ref.nerr(to_np(fma), to_np(x), wd) < TOL
+    assert skinny_ref.nerr(to_np(tc), to_np(x), wd) < TOL
+
+
+@pytest.mark.parametrize("n,k", [(100352, 2048), (2048, 2048), (129, 640), (1, 128), (300, 64)])
+def test_stream_k_split_tiles_are_deterministic_and_leave_the_workspace_clean(n, k):
+    """Tiles shared by several CTAs are summed by the last arriving one in a fixed order: repeated calls
+    give identical bits, and the per-tile counters are back to zero after each call."""
+    from byteprof_b200 import _lib
+
+    _, args = make_weights("bf16", n, k, seed=11)
+    x = x_rows(16, k, seed=11)
+    first = S.skinny_mm(x, *args)
+    for _ in range(4):
+        assert torch.equal(S.skinny_mm(x, *args), first)
+    torch.cuda.synchronize()
+    ws = _lib._workspaces[torch.cuda.current_device()]
+    tiles = (n + 127) // 128
+    assert int(ws[:4 * tiles].view(torch.int32).abs().sum()) == 0
+    assert skinny_ref.nerr(to_np(first), to_np(x), deq_np("bf16", args)) < TOL
