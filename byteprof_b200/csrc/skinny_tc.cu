@@ -345,19 +345,24 @@ Partition partition(int N, int K) {
   return p;
 }
 
-size_t counters_bytes(int tiles) { return (static_cast<size_t>(tiles) * 4 + 255) / 256 * 256; }
+// The workspace layout is the same for every shape: kMaxTiles tile counters, then the partials. (A
+// layout that depended on the tile count would let one shape's partials land on another shape's
+// counters, which must stay zero between launches.)
+constexpr int kMaxTiles = 8192;  // N up to 1,048,576 rows
+constexpr size_t kCountersBytes = static_cast<size_t>(kMaxTiles) * 4;
 
 }  // namespace
 
 size_t skinny_tc_workspace_bytes(int N, int K) {
   if (N <= 0 || K <= 0) return 0;
   const Partition p = partition(N, K);
-  return counters_bytes(p.tiles) + static_cast<size_t>(p.P) * 2 * kNP * kBM * sizeof(float);
+  return kCountersBytes + static_cast<size_t>(p.P) * 2 * kNP * kBM * sizeof(float);
 }
 
 bool skinny_tc_supported(const void* x, long long ldx, const void* w, int M, int N, int K) {
   const bool al = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
-  return al && M >= 1 && M <= kNP && N >= 1 && K >= 8 && K % 8 == 0 && ldx % 8 == 0;
+  return al && M >= 1 && M <= kNP && N >= 1 && (N + kBM - 1) / kBM <= kMaxTiles && K >= 8 && K % 8 == 0 &&
+         ldx % 8 == 0;
 }
 
 int launch_skinny_tc(const void* x, long long ldx, const void* w, void* y, long long ldy, int y_f32, int M, int N,
@@ -390,7 +395,7 @@ int launch_skinny_tc(const void* x, long long ldx, const void* w, void* y, long 
   a.units = p.units;
   a.P = p.P;
   a.counters = static_cast<int*>(ws);
-  a.partials = reinterpret_cast<float*>(static_cast<char*>(ws) + counters_bytes(p.tiles));
+  a.partials = reinterpret_cast<float*>(static_cast<char*>(ws) + kCountersBytes);
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.P, 1, 1);
