@@ -489,6 +489,15 @@ def run_case(args) -> int:
     for i in range(args.warmup):
         skinny_mm(x, *ring[i % len(ring)], out=y)
     torch.cuda.synchronize()
+    if args.graph:  # one graph of a call per ring member, replayed: device time per call without host gaps
+        gr = capture(lambda: [skinny_mm(x, *wq, out=y) for wq in ring])
+        reps = max(1, args.steps // len(ring))
+        time_graph_replays(gr, 2)
+        us = time_graph_replays(gr, reps) * 1e3 / (reps * len(ring))
+        nb = alg_bytes(m, n, k, kind)
+        print(json.dumps({"case": f"{n}x{k}|M{m}|{kind}", "us": round(us, 3), "gbs": round(nb / (us * 1e-6) / 1e9, 1),
+                          "bytes": nb, "graph": True, "pdl": os.environ.get("BP_DISABLE_PDL") != "1"}), flush=True)
+        return 0
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for i in range(args.steps):
@@ -510,6 +519,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the per-cell, int8, scan and CPU passes")
     ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8]: time one sweep cell alone (ncu captures)")
+    ap.add_argument("--graph", action="store_true", help="with --case: time a CUDA graph of the weight ring")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")

@@ -47,9 +47,10 @@ struct TcArgs {
   int M, N, K;
   int tiles, kblocks;
   long long units;
-  int P;
-  int* counters;    // [tiles], zero between launches
-  float* partials;  // [P][2][kNP][kBM]
+  int P;            // CTAs
+  int S;            // cluster mode: CTAs per tile (split-K inside a cluster); 0: stream-K mode
+  int* counters;    // stream-K: [tiles], zero between launches
+  float* partials;  // stream-K: [P][2][kNP][kBM]
 };
 
 struct __align__(1024) TcSmem {
@@ -99,6 +100,10 @@ __device__ __forceinline__ void store_rows(const TcArgs& a, int row, const float
   }
 }
 
+// kCluster = false: stream-K over (tile, k-block) units, split tiles finished through the workspace.
+// kCluster = true: grid = tiles x S, the S CTAs of a cluster split one tile's K range evenly and add
+// their partials through distributed shared memory (used when there are few tiles).
+template <bool kCluster>
 __global__ void __launch_bounds__(kThreads, 2)
     skinny_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
@@ -107,7 +112,17 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int c = blockIdx.x;
   const long long U = a.units;
   const int KB = a.kblocks;
-  const long long u0 = unit_start(c, U, a.P), u1 = unit_start(c + 1, U, a.P);
+  long long u0, u1;
+  int rank = 0;
+  if constexpr (kCluster) {
+    rank = static_cast<int>(cluster_ctarank());
+    const long long t = cluster_id_x();
+    u0 = t * KB + static_cast<long long>(rank) * KB / a.S;
+    u1 = t * KB + static_cast<long long>(rank + 1) * KB / a.S;
+  } else {
+    u0 = unit_start(c, U, a.P);
+    u1 = unit_start(c + 1, U, a.P);
+  }
   const int n_units = static_cast<int>(u1 - u0);
   const int t_first = static_cast<int>(u0 / KB);
   const int t_last = n_units > 0 ? static_cast<int>((u1 - 1) / KB) : t_first - 1;
@@ -221,6 +236,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       tmem_ld_32x32b_x16(tmem + (static_cast<uint32_t>(32 * q) << 16) + static_cast<uint32_t>(buf * kNP), acc);
       tc_fence_before_sync();
       mbar_arrive(&s.tempty[buf]);
+      if constexpr (kCluster) {
+        // one tile per CTA: the partial goes to this CTA's shared memory (stage 0 is free: every MMA
+        // that read it has completed) for the cluster reduction below
+        float* red = reinterpret_cast<float*>(s.a[0]);
+#pragma unroll
+        for (int m = 0; m < kNP; ++m)
+          if (m < a.M) red[m * kBM + r] = acc[m];
+        continue;
+      }
       const int row = t * kBM + r;
       const int c_lo = unit_owner(static_cast<long long>(t) * KB, U, a.P);
       const int c_hi = unit_owner(static_cast<long long>(t + 1) * KB - 1, U, a.P);
@@ -231,32 +255,88 @@ __global__ void __launch_bounds__(kThreads, 2)
       const int slot = (t == t_first) ? 0 : 1;
       float* mine = a.partials + static_cast<size_t>(c * 2 + slot) * kNP * kBM;
 #pragma unroll
-      for (int m = 0; m < kNP; ++m) mine[m * kBM + r] = acc[m];
-      __threadfence();
+      for (int m = 0; m < kNP; ++m)
+        if (m < a.M) mine[m * kBM + r] = acc[m];  // only the live activation rows travel
       __syncwarp();
-      named_barrier_sync(1, kEpiThreads);
+      named_barrier_sync(1, kEpiThreads);  // every partial of this CTA is written ...
       if (et == 0) {
+        __threadfence();  // ... and (cumulatively) visible GPU-wide before the arrival is counted
         const int old = atomicAdd(&a.counters[t], 1);
         const int last = old == c_hi - c_lo;
-        if (last) a.counters[t] = 0;  // every contributor has arrived: ready for the next launch
+        if (last) {
+          a.counters[t] = 0;  // every contributor has arrived: ready for the next launch
+          __threadfence();    // acquire side: the other contributors' partials are visible from here on
+        }
         s.last_flag = last;
       }
       __syncwarp();
       named_barrier_sync(1, kEpiThreads);
       if (s.last_flag) {
-        __threadfence();
         float v[kNP];
 #pragma unroll
         for (int m = 0; m < kNP; ++m) v[m] = 0.0f;
-        for (int cc = c_lo; cc <= c_hi; ++cc) {  // fixed order: the sum does not depend on arrival order
+        // fixed order c_lo..c_hi (the sum does not depend on arrival order); four contributors' loads
+        // are in flight at once
+        int cc = c_lo;
+        for (; cc + 3 <= c_hi; cc += 4) {
+          float t4[4][kNP];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int cj = cc + j;
+            const int cslot = (t == static_cast<int>(unit_start(cj, U, a.P) / KB)) ? 0 : 1;
+            const float* p = a.partials + static_cast<size_t>(cj * 2 + cslot) * kNP * kBM;
+#pragma unroll
+            for (int m = 0; m < kNP; ++m) t4[j][m] = m < a.M ? __ldcg(p + m * kBM + r) : 0.0f;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int m = 0; m < kNP; ++m) v[m] += t4[j][m];
+        }
+        for (; cc <= c_hi; ++cc) {
           const int cslot = (t == static_cast<int>(unit_start(cc, U, a.P) / KB)) ? 0 : 1;
           const float* p = a.partials + static_cast<size_t>(cc * 2 + cslot) * kNP * kBM;
 #pragma unroll
-          for (int m = 0; m < kNP; ++m) v[m] += __ldcg(p + m * kBM + r);
+          for (int m = 0; m < kNP; ++m)
+            if (m < a.M) v[m] += __ldcg(p + m * kBM + r);
         }
         store_rows(a, row, v);
       }
     }
+  }
+
+  if constexpr (kCluster) {
+    // Split-K through distributed shared memory: CTA `rank` finishes rows [rank R, rank R + R) of the
+    // tile, adding the S partials in rank order (deterministic), then stores them.
+    cluster_sync_unaligned();  // every CTA's partial is in its shared memory
+    const int S = a.S;
+    const int R = (kBM + S - 1) / S;
+    const int r0 = rank * R;
+    const int nrows = (r0 + R <= kBM ? R : kBM - r0) > 0 ? (r0 + R <= kBM ? R : kBM - r0) : 0;
+    const int t = static_cast<int>(cluster_id_x());
+    const uint32_t red = smem_addr(s.a[0]);
+    if (!*abort) {
+      for (int item = threadIdx.x; item < nrows * a.M; item += kThreads) {
+        const int m = item / nrows, lr = item - m * nrows;
+        const int rr = r0 + lr;
+        const uint32_t off = red + static_cast<uint32_t>((m * kBM + rr) * 4);
+        float part[16];
+#pragma unroll
+        for (int qq = 0; qq < 16; ++qq) part[qq] = qq < S ? ld_shared_cluster_f32(mapa_shared(off, qq)) : 0.0f;
+        float v = 0.0f;
+#pragma unroll
+        for (int qq = 0; qq < 16; ++qq)
+          if (qq < S) v += part[qq];
+        const int row = t * kBM + rr;
+        if (row < a.N) {
+          if (a.y_f32)
+            static_cast<float*>(a.y)[m * a.ldy + row] = v;
+          else
+            static_cast<__nv_bfloat16*>(a.y)[m * a.ldy + row] = __float2bfloat16_rn(v);
+        }
+      }
+    }
+    cluster_sync_unaligned();  // peers have finished reading this CTA's shared memory
   }
 
   tc_fence_before_sync();
@@ -309,12 +389,13 @@ int tc_sm_count() {
   return cached[dev];
 }
 
-int ensure_smem_attr() {
+template <bool kCluster>
+int ensure_attrs() {
   static bool done[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && done[dev]) return BP_OK;
-  cudaError_t e = cudaFuncSetAttribute(skinny_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(skinny_tc_kernel<kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(kSmemBytes));
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "cudaFuncSetAttribute(smem %zu): %s", kSmemBytes, cudaGetErrorString(e));
   if (dev >= 0 && dev < 64) done[dev] = true;
@@ -330,8 +411,11 @@ bool pdl_enabled() {
   return v == 1;
 }
 
+constexpr int kMaxClusterSplit = 8;  // portable cluster size
+
+// Work partition; depends on (N, K) and the SM count only, never on M.
 struct Partition {
-  int tiles, kblocks, P;
+  int tiles, kblocks, P, S;  // S > 0: cluster mode with S CTAs per tile; S == 0: stream-K over P CTAs
   long long units;
 };
 
@@ -341,7 +425,17 @@ Partition partition(int N, int K) {
   p.kblocks = (K + kBK - 1) / kBK;
   p.units = static_cast<long long>(p.tiles) * p.kblocks;
   const int sms = tc_sm_count();
-  p.P = static_cast<int>(p.units < sms ? p.units : sms);
+  if (2 * p.tiles <= sms) {
+    // few tiles: split each tile's K range over a cluster of S CTAs (no workspace, no global fix-up)
+    int S = sms / p.tiles;
+    if (S > kMaxClusterSplit) S = kMaxClusterSplit;
+    if (S > p.kblocks) S = p.kblocks;
+    p.S = S < 1 ? 1 : S;
+    p.P = p.tiles * p.S;
+  } else {
+    p.S = 0;
+    p.P = static_cast<int>(p.units < sms ? p.units : sms);
+  }
   return p;
 }
 
@@ -356,6 +450,7 @@ constexpr size_t kCountersBytes = static_cast<size_t>(kMaxTiles) * 4;
 size_t skinny_tc_workspace_bytes(int N, int K) {
   if (N <= 0 || K <= 0) return 0;
   const Partition p = partition(N, K);
+  if (p.S > 0) return 0;  // cluster mode needs no workspace
   return kCountersBytes + static_cast<size_t>(p.P) * 2 * kNP * kBM * sizeof(float);
 }
 
@@ -369,11 +464,12 @@ int launch_skinny_tc(const void* x, long long ldx, const void* w, void* y, long 
                      int K, void* ws, size_t ws_bytes, cudaStream_t stream) {
   const Partition p = partition(N, K);
   const size_t need = skinny_tc_workspace_bytes(N, K);
-  if (ws == nullptr || ws_bytes < need)
+  if (need > 0 && (ws == nullptr || ws_bytes < need))
     return fail(BP_ERR_INVALID_ARGUMENT, "the tensor-core path needs a zero-initialised workspace of %zu bytes (got %zu)",
                 need, ws_bytes);
-  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return fail(BP_ERR_MISALIGNED, "workspace must be 256-byte aligned");
-  int st = ensure_smem_attr();
+  if (need > 0 && (reinterpret_cast<uintptr_t>(ws) & 255u) != 0)
+    return fail(BP_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+  int st = p.S > 0 ? ensure_attrs<true>() : ensure_attrs<false>();
   if (st != BP_OK) return st;
   CUtensorMap tw, tx;
   st = encode_2d_bf16(&tw, w, static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint64_t>(K) * 2, kBK, kBM,
@@ -394,22 +490,36 @@ int launch_skinny_tc(const void* x, long long ldx, const void* w, void* y, long 
   a.kblocks = p.kblocks;
   a.units = p.units;
   a.P = p.P;
-  a.counters = static_cast<int*>(ws);
-  a.partials = reinterpret_cast<float*>(static_cast<char*>(ws) + kCountersBytes);
+  a.S = p.S;
+  a.counters = need > 0 ? static_cast<int*>(ws) : nullptr;
+  a.partials = need > 0 ? reinterpret_cast<float*>(static_cast<char*>(ws) + kCountersBytes) : nullptr;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.P, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl_enabled()) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (p.S > 0) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = p.S;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_tc_kernel, tw, tx, a);
+  cfg.numAttrs = na;
+  cudaError_t e = p.S > 0 ? cudaLaunchKernelEx(&cfg, skinny_tc_kernel<true>, tw, tx, a)
+                          : cudaLaunchKernelEx(&cfg, skinny_tc_kernel<false>, tw, tx, a);
   if (e != cudaSuccess)
-    return fail(BP_ERR_CUDA, "tensor-core skinny launch (M=%d N=%d K=%d P=%d): %s", M, N, K, p.P, cudaGetErrorString(e));
+    return fail(BP_ERR_CUDA, "tensor-core skinny launch (M=%d N=%d K=%d P=%d S=%d): %s", M, N, K, p.P, p.S,
+                cudaGetErrorString(e));
   return BP_OK;
 }
 

@@ -173,6 +173,34 @@ __device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred
   return r != 0;
 }
 
+// ---- thread-block clusters ------------------------------------------------------------------------------
+// Cluster barrier without `.aligned`: every thread of every CTA of the cluster arrives, possibly from
+// divergent places. Release / acquire order shared-memory writes before peers' distributed reads.
+__device__ __forceinline__ void cluster_sync_unaligned() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
+
 // CTA-wide barrier without the `.aligned` requirement: threads of one warp may arrive from different
 // places (single-lane producer and MMA loops).
 __device__ __forceinline__ void cta_barrier_unaligned() { asm volatile("barrier.sync 0;" ::: "memory"); }

@@ -185,7 +185,8 @@ def test_cuda_core_bf16_path_matches_too(n, k, monkeypatch):
     assert skinny_ref.nerr(to_np(tc), to_np(x), wd) < TOL
 
 
-@pytest.mark.parametrize("n,k", [(100352, 2048), (2048, 2048), (129, 640), (1, 128), (300, 64)])
+@pytest.mark.parametrize("n,k", [(100352, 2048), (12288, 2048), (2048, 2048), (129, 640), (1, 128), (300, 64),
+                                 (1024, 2048), (2048, 8192)])
 def test_stream_k_split_tiles_are_deterministic_and_leave_the_workspace_clean(n, k):
     """Tiles shared by several CTAs are summed by the last arriving one in a fixed order: repeated calls
     give identical bits, and the per-tile counters are back to zero after each call."""
@@ -197,16 +198,17 @@ def test_stream_k_split_tiles_are_deterministic_and_leave_the_workspace_clean(n,
     for _ in range(4):
         assert torch.equal(S.skinny_mm(x, *args), first)
     torch.cuda.synchronize()
-    ws = _lib._workspaces[torch.cuda.current_device()]
+    ws = _lib._workspaces.get(torch.cuda.current_device())
     tiles = (n + 127) // 128
-    assert int(ws[:4 * tiles].view(torch.int32).abs().sum()) == 0
+    if ws is not None:  # shapes with few tiles split K inside a cluster and need no workspace
+        assert int(ws[:4 * tiles].view(torch.int32).abs().sum()) == 0
     assert skinny_ref.nerr(to_np(first), to_np(x), deq_np("bf16", args)) < TOL
 
 
 def test_one_workspace_serves_alternating_shapes():
     """The per-device workspace is shared by every shape: a small shape's stream-K partials must never
     land on a larger shape's tile counters (which have to be zero at the start of each call)."""
-    shapes = [(37, 256), (100352, 2048), (2048, 2048), (49152, 2048), (129, 640), (100352, 2048)]
+    shapes = [(37, 256), (100352, 2048), (2048, 2048), (49152, 2048), (129, 640), (12288, 2048), (100352, 2048)]
     made = {}
     for n, k in shapes:
         if (n, k) not in made:
