@@ -523,6 +523,70 @@ int launch_skinny_tc(const void* x, long long ldx, const void* w, void* y, long 
   return BP_OK;
 }
 
+// ---- entry point for callers that cannot allocate device memory -----------------------------------
+//
+// Some callers have no way to allocate device memory for the stream-K scratch: code that runs while a
+// stream is being captured into a CUDA graph in global capture mode (cudaMalloc is refused there), and
+// host applications that hand out all device memory from their own pre-reserved pool and give plugins
+// no allocator. For them, the scratch of the bf16 tensor-core path lives in this fixed array instead of
+// a caller-provided workspace. It is part of the module, so every GPU that loads the library holds it
+// (2.6 MB) until the process exits. Limits: at most kStaticMaxCtas streaming multiprocessors (B200 has
+// 148) and N <= kMaxTiles * 128 rows; larger problems are rejected with BP_ERR_UNSUPPORTED.
+constexpr int kStaticMaxCtas = 160;
+constexpr size_t kStaticScratchBytes = kCountersBytes + static_cast<size_t>(kStaticMaxCtas) * 2 * kNP * kBM * sizeof(float);
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device (host code must not pass the symbol itself:
+// on the host it is only a stand-in). Looked up once per device.
+static int static_scratch_ptr(void** out) {
+  static void* ptrs[64] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(BP_ERR_UNSUPPORTED, "device index %d out of range", dev);
+  if (ptrs[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(BP_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+    ptrs[dev] = p;
+  }
+  *out = ptrs[dev];
+  return BP_OK;
+}
+
+}  // namespace bp
+
+extern "C" int bp_skinny_mm_static_scratch(const void* x, long long ldx, const void* w, int w_dtype,
+                                           const void* w_scale, void* y, long long ldy, int y_dtype, int M, int N,
+                                           int K, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (M > 0 && N > 0 && K > 0 && w_dtype == BP_DTYPE_BF16) {
+    int st = require_sm100();
+    if (st != BP_OK) return st;
+    const size_t need = skinny_tc_workspace_bytes(N, K);
+    if ((N + kBM - 1) / kBM > kMaxTiles || need > kStaticScratchBytes)
+      return fail(BP_ERR_UNSUPPORTED,
+                  "N=%d K=%d needs %zu bytes of scratch; the static scratch holds %zu (N <= %d rows, <= %d SMs)", N, K,
+                  need, kStaticScratchBytes, kMaxTiles * kBM, kStaticMaxCtas);
+    if (need > 0) {
+      void* scratch = nullptr;
+      st = static_scratch_ptr(&scratch);
+      if (st != BP_OK) return st;
+      // The tile counters must start at zero. Every call leaves them at zero, but a call that stopped
+      // early (device error) would not, so they are cleared on the stream before each call.
+      const size_t tiles = static_cast<size_t>((N + kBM - 1) / kBM);
+      cudaError_t e = cudaMemsetAsync(scratch, 0, tiles * 4, static_cast<cudaStream_t>(stream));
+      if (e != cudaSuccess) return fail(BP_ERR_CUDA, "clearing the static scratch counters: %s", cudaGetErrorString(e));
+      return bp_skinny_mm(x, ldx, w, w_dtype, w_scale, y, ldy, y_dtype, M, N, K, scratch, kStaticScratchBytes, stream);
+    }
+  }
+  return bp_skinny_mm(x, ldx, w, w_dtype, w_scale, y, ldy, y_dtype, M, N, K, nullptr, 0, stream);
+}
+
+namespace bp {
+
 unsigned int read_and_clear_device_errors() {
   unsigned int v = 0, zero = 0;
   cudaMemcpyFromSymbol(&v, g_bp_device_errors, sizeof(v));

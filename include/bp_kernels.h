@@ -79,6 +79,21 @@ int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const
 size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype);
 
 /*
+ * bp_skinny_mm for callers that cannot allocate device memory (no counterpart in the reference).
+ * Same arguments and results as bp_skinny_mm without the workspace: the scratch of the bf16
+ * tensor-core path is a fixed 2.6 MB array inside the library (held by every GPU that loads it, until
+ * the process exits). Meant for code that runs during CUDA-graph capture in global mode, where
+ * cudaMalloc is refused, and for hosts that give their plugins no allocator.
+ * Limits: N <= 1,048,576 rows and a device with at most 160 SMs; larger problems return
+ * BP_ERR_UNSUPPORTED. Allocates nothing. The first call on a device looks up the array's device
+ * address (cudaGetSymbolAddress): make that first call before any stream capture. Each call clears the
+ * array's tile counters on the stream, then launches; every call shares the one array, so calls that
+ * overlap on the GPU (other streams) race with each other.
+ */
+int bp_skinny_mm_static_scratch(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale,
+                                void* y, long long ldy, int y_dtype, int M, int N, int K, void* stream);
+
+/*
  * int8 weight-only GEMV for one activation row: y[1, N] = scale[n] * sum_k x[k] * q[n, k].
  * Same kernel family as bp_skinny_mm with M = 1 (byteprof/quant/triton_int8.py:15-47).
  */

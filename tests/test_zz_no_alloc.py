@@ -1,0 +1,55 @@
+"""The entry point for callers that cannot allocate device memory, bp_skinny_mm_static_scratch.
+
+Code running inside a CUDA-graph capture in global mode (where cudaMalloc is refused), or inside a host
+application that gives its plugins no allocator, cannot hand bp_skinny_mm a workspace. This entry point
+keeps the tensor-core path's scratch in a fixed array inside the library instead. Its results must be
+those of bp_skinny_mm with a caller-provided workspace, call after call.
+
+This file is collected last (test_zz_*), and it depends on no state left by other tests: it passes run
+alone in a fresh process and after the rest of the suite.
+"""
+
+import pytest
+import torch
+
+from byteprof_b200 import _lib
+from byteprof_b200.optim.skinny import skinny_mm
+from helpers import deq_np, make_weights, to_np
+from oracle import skinny_ref
+
+pytestmark = pytest.mark.gpu
+
+
+def _static_scratch_mm(x, w, out):
+    m, k = x.shape
+    n = w.shape[0]
+    with torch.cuda.device(x.device):
+        _lib.call("bp_skinny_mm_static_scratch", x.data_ptr(), k, w.data_ptr(), _lib.BP_DTYPE_BF16, None, out.data_ptr(),
+                  out.stride(0), _lib.dtype_code(out.dtype), m, n, k, torch.cuda.current_stream(x.device).cuda_stream)
+    return out
+
+
+@pytest.mark.parametrize("n,k,m", [(100352, 2048, 4), (12288, 2048, 16), (2048, 2048, 1), (37, 256, 3)])
+def test_static_scratch_matches_the_workspace_entry_point_twice_in_a_row(n, k, m):
+    """Large shapes (many tiles) use the static scratch for their stream-K partials; small ones need none.
+    Two consecutive calls must both equal the result of the entry point with a caller workspace."""
+    _, args = make_weights("bf16", n, k, seed=31)
+    w = args[0]
+    g = torch.Generator(device="cuda").manual_seed(7)
+    x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
+    want = skinny_mm(x, w)
+    for _ in range(2):
+        got = _static_scratch_mm(x, w, torch.empty(m, n, device="cuda", dtype=torch.bfloat16))
+        torch.cuda.synchronize()
+        assert skinny_ref.nerr(to_np(got), to_np(x), deq_np("bf16", args)) < skinny_ref.TOL_COMPONENTWISE
+        assert torch.equal(got, want)
+    assert _lib.device_errors() == 0
+
+
+def test_static_scratch_rejects_problems_beyond_its_limit():
+    x = torch.zeros(1, 64, device="cuda", dtype=torch.bfloat16)
+    w = torch.zeros(8, 64, device="cuda", dtype=torch.bfloat16)
+    y = torch.empty(1, 8, device="cuda", dtype=torch.bfloat16)
+    st = _lib.lib().bp_skinny_mm_static_scratch(x.data_ptr(), 64, w.data_ptr(), 0, None, y.data_ptr(), 8, 0, 1,
+                                                2_000_000, 64, None)
+    assert st == 2 and b"static scratch" in _lib.lib().bp_last_error()
