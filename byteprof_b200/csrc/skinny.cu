@@ -321,8 +321,8 @@ bool tc_path_enabled() {
 }  // namespace bp
 
 extern "C" size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype) {
-  if (M <= 0 || N <= 0 || K <= 0 || w_dtype != BP_DTYPE_BF16) return 0;
-  return bp::skinny_tc_workspace_bytes(N, K);
+  if (M <= 0 || N <= 0 || K <= 0 || (w_dtype != BP_DTYPE_BF16 && w_dtype != BP_DTYPE_INT8)) return 0;
+  return bp::skinny_tc_workspace_bytes(N, K, w_dtype == BP_DTYPE_INT8);
 }
 
 extern "C" int bp_device_errors(unsigned int* flags) {
@@ -378,8 +378,8 @@ extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_d
     const int m = M - r0 < 16 ? M - r0 : 16;
     a.x = static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r0) * ldx;
     a.y = static_cast<char*>(y) + static_cast<long long>(r0) * ldy * static_cast<long long>(ysz);
-    if (!is8 && tc_path_enabled() && skinny_tc_supported(a.x, ldx, w, m, N, K))
-      st = launch_skinny_tc(a.x, ldx, w, a.y, ldy, a.y_f32, m, N, K, workspace, workspace_bytes, s);
+    if (tc_path_enabled() && skinny_tc_supported(a.x, ldx, w, m, N, K, is8))
+      st = launch_skinny_tc(a.x, ldx, w, w_scale, a.y, ldy, a.y_f32, m, N, K, is8, workspace, workspace_bytes, s);
     else
       st = is8 ? dispatch_m<int8_t>(a, m, vec, s) : dispatch_m<__nv_bfloat16>(a, m, vec, s);
     if (st != BP_OK) return st;
@@ -388,6 +388,6 @@ extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_d
 }
 
 extern "C" int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,
-                            void* stream) {
-  return bp_skinny_mm(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, nullptr, 0, stream);
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  return bp_skinny_mm(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, workspace, workspace_bytes, stream);
 }

@@ -80,8 +80,8 @@ size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype);
 
 /*
  * bp_skinny_mm for callers that cannot allocate device memory (no counterpart in the reference).
- * Same arguments and results as bp_skinny_mm without the workspace: the scratch of the bf16
- * tensor-core path is a fixed 2.6 MB array inside the library (held by every GPU that loads it, until
+ * Same arguments and results as bp_skinny_mm without the workspace: the scratch of the
+ * tensor-core path (bf16 and int8 weights) is a fixed 2.6 MB array inside the library (held by every GPU that loads it, until
  * the process exits). Meant for code that runs during CUDA-graph capture in global mode, where
  * cudaMalloc is refused, and for hosts that give their plugins no allocator.
  * Limits: N <= 1,048,576 rows and a device with at most 160 SMs; larger problems return
@@ -95,10 +95,11 @@ int bp_skinny_mm_static_scratch(const void* x, long long ldx, const void* w, int
 
 /*
  * int8 weight-only GEMV for one activation row: y[1, N] = scale[n] * sum_k x[k] * q[n, k].
- * Same kernel family as bp_skinny_mm with M = 1 (byteprof/quant/triton_int8.py:15-47).
+ * bp_skinny_mm with M = 1 and int8 weights, including its workspace rule
+ * (byteprof/quant/triton_int8.py:15-47).
  */
 int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,
-                 void* stream);
+                 void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * Fused mLSTM recurrence over T positions (exponential gating with the max stabiliser m), one head

@@ -170,12 +170,13 @@ def test_cuda_graph_replay_equals_eager(kind):
     assert torch.equal(y, S.skinny_mm(x, *args))
 
 
-@pytest.mark.parametrize("n,k", [(2048, 2048), (8192, 2048), (2048, 8192), (37, 256), (129, 640)])
-def test_cuda_core_bf16_path_matches_too(n, k, monkeypatch):
-    """bf16 problems run on the tensor-core kernel; BP_SKINNY_PATH=fma selects the CUDA-core kernel,
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
+@pytest.mark.parametrize("n,k", [(2048, 2048), (8192, 2048), (2048, 8192), (37, 256), (129, 640), (12288, 2048)])
+def test_cuda_core_path_matches_too(kind, n, k, monkeypatch):
+    """Aligned problems run on the tensor-core kernel; BP_SKINNY_PATH=fma selects the CUDA-core kernel,
     which stays correct (it also serves unaligned shapes)."""
-    _, args = make_weights("bf16", n, k, seed=3)
-    wd = deq_np("bf16", args)
+    _, args = make_weights(kind, n, k, seed=3)
+    wd = deq_np(kind, args)
     x = x_rows(7, k, seed=3)
     tc = S.skinny_mm(x, *args)
     monkeypatch.setenv("BP_SKINNY_PATH", "fma")

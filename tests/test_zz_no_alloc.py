@@ -20,28 +20,30 @@ from oracle import skinny_ref
 pytestmark = pytest.mark.gpu
 
 
-def _static_scratch_mm(x, w, out):
+def _static_scratch_mm(x, w, out, scale=None):
     m, k = x.shape
     n = w.shape[0]
     with torch.cuda.device(x.device):
-        _lib.call("bp_skinny_mm_static_scratch", x.data_ptr(), k, w.data_ptr(), _lib.BP_DTYPE_BF16, None, out.data_ptr(),
-                  out.stride(0), _lib.dtype_code(out.dtype), m, n, k, torch.cuda.current_stream(x.device).cuda_stream)
+        _lib.call("bp_skinny_mm_static_scratch", x.data_ptr(), k, w.data_ptr(), _lib.dtype_code(w.dtype),
+                  _lib.ptr(scale), out.data_ptr(), out.stride(0), _lib.dtype_code(out.dtype), m, n, k,
+                  torch.cuda.current_stream(x.device).cuda_stream)
     return out
 
 
+@pytest.mark.parametrize("kind", ["bf16", "int8"])
 @pytest.mark.parametrize("n,k,m", [(100352, 2048, 4), (12288, 2048, 16), (2048, 2048, 1), (37, 256, 3)])
-def test_static_scratch_matches_the_workspace_entry_point_twice_in_a_row(n, k, m):
+def test_static_scratch_matches_the_workspace_entry_point_twice_in_a_row(kind, n, k, m):
     """Large shapes (many tiles) use the static scratch for their stream-K partials; small ones need none.
     Two consecutive calls must both equal the result of the entry point with a caller workspace."""
-    _, args = make_weights("bf16", n, k, seed=31)
-    w = args[0]
+    _, args = make_weights(kind, n, k, seed=31)
     g = torch.Generator(device="cuda").manual_seed(7)
     x = torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
-    want = skinny_mm(x, w)
+    want = skinny_mm(x, *args)
     for _ in range(2):
-        got = _static_scratch_mm(x, w, torch.empty(m, n, device="cuda", dtype=torch.bfloat16))
+        got = _static_scratch_mm(x, args[0], torch.empty(m, n, device="cuda", dtype=torch.bfloat16),
+                                 args[1] if kind == "int8" else None)
         torch.cuda.synchronize()
-        assert skinny_ref.nerr(to_np(got), to_np(x), deq_np("bf16", args)) < skinny_ref.TOL_COMPONENTWISE
+        assert skinny_ref.nerr(to_np(got), to_np(x), deq_np(kind, args)) < skinny_ref.TOL_COMPONENTWISE
         assert torch.equal(got, want)
     assert _lib.device_errors() == 0
 
