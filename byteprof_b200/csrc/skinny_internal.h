@@ -1,21 +1,43 @@
-// Internal interface between the C-ABI entry point (skinny.cu) and the tensor-core kernel (skinny_tc.cu).
+// Internal interface between the C-ABI entry point (skinny.cu) and the tensor-core kernels
+// (skinny_tc.cu: bf16 weights; skinny_i8.cu: int8 weights).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
+#include <stdint.h>
 
 namespace bp {
+
+// Stream-K workspace layout, the same for every shape: kTcMaxTiles tile counters, then the partials. (A
+// layout that depended on the tile count would let one shape's partials land on another shape's
+// counters, which must stay zero between launches.)
+constexpr int kTcMaxTiles = 8192;
+constexpr size_t kTcCountersBytes = static_cast<size_t>(kTcMaxTiles) * 4;
 
 // Bytes of zero-initialised workspace the tensor-core path needs for an N x K weight (0 if N or K is 0,
 // or if the shape runs in cluster mode).
 size_t skinny_tc_workspace_bytes(int N, int K, bool int8);
 
 // Whether the tensor-core path takes this problem (16-byte aligned bases, ldx a multiple of 8,
-// 1 <= M <= 16, K a multiple of 8 for bf16 and of 128 for int8 weights).
+// 1 <= M <= 16; K a multiple of 8 for bf16 weights, of 16 and at most 131072 for int8 weights).
 bool skinny_tc_supported(const void* x, long long ldx, const void* w, int M, int N, int K, bool int8);
 
 int launch_skinny_tc(const void* x, long long ldx, const void* w, const void* w_scale, void* y, long long ldy, int y_f32,
                      int M, int N, int K, bool int8, void* ws, size_t ws_bytes, cudaStream_t stream);
+
+// int8 weights (skinny_i8.cu).
+size_t skinny_i8_workspace_bytes(int N, int K);
+bool skinny_i8_supported(const void* x, long long ldx, const void* w, int M, int N, int K);
+int launch_skinny_i8(const void* x, long long ldx, const void* w, const void* w_scale, void* y, long long ldy, int y_f32,
+                     int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t stream);
+
+// Shared host helpers (skinny_tc.cu): a 2D tensor map with 128-byte swizzle, the SM count of the current
+// device, and whether programmatic dependent launch is on (BP_DISABLE_PDL=1 turns it off).
+int tc_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapL2promotion promo);
+int tc_sm_count();
+bool tc_pdl_enabled();
 
 // Reads and clears the device error word (synchronising copy).
 unsigned int read_and_clear_device_errors();

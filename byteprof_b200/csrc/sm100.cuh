@@ -134,6 +134,19 @@ __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 lanes x 32 consecutive 32-bit TMEM columns (raw bits).
+__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
 // Shared-memory matrix descriptor: K-major operand written by TMA with 128-byte swizzling, rows of
 // 128 bytes, 8-row groups 1024 bytes apart (the stage buffers are 1024-byte aligned).
 __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
@@ -176,7 +189,10 @@ __device__ __forceinline__ bool named_barrier_or(int id, int nthreads, bool pred
 // ---- thread-block clusters ------------------------------------------------------------------------------
 // Cluster barrier without `.aligned`: every thread of every CTA of the cluster arrives, possibly from
 // divergent places. Release / acquire order shared-memory writes before peers' distributed reads.
+// Cluster-wide barrier (release / acquire); each warp reconverges first so that all its threads arrive
+// together.
 __device__ __forceinline__ void cluster_sync_unaligned() {
+  __syncwarp();
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
 __device__ __forceinline__ uint32_t cluster_ctarank() {
@@ -201,8 +217,12 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   return v;
 }
 
-// CTA-wide barrier without the `.aligned` requirement: threads of one warp may arrive from different
-// places (single-lane producer and MMA loops).
-__device__ __forceinline__ void cta_barrier_unaligned() { asm volatile("barrier.sync 0;" ::: "memory"); }
+// CTA-wide barrier at the end of a warp-specialised kernel: each warp first reconverges (its lane 0 may
+// still be running a single-lane producer or MMA loop while lanes 1-31 are already here), then all warps
+// meet at an aligned barrier, so every thread of the CTA has arrived before any thread leaves.
+__device__ __forceinline__ void cta_teardown_barrier() {
+  __syncwarp();
+  __syncthreads();
+}
 
 }  // namespace bp

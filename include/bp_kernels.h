@@ -56,7 +56,10 @@ const char* bp_last_error(void);
  * Skinny linear  y[M, N] = x[M, K] . W[N, K]^T  (fp32 accumulation).
  *   x      bf16, row stride ldx elements (ldx >= K); rows beyond M are never read
  *   w      w_dtype = BP_DTYPE_BF16: bf16 [N, K] contiguous
- *          w_dtype = BP_DTYPE_INT8: int8 [N, K] contiguous, w_scale = bf16 [N]; y = scale[n] * sum_k x*q
+ *          w_dtype = BP_DTYPE_INT8: int8 [N, K] contiguous, w_scale = bf16 [N]; y = scale[n] * sum_k x*q.
+ *          The int8 tensor-core path sums exactly over x written in fixed point (29 bits below each
+ *          row's largest exponent: every x within 2^-22 of the row maximum is exact) and rounds
+ *          scale * sum once; a row of x holding Inf or NaN gives a NaN row of y
  *   y      y_dtype BP_DTYPE_BF16 or BP_DTYPE_F32 (the fp32 store is the un-rounded accumulator), row
  *          stride ldy elements; exactly the M x N block is written
  *   workspace, workspace_bytes  caller-owned device scratch of at least
@@ -73,7 +76,8 @@ int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const
 
 /*
  * Workspace bytes bp_skinny_mm needs for this problem on the current device (0: none needed). The
- * stream-K partial sums of the bf16 tensor-core path live there (byteprof/optim/skinny.py:125 allocates
+ * stream-K partial sums of the tensor-core paths live there (int8: also the activations' digit planes,
+ * 64 K bytes, and exact int64 partials, about 9.5 MB on 148 SMs; byteprof/optim/skinny.py:125 allocates
  * its split-K workspace per call instead).
  */
 size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype);
@@ -81,10 +85,10 @@ size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype);
 /*
  * bp_skinny_mm for callers that cannot allocate device memory (no counterpart in the reference).
  * Same arguments and results as bp_skinny_mm without the workspace: the scratch of the
- * tensor-core path (bf16 and int8 weights) is a fixed 2.6 MB array inside the library (held by every GPU that loads it, until
+ * tensor-core path (bf16 and int8 weights) is a fixed 11.5 MB array inside the library (held by every GPU that loads it, until
  * the process exits). Meant for code that runs during CUDA-graph capture in global mode, where
  * cudaMalloc is refused, and for hosts that give their plugins no allocator.
- * Limits: N <= 1,048,576 rows and a device with at most 160 SMs; larger problems return
+ * Limits: N <= 1,048,576 rows, K <= 16384 for int8 weights and a device with at most 160 SMs; larger problems return
  * BP_ERR_UNSUPPORTED. Allocates nothing. The first call on a device looks up the array's device
  * address (cudaGetSymbolAddress): make that first call before any stream capture. Each call clears the
  * array's tile counters on the stream, then launches; every call shares the one array, so calls that

@@ -87,7 +87,9 @@ def test_accept_rejects_bad_sizes():
 
 def test_workspace_query_without_a_device():
     L = _lib.lib()
-    assert L.bp_skinny_workspace_bytes(4, 2048, 2048, 2) == 0  # int8: CUDA-core path, no workspace
+    assert L.bp_skinny_workspace_bytes(4, 2048, 2048, 0) == 0  # bf16, few tiles: cluster split-K, no workspace
+    assert L.bp_skinny_workspace_bytes(4, 2048, 2048, 2) > 0   # int8: stream-K, exact int64 partials
+    assert L.bp_skinny_workspace_bytes(4, 100352, 2048, 2) <= 16 << 20  # fits the operator API's buffer
     assert L.bp_skinny_workspace_bytes(0, 2048, 2048, 0) == 0
     assert L.bp_skinny_workspace_bytes(4, 0, 2048, 0) == 0
 

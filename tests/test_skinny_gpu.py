@@ -206,15 +206,17 @@ def test_stream_k_split_tiles_are_deterministic_and_leave_the_workspace_clean(n,
     assert skinny_ref.nerr(to_np(first), to_np(x), deq_np("bf16", args)) < TOL
 
 
-def test_one_workspace_serves_alternating_shapes():
-    """The per-device workspace is shared by every shape: a small shape's stream-K partials must never
-    land on a larger shape's tile counters (which have to be zero at the start of each call)."""
+@pytest.mark.parametrize("kinds", [("bf16",), ("int8",), ("bf16", "int8")])
+def test_one_workspace_serves_alternating_shapes(kinds):
+    """The per-device workspace is shared by every shape and weight kind: one problem's stream-K partials
+    must never land on another problem's tile counters (which have to be zero at the start of each call)."""
     shapes = [(37, 256), (100352, 2048), (2048, 2048), (49152, 2048), (129, 640), (12288, 2048), (100352, 2048)]
     made = {}
-    for n, k in shapes:
-        if (n, k) not in made:
-            made[(n, k)] = make_weights("bf16", n, k, seed=n % 97)[1]
-        args = made[(n, k)]
+    for j, (n, k) in enumerate(shapes):
+        kind = kinds[j % len(kinds)]
+        if (kind, n, k) not in made:
+            made[(kind, n, k)] = make_weights(kind, n, k, seed=n % 97)[1]
+        args = made[(kind, n, k)]
         x = x_rows(9, k, seed=n % 13)
         y = S.skinny_mm(x, *args)
-        assert skinny_ref.nerr(to_np(y), to_np(x), deq_np("bf16", args)) < TOL, (n, k)
+        assert skinny_ref.nerr(to_np(y), to_np(x), deq_np(kind, args)) < TOL, (kind, n, k)
