@@ -23,7 +23,8 @@
 //  * Two partitions, chosen from (N, K) only: stream-K over (256-row tile, 128-wide k-block) units on a
 //    persistent grid of one CTA per SM, split tiles finished by the CTA that arrives last (exact int64
 //    partials in the workspace); or, for few tiles, 128-row tiles whose K range is split over the S CTAs
-//    of a cluster, the partials added through distributed shared memory.
+//    of a cluster; each CTA stores its exact sums of every column into a slot of the CTA owning that
+//    column (distributed shared memory), and after one cluster barrier the owner adds its S slots.
 //  * TMEM: two accumulators of TN int32 columns, so draining one tile overlaps the next tile's MMAs. For
 //    M = 64 the MMA writes D row i to TMEM lane 32 (i / 16) + i % 16: the four planes of activation rows
 //    4 q .. 4 q + 3 sit in lanes 0-15 of quadrant q; each epilogue warp moves a 32-column chunk of them
@@ -46,7 +47,6 @@ constexpr int kBK = 128;                   // K per unit: one 128-byte swizzle r
 constexpr int kRows = 16;                  // activation rows per launch
 constexpr int kPlanes = 4;                 // base-256 digits per activation
 constexpr int kAM = kRows * kPlanes;       // MMA M
-constexpr int kAStages = 6;
 constexpr int kABytes = kAM * kBK;         // 8 KB
 constexpr int kThreads = 224;              // weight TMA, MMA, digit TMA, 4 epilogue warps
 constexpr int kEpiWarp0 = 3;
@@ -56,10 +56,17 @@ constexpr int kNonFinite = 0x7fffffff;     // row exponent marker: the row holds
 constexpr int kMaxClusterSplit = 8;        // portable cluster size
 constexpr size_t kExpBytes = 1024;         // workspace: row exponents after the tile counters, then the digits
 
+// TN = 256: stream-K, one CTA per SM with 160 KB of weights in flight. TN = 128: cluster split-K, where a
+// CTA streams only a few units: a shorter ring, so that two CTAs fit per SM and the next call's CTAs start
+// (and request their weights) under this call's tail.
 template <int TN>
 struct I8Cfg {
-  static constexpr int kWStages = TN == 256 ? 5 : 10;  // 160 KB of weights in flight per SM
+  static constexpr int kWStages = TN == 256 ? 5 : 4;
+  static constexpr int kAStages = TN == 256 ? 6 : 2;
+  static constexpr int kMinBlocks = TN == 256 ? 1 : 2;
   static constexpr int kWBytes = TN * kBK;
+  // cluster mode: [source rank][row][column of the owner's share] exact partials (S * R <= TN + S - 1)
+  static constexpr int kRedElems = TN == 128 ? kRows * (TN + kMaxClusterSplit) : 2;
   static constexpr uint32_t kTmemCols = 2 * TN;
 };
 
@@ -81,9 +88,10 @@ struct I8Args {
 template <int TN>
 struct __align__(1024) I8Smem {
   uint8_t w[I8Cfg<TN>::kWStages][I8Cfg<TN>::kWBytes];
-  uint8_t a[kAStages][kABytes];
+  uint8_t a[I8Cfg<TN>::kAStages][kABytes];
+  long long red[I8Cfg<TN>::kRedElems];  // cluster mode: the peers' exact partials of this CTA's columns
   uint64_t full[I8Cfg<TN>::kWStages], empty[I8Cfg<TN>::kWStages];
-  uint64_t afull[kAStages], aempty[kAStages];
+  uint64_t afull[I8Cfg<TN>::kAStages], aempty[I8Cfg<TN>::kAStages];
   uint64_t tfull[2], tempty[2];
   uint64_t mma_done;
   float tscale[TN];
@@ -97,7 +105,8 @@ template <int TN>
 constexpr size_t smem_bytes() {
   return sizeof(I8Smem<TN>) + 1024;
 }
-static_assert(smem_bytes<256>() <= 232448 && smem_bytes<128>() <= 232448, "shared memory per CTA");
+static_assert(smem_bytes<256>() <= 232448, "shared memory per CTA");
+static_assert(smem_bytes<128>() <= 115712, "two CTAs per SM (228 KB, 1 KB reserved per CTA)");
 
 __device__ __forceinline__ long long unit_start(int c, long long U, int P) { return static_cast<long long>(c) * U / P; }
 __device__ __forceinline__ int unit_owner(long long u, long long U, int P) {
@@ -129,12 +138,6 @@ __device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64
 __host__ __device__ constexpr uint32_t umma_idesc_s8(int m, int n) {
   return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-__device__ __forceinline__ long long ld_shared_cluster_s64(uint32_t addr) {
-  long long v;
-  asm volatile("ld.shared::cluster.s64 %0, [%1];" : "=l"(v) : "r"(addr) : "memory");
-  return v;
 }
 
 // Exponent e with 2^e <= max|x| < 2^(e+1) from the largest |x| bit pattern of a bf16 row.
@@ -210,7 +213,9 @@ __global__ void __launch_bounds__(256) i8_digitise_kernel(const __nv_bfloat16* x
   pdl_wait_prior_grids();   // x may come from the previous kernel
   const int m = blockIdx.x;
   const __nv_bfloat16* xr = x + static_cast<long long>(m) * ldx;
+  // the first 8192 values of the row stay in registers for the digit pass (one read of x for K <= 8192)
   uint32_t amax = 0;
+  uint4 keep[4];
   for (int k0 = 8 * threadIdx.x; k0 < K; k0 += 4 * 8 * 256) {
     uint4 v[4];
 #pragma unroll
@@ -218,6 +223,9 @@ __global__ void __launch_bounds__(256) i8_digitise_kernel(const __nv_bfloat16* x
       const int k = k0 + j * 8 * 256;
       v[j] = k < K ? __ldcg(reinterpret_cast<const uint4*>(xr + k)) : make_uint4(0, 0, 0, 0);
     }
+    if (k0 == 8 * static_cast<int>(threadIdx.x))
+#pragma unroll
+      for (int j = 0; j < 4; ++j) keep[j] = v[j];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const uint32_t wv[4] = {v[j].x, v[j].y, v[j].z, v[j].w};
@@ -241,13 +249,19 @@ __global__ void __launch_bounds__(256) i8_digitise_kernel(const __nv_bfloat16* x
   const bool nonfinite = e_row == kNonFinite;  // the row's output is NaN; its digits are zero
   const int e = nonfinite ? 0 : e_row;
   uint8_t* drow = digits + static_cast<size_t>(4 * m) * K;
-  for (int k = 8 * threadIdx.x; k < K; k += 8 * 256) {
-    const uint4 v = nonfinite ? make_uint4(0, 0, 0, 0) : __ldcg(reinterpret_cast<const uint4*>(xr + k));
-    uint32_t pl[kPlanes][2];
-    digitise8(v, e, pl);
+  for (int k0 = 8 * threadIdx.x; k0 < K; k0 += 4 * 8 * 256) {
 #pragma unroll
-    for (int p = 0; p < kPlanes; ++p)
-      *reinterpret_cast<uint2*>(drow + static_cast<size_t>(p) * K + k) = make_uint2(pl[p][0], pl[p][1]);
+    for (int j = 0; j < 4; ++j) {
+      const int k = k0 + j * 8 * 256;
+      if (k >= K) break;
+      uint4 v = k0 == 8 * static_cast<int>(threadIdx.x) ? keep[j] : __ldcg(reinterpret_cast<const uint4*>(xr + k));
+      if (nonfinite) v = make_uint4(0, 0, 0, 0);
+      uint32_t pl[kPlanes][2];
+      digitise8(v, e, pl);
+#pragma unroll
+      for (int p = 0; p < kPlanes; ++p)
+        *reinterpret_cast<uint2*>(drow + static_cast<size_t>(p) * K + k) = make_uint2(pl[p][0], pl[p][1]);
+    }
   }
 }
 
@@ -255,10 +269,10 @@ __global__ void __launch_bounds__(256) i8_digitise_kernel(const __nv_bfloat16* x
 // kCluster = true: grid = tiles x S, the S CTAs of a cluster split one tile's K range and add their exact
 // partials through distributed shared memory, in rank order.
 template <int TN, bool kCluster>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, I8Cfg<TN>::kMinBlocks)
     skinny_i8_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap ta, const I8Args a) {
   using Cfg = I8Cfg<TN>;
-  constexpr int kWStages = Cfg::kWStages;
+  constexpr int kWStages = Cfg::kWStages, kAStages = Cfg::kAStages;
   extern __shared__ uint8_t smem_raw[];
   I8Smem<TN>& s =
       *reinterpret_cast<I8Smem<TN>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -421,7 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         owned = c_lo == c_hi;
         mine = a.partials + (static_cast<size_t>(c * 2 + (t == t_first ? 0 : 1)) * kRows + m) * TN;
       }
-      long long* red = reinterpret_cast<long long*>(s.w[0]) + m * TN;  // cluster mode: this CTA's partial
+      const int R = kCluster ? (TN + a.S - 1) / a.S : TN;  // cluster mode: rank c / R owns column c
+      const int slot0 = kCluster ? static_cast<int>(rank) * kRows * R : 0;  // this CTA's slot in each owner
 #pragma unroll 1
       for (int ch = 0; ch < TN / 32; ++ch) {
         uint32_t raw[32];
@@ -450,8 +465,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const int c0 = 32 * ch + cl;
           if constexpr (kCluster) {
-            *reinterpret_cast<longlong2*>(red + c0) = make_longlong2(v[0], v[1]);
-            *reinterpret_cast<longlong2*>(red + c0 + 2) = make_longlong2(v[2], v[3]);
+            // this CTA's exact partial goes to the owning CTA's slot for this rank (remote stores)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int col = c0 + i, own = col / R;
+              const uint32_t dst =
+                  mapa_shared(smem_addr(&s.red[slot0 + m * R + (col - own * R)]), static_cast<uint32_t>(own));
+              asm volatile("st.shared::cluster.u64 [%0], %1;" ::"r"(dst), "l"(v[i]) : "memory");
+            }
           } else if (owned) {
             const int n0 = t * TN + c0;
 #pragma unroll
@@ -525,29 +546,23 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if constexpr (kCluster) {
-    // CTA `rank` finishes columns [rank R, rank R + R) of the tile, adding the S exact partials.
-    cluster_sync_unaligned();  // every CTA's partial is in its shared memory
+    // CTA `rank` owns columns [rank R, rank R + R) of the tile; every CTA of the cluster has stored its
+    // exact partial sums of them into this CTA's slots. Integer sums: the order does not matter.
+    cluster_sync_unaligned();  // release / acquire: every remote store has landed
     const int S = a.S;
     const int R = (TN + S - 1) / S;
     const int r0 = rank * R;
     const int ncols = r0 >= TN ? 0 : (r0 + R <= TN ? R : TN - r0);
     const int t = static_cast<int>(cluster_id_x());
-    const uint32_t base = smem_addr(s.w[0]);
     if (!*abort) {
       for (int item = threadIdx.x; item < ncols * a.M; item += kThreads) {
-        const int mm = item / ncols, col = r0 + item - mm * ncols;
-        const uint32_t off = base + static_cast<uint32_t>((mm * TN + col) * 8);
-        long long part[kMaxClusterSplit];
-#pragma unroll
-        for (int qq = 0; qq < kMaxClusterSplit; ++qq) part[qq] = qq < S ? ld_shared_cluster_s64(mapa_shared(off, qq)) : 0;
+        const int mm = item / ncols, lc = item - mm * ncols;
         long long v = 0;
-#pragma unroll
-        for (int qq = 0; qq < kMaxClusterSplit; ++qq) v += part[qq];
-        const int n = t * TN + col;
+        for (int src = 0; src < S; ++src) v += s.red[(src * kRows + mm) * R + lc];
+        const int n = t * TN + r0 + lc;
         if (n < a.N) store_i8(a, mm, n, v, s.row_exp[mm], __bfloat162float(a.scale[n]));
       }
     }
-    cluster_sync_unaligned();  // peers have finished reading this CTA's shared memory
   }
 
   tc_fence_before_sync();
