@@ -541,7 +541,7 @@ int launch_skinny_tc(const void* x, long long ldx, const void* w, const void* w_
 // host applications that hand out all device memory from their own pre-reserved pool and give plugins
 // no allocator. For them, the scratch of the tensor-core paths lives in this fixed array instead of a
 // caller-provided workspace. It is part of the module, so every GPU that loads the library holds it
-// (11.5 MB: the int8 path's digit matrix and exact int64 partials) until the process exits. Limits: at
+// (11.6 MB: the int8 path's digit matrix and exact int64 partials) until the process exits. Limits: at
 // most kStaticMaxCtas streaming multiprocessors (B200 has 148), N <= kTcMaxTiles * 128 rows and, for
 // int8 weights, K <= 16384; larger problems are rejected with BP_ERR_UNSUPPORTED.
 constexpr int kStaticMaxCtas = 160;

@@ -85,7 +85,7 @@ size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype);
 /*
  * bp_skinny_mm for callers that cannot allocate device memory (no counterpart in the reference).
  * Same arguments and results as bp_skinny_mm without the workspace: the scratch of the
- * tensor-core path (bf16 and int8 weights) is a fixed 11.5 MB array inside the library (held by every GPU that loads it, until
+ * tensor-core path (bf16 and int8 weights) is a fixed 11.6 MB array inside the library (held by every GPU that loads it, until
  * the process exits). Meant for code that runs during CUDA-graph capture in global mode, where
  * cudaMalloc is refused, and for hosts that give their plugins no allocator.
  * Limits: N <= 1,048,576 rows, K <= 16384 for int8 weights and a device with at most 160 SMs; larger problems return
