@@ -49,7 +49,14 @@ PEAK_FALLBACK_GBS = 6650.0
 
 
 def alg_bytes(m: int, n: int, k: int, kind: str = "bf16") -> int:
-    w = 2 * n * k if kind == "bf16" else n * k + 2 * n
+    """Bytes one call must move: the weights once (int8: + the [N] scale; int4: packed codes + the
+    [K/128, N] bf16 scale and fp16 zero), the activations and the output."""
+    if kind == "bf16":
+        w = 2 * n * k
+    elif kind == "int8":
+        w = n * k + 2 * n
+    else:
+        w = n * k // 2 + 4 * n * (k // 128)
     return w + 2 * m * k + 2 * m * n
 
 
@@ -243,6 +250,30 @@ def int8_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
     return out
 
 
+def int4_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
+    """The int4 group-128 weight kind (tile-major format) on the same shapes."""
+    from byteprof_b200.optim.skinny import quantize_int4, skinny_mm
+
+    out = {}
+    for si, (n, k) in enumerate(SHAPES):
+        ring_n = max(2, math.ceil(RING_BYTES / (n * k // 2)))
+        g0 = torch.Generator(device=device).manual_seed(99 + si)
+        ring = [quantize_int4((torch.randn(n, k, generator=g0, device=device) * 0.02).to(torch.bfloat16))
+                for _ in range(ring_n)]
+        x = torch.randn(max(INT8_MS), k, generator=g0, device=device).to(torch.bfloat16)
+        y = torch.empty(max(INT8_MS), n, device=device, dtype=torch.bfloat16)
+        for m in INT8_MS:
+            g = capture(lambda: [skinny_mm(x[:m], p, s, z, out=y[:m]) for p, s, z in ring])
+            time_graph_replays(g, 2)
+            us = time_graph_replays(g, reps) * 1e3 / (reps * ring_n)
+            gbs = alg_bytes(m, n, k, "int4") / (us * 1e-6) / 1e9
+            out[f"{n}x{k}|M{m}"] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+            del g
+        del ring
+    torch.cuda.empty_cache()
+    return out
+
+
 def scan_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
     """NH=4, dk=dv=512, T positions from a zero state, h and the final state."""
     from byteprof_b200.optim.draft_core import mlstm_scan
@@ -402,6 +433,7 @@ def run_ours(args) -> int:
     extras = {}
     if not args.quick:
         extras["int8"] = int8_cells(device, peak)
+        extras["int4"] = int4_cells(device, peak)
         extras["scan"] = scan_cells(device, peak)
 
     if rank == 0:
@@ -468,9 +500,9 @@ def _cpu_baseline() -> dict:
 
 
 def run_case(args) -> int:
-    """One sweep cell alone (for ncu captures): `--case N,K,M[,bf16|int8]`; W eager warm-up calls, then K
+    """One sweep cell alone (for ncu captures): `--case N,K,M[,bf16|int8|int4]`; W eager warm-up calls, then K
     timed calls over a weight ring > 2x L2. Prints a JSON line with us per call and GB/s."""
-    from byteprof_b200.optim.skinny import skinny_mm
+    from byteprof_b200.optim.skinny import quantize_int4, skinny_mm
     from byteprof_b200.quant.int8 import quantize_rowwise_int8
 
     parts = args.case.split(",")
@@ -479,11 +511,11 @@ def run_case(args) -> int:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     g = torch.Generator(device=dev).manual_seed(0)
-    wbytes = 2 * n * k if kind == "bf16" else n * k
+    wbytes = 2 * n * k if kind == "bf16" else (n * k if kind == "int8" else n * k // 2)
     ring = []
     for _ in range(max(2, math.ceil(RING_BYTES / wbytes))):
         w = (torch.randn(n, k, generator=g, device=dev) * 0.02).to(torch.bfloat16)
-        ring.append((w,) if kind == "bf16" else quantize_rowwise_int8(w))
+        ring.append((w,) if kind == "bf16" else quantize_rowwise_int8(w) if kind == "int8" else quantize_int4(w))
     x = torch.randn(m, k, generator=g, device=dev).to(torch.bfloat16)
     y = torch.empty(m, n, device=dev, dtype=torch.bfloat16)
     for i in range(args.warmup):
@@ -518,7 +550,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the per-cell, int8, scan and CPU passes")
-    ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8]: time one sweep cell alone (ncu captures)")
+    ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8|int4]: time one sweep cell alone (ncu captures)")
     ap.add_argument("--graph", action="store_true", help="with --case: time a CUDA graph of the weight ring")
     args = ap.parse_args(argv)
     if args.warmup < 3:

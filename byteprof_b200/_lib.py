@@ -31,6 +31,8 @@ _SIGNATURES = {
                                             c_int, c_int, c_int, c_int, c_void_p]),
     "bp_gemv_int8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
                              c_void_p]),
+    "bp_skinny_mm_int4": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_int,
+                                  c_int, c_int, c_int, c_int, c_void_p]),
     "bp_mlstm_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_int, c_int, c_int, c_int, c_longlong, c_longlong, c_longlong, c_longlong,

@@ -1,0 +1,321 @@
+// Skinny linear with int4 weights in groups of 128 along K, byteprof's tile-major format, M <= 16 rows per
+// launch:  y[m, n] = sum_g scale[g, n] * sum_{k in g} (q[n, k] - zero[g, n]) * x[m, k].
+//
+// Reference: byteprof/optim/skinny.py:1-19 (the format), 46-63 (_skinny_kernel MODE 3: q - zero rounded to
+// bf16 per weight, tl.dot per group, the group scale applied to the fp32 partial) and 136-166 (skinny_mm).
+//
+// The format: packed uint8 [ceil(N / 32), K / 128, 32, 64]; inside a group of 128 along K, byte j of a row
+// holds code j in its low nibble and code j + 64 in its high nibble; the 32 rows of a row tile and one group
+// are one contiguous 2 KB block. scale [K / 128, N] bf16, zero [K / 128, N] fp16.
+//
+// B200 design (CUDA cores: a tensor-core MMA costs the same for N = 16 as for N = 128, so int4 weights
+// widened to bf16 would make the MMA issue rate, not HBM, the limit at this size):
+//  * A warp covers 8 rows of a row tile: lane l reads bytes [16 l, 16 l + 16) of the 512-byte slice of
+//    each group block, i.e. row l / 4, chunk c = l % 4 (codes 16 c .. 16 c + 15 and 64 + 16 c .. + 15):
+//    every load instruction of the warp reads 512 contiguous bytes, streamed with an L2 evict-first policy
+//    through a U-deep register pipeline. A CTA (8 warps) covers 64 rows; split-K over groups forms a
+//    thread-block cluster along y whose partials are added through distributed shared memory in rank
+//    order (deterministic, no workspace).
+//  * A byte b becomes two exact fp32 values: a byte permute gives 0x43bb0000; masking the high nibble
+//    away leaves 0x430L0000 = 128 + lo, and the high nibble moved down to bits 16-19 gives 0x430H0000 =
+//    128 + hi (the nibble must stay clear of bit 23, the exponent's lowest bit). Per group the lane
+//    accumulates P = sum (128 + q) x over its 32 codes, then adds scale * (P - (128 + zero) X) with X the
+//    sum of its 32 activations (staged once per CTA): the group term sum (q - zero) x, q - zero exact.
+//  * Activations are staged per CTA in shared memory as fp32, four floats of padding per 32 so that the
+//    four chunks a warp reads at once fall in different banks.
+//  * The K partition depends on (N, K) only, so a row's result does not depend on M.
+#include <cooperative_groups.h>
+#include <cuda_fp16.h>
+
+#include "bp_common.cuh"
+#include "skinny_internal.h"
+
+namespace cg = cooperative_groups;
+
+namespace bp {
+namespace {
+
+constexpr int kGroup = 128;
+constexpr int kTileRows = 32;
+constexpr int kWarps = 8;
+constexpr int kThreads = kWarps * 32;
+constexpr int kRowsPerCta = 8 * kWarps;
+constexpr int kStageBytes = 40 * 1024;  // activation staging budget per CTA
+constexpr int kMaxSplit = 8;            // portable cluster size
+
+struct I4Args {
+  const __nv_bfloat16* x;
+  long long ldx;
+  const uint8_t* w;
+  const __nv_bfloat16* scale;
+  const __half* zero;
+  void* y;
+  long long ldy;
+  int y_f32;
+  int N, K, G;
+  int g_chunk;  // groups per split
+  int gb;       // groups per staging batch (a multiple of the pipeline depth)
+};
+
+__device__ __forceinline__ int xs_index(int k) { return k + ((k >> 5) << 2); }
+__host__ __device__ constexpr int padded_len(int gb) { return gb * kGroup + (gb * kGroup / 32) * 4; }
+
+__device__ __forceinline__ void store_y(const I4Args& a, int m, int row, float v) {
+  if (a.y_f32)
+    static_cast<float*>(a.y)[m * a.ldy + row] = v;
+  else
+    static_cast<__nv_bfloat16*>(a.y)[m * a.ldy + row] = __float2bfloat16_rn(v);
+}
+
+template <int M, int U>
+__global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
+  extern __shared__ float xs[];  // [M][padded_len(gb)] activations, then [M][gb][4][2] chunk sums
+  __shared__ float part[kRowsPerCta * M];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kRowsPerCta + warp * 8 + (lane >> 2);
+  const int c = lane & 3;
+  const bool rv = row < a.N;
+  const int g0 = blockIdx.y * a.g_chunk;
+  const int g1 = min(a.G, g0 + a.g_chunk);
+  const int plen = padded_len(a.gb);
+  float* xsum = xs + M * plen;
+
+  // this lane's 16 bytes of group g: ((t G + g) 32 + r) 64 + 16 c  (padding rows of the format are zero)
+  const int t = row / kTileRows, rr = row % kTileRows;
+  const uint8_t* wl = a.w + (static_cast<long long>(t) * a.G * kTileRows + rr) * 64 + 16 * c;
+  const long long gstride = static_cast<long long>(kTileRows) * 64;
+  const uint64_t pol = l2_evict_first_policy();
+
+  float acc[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+
+  uint4 buf[U];
+  float sc[U], zc[U];
+  auto fetch = [&](int g, int slot_u) {
+    // (slot_u is a compile-time index after unrolling)
+    if (g < g1) {
+      buf[slot_u] = ldg_stream16(wl + g * gstride, pol);
+      sc[slot_u] = rv ? __bfloat162float(a.scale[static_cast<long long>(g) * a.N + row]) : 0.0f;
+      zc[slot_u] = rv ? __half2float(a.zero[static_cast<long long>(g) * a.N + row]) : 0.0f;
+    } else {
+      buf[slot_u] = make_uint4(0, 0, 0, 0);
+      sc[slot_u] = zc[slot_u] = 0.0f;
+    }
+  };
+#pragma unroll
+  for (int u = 0; u < U - 1; ++u) fetch(g0 + u, u);
+
+  int bb = g0;  // first group of the staged batch
+  for (int gg = g0; gg < g1; gg += U) {
+    if ((gg - g0) % a.gb == 0) {
+      // ---- stage activations of groups [gg, gg + gn) as fp32, then the per-chunk sums ----
+      bb = gg;
+      const int gn = min(a.gb, g1 - gg);
+      __syncthreads();  // the previous batch is consumed
+      const int vecs = M * gn * (kGroup / 8);
+      for (int i = threadIdx.x; i < vecs; i += kThreads) {
+        const int m = i / (gn * (kGroup / 8)), kv = (i - m * gn * (kGroup / 8)) * 8;
+        const uint4 v = ldg16(a.x + m * a.ldx + static_cast<long long>(gg) * kGroup + kv);
+        float* d = xs + m * plen + xs_index(kv);
+        *reinterpret_cast<float4*>(d) = make_float4(bf16lo(v.x), bf16hi(v.x), bf16lo(v.y), bf16hi(v.y));
+        *reinterpret_cast<float4*>(d + 4) = make_float4(bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w));
+      }
+      __syncthreads();
+      for (int i = threadIdx.x; i < M * gn * 8; i += kThreads) {
+        const int m = i / (gn * 8), rest = i - m * gn * 8, gl = rest >> 3, cc = (rest >> 1) & 3, h = rest & 1;
+        const float* p = xs + m * plen + xs_index(gl * kGroup + 64 * h + 16 * cc);
+        float s = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) s += p[j];
+        xsum[((m * a.gb + gl) * 4 + cc) * 2 + h] = s;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      fetch(gg + u + U - 1, (u + U - 1) % U);  // refill the slot consumed one step ago
+      const int g = gg + u;
+      if (g < g1) {
+        const int gl = g - bb;
+        const uint32_t words[4] = {buf[u].x, buf[u].y, buf[u].z, buf[u].w};
+        float plo[M], phi[M];
+#pragma unroll
+        for (int m = 0; m < M; ++m) plo[m] = phi[m] = 0.0f;
+#pragma unroll
+        for (int jq = 0; jq < 4; ++jq) {
+          float flo[4], fhi[4];
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const uint32_t r = __byte_perm(words[jq], 0x43u, 0x4055u | (static_cast<uint32_t>(b) << 8));
+            flo[b] = __uint_as_float(r & 0xFF0FFFFFu);                            // 128 + low nibble
+            fhi[b] = __uint_as_float(((r >> 4) & 0x000F0000u) | 0x43000000u);  // 128 + high nibble
+          }
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const float4 xl = *reinterpret_cast<const float4*>(xs + m * plen + xs_index(gl * kGroup + 16 * c + 4 * jq));
+            const float4 xh =
+                *reinterpret_cast<const float4*>(xs + m * plen + xs_index(gl * kGroup + 64 + 16 * c + 4 * jq));
+            plo[m] = fmaf(flo[0], xl.x, plo[m]);
+            plo[m] = fmaf(flo[1], xl.y, plo[m]);
+            plo[m] = fmaf(flo[2], xl.z, plo[m]);
+            plo[m] = fmaf(flo[3], xl.w, plo[m]);
+            phi[m] = fmaf(fhi[0], xh.x, phi[m]);
+            phi[m] = fmaf(fhi[1], xh.y, phi[m]);
+            phi[m] = fmaf(fhi[2], xh.z, phi[m]);
+            phi[m] = fmaf(fhi[3], xh.w, phi[m]);
+          }
+        }
+        const float cz = 128.0f + zc[u];
+#pragma unroll
+        for (int m = 0; m < M; ++m) {
+          const float* sm = xsum + ((m * a.gb + gl) * 4 + c) * 2;
+          const float grp = (plo[m] + phi[m]) - cz * (sm[0] + sm[1]);
+          acc[m] = fmaf(sc[u], grp, acc[m]);
+        }
+      }
+    }
+  }
+
+  // the row's 4 chunk lanes -> every one of them holds the row sum
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], 1);
+    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], 2);
+  }
+
+  if (gridDim.y == 1) {
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      if ((m & 3) == c && rv) store_y(a, m, row, acc[m]);
+    return;
+  }
+  const int lr = warp * 8 + (lane >> 2);
+#pragma unroll
+  for (int m = 0; m < M; ++m)
+    if ((m & 3) == c) part[lr * M + m] = acc[m];
+  cg::cluster_group cluster = cg::this_cluster();
+  cluster.sync();
+  const int S = gridDim.y;
+  const int rank = static_cast<int>(cluster.block_rank());
+  for (int e = rank + S * threadIdx.x; e < kRowsPerCta * M; e += S * kThreads) {
+    const int r = blockIdx.x * kRowsPerCta + e / M, m = e % M;
+    if (r >= a.N) continue;
+    float s = 0.0f;
+    for (int q = 0; q < S; ++q) s += cluster.map_shared_rank(part, q)[e];
+    store_y(a, m, r, s);
+  }
+  cluster.sync();  // keep this CTA's partials alive until every peer has read them
+}
+
+template <int M>
+constexpr int pipeline_depth() {
+  return M <= 4 ? 4 : (M <= 8 ? 3 : 2);
+}
+
+template <int M>
+int launch_i4(I4Args a, cudaStream_t st) {
+  constexpr int U = pipeline_depth<M>();
+  const int row_ctas = (a.N + kRowsPerCta - 1) / kRowsPerCta;
+  // split from (N, K) only: about two CTAs per SM in total
+  const int target = 2 * tc_sm_count();
+  int S = (target + row_ctas - 1) / row_ctas;
+  S = S < 1 ? 1 : (S > kMaxSplit ? kMaxSplit : S);
+  if (S > a.G) S = a.G;
+  a.g_chunk = (a.G + S - 1) / S;
+  S = (a.G + a.g_chunk - 1) / a.g_chunk;
+  // staging batch: as many groups as fit the budget, a multiple of U
+  const int per_group = M * (padded_len(1) + 8) * static_cast<int>(sizeof(float));
+  int gb = kStageBytes / per_group;
+  gb = gb < U ? U : gb - gb % U;
+  const int chunk_u = (a.g_chunk + U - 1) / U * U;
+  if (gb > chunk_u) gb = chunk_u;
+  a.gb = gb;
+  const size_t smem = static_cast<size_t>(M) * (padded_len(gb) + gb * 8) * sizeof(float);
+
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(row_ctas, S, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  cfg.numAttrs = 0;
+  if (S > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = S;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_i4_kernel<M, U>, a);
+  if (e != cudaSuccess)
+    return fail(BP_ERR_CUDA, "int4 skinny launch (M=%d N=%d K=%d split=%d): %s", M, a.N, a.K, S, cudaGetErrorString(e));
+  return BP_OK;
+}
+
+int dispatch_i4(const I4Args& a, int m, cudaStream_t st) {
+  switch (m) {
+#define BP_CASE(MM) \
+  case MM: return launch_i4<MM>(a, st);
+    BP_CASE(1) BP_CASE(2) BP_CASE(3) BP_CASE(4) BP_CASE(5) BP_CASE(6) BP_CASE(7) BP_CASE(8)
+    BP_CASE(9) BP_CASE(10) BP_CASE(11) BP_CASE(12) BP_CASE(13) BP_CASE(14) BP_CASE(15) BP_CASE(16)
+#undef BP_CASE
+    default: return fail(BP_ERR_INVALID_ARGUMENT, "rows per launch must be 1..16, got %d", m);
+  }
+}
+
+}  // namespace
+}  // namespace bp
+
+extern "C" int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_packed, const void* scale,
+                                 const void* zero, void* y, long long ldy, int y_dtype, int M, int N, int K,
+                                 int tile_rows, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (M < 0 || N < 0 || K < 0) return fail(BP_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d K=%d)", M, N, K);
+  if (y_dtype != BP_DTYPE_BF16 && y_dtype != BP_DTYPE_F32)
+    return fail(BP_ERR_INVALID_ARGUMENT, "output dtype %d is not bf16 or fp32", y_dtype);
+  if (K % kGroup != 0) return fail(BP_ERR_INVALID_ARGUMENT, "int4 needs K %% 128 == 0 (K=%d)", K);
+  if (tile_rows != kTileRows)
+    return fail(BP_ERR_UNSUPPORTED, "int4 weights packed with %d rows per tile; the kernel reads 32", tile_rows);
+  if (M == 0 || N == 0) return BP_OK;
+  if (y == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "y is NULL");
+  if (ldy < N) return fail(BP_ERR_INVALID_ARGUMENT, "ldy (%lld) < N (%d)", ldy, N);
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t ysz = y_dtype == BP_DTYPE_F32 ? 4 : 2;
+  if (K == 0) {
+    cudaError_t e = cudaMemset2DAsync(y, static_cast<size_t>(ldy) * ysz, 0, static_cast<size_t>(N) * ysz, M, s);
+    if (e != cudaSuccess) return fail(BP_ERR_CUDA, "zero fill for K = 0: %s", cudaGetErrorString(e));
+    return BP_OK;
+  }
+  if (x == nullptr || w_packed == nullptr || scale == nullptr || zero == nullptr)
+    return fail(BP_ERR_INVALID_ARGUMENT, "x, w, scale or zero is NULL");
+  if (ldx < K) return fail(BP_ERR_INVALID_ARGUMENT, "ldx (%lld) < K (%d)", ldx, K);
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) != 0 || (reinterpret_cast<uintptr_t>(w_packed) & 15u) != 0 || ldx % 8 != 0)
+    return fail(BP_ERR_MISALIGNED, "int4: x and w must be 16-byte aligned and ldx a multiple of 8");
+
+  I4Args a;
+  a.ldx = ldx;
+  a.w = w_packed;
+  a.scale = static_cast<const __nv_bfloat16*>(scale);
+  a.zero = static_cast<const __half*>(zero);
+  a.ldy = ldy;
+  a.y_f32 = y_dtype == BP_DTYPE_F32;
+  a.N = N;
+  a.K = K;
+  a.G = K / kGroup;
+  a.g_chunk = a.G;
+  a.gb = 1;
+  for (int r0 = 0; r0 < M; r0 += 16) {
+    const int m = M - r0 < 16 ? M - r0 : 16;
+    a.x = static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r0) * ldx;
+    a.y = static_cast<char*>(y) + static_cast<long long>(r0) * ldy * static_cast<long long>(ysz);
+    st = dispatch_i4(a, m, s);
+    if (st != BP_OK) return st;
+  }
+  return BP_OK;
+}

@@ -3,7 +3,7 @@
 Same constructor, attributes and forward behaviour as byteprof/optim/skinny_linear.py:20-69:
   * schemes bf16_wo (keeps the bf16 weight Parameter) and int8_wo (per-row int8 `q` and bf16 `scale`
     buffers plus an empty `weight` Parameter that only carries the dtype, which Bolmo's cache setup
-    reads); int4_wo raises NotImplementedError until the int4 format is built;
+    reads) and int4_wo (the packed group-128 codes `q` with `scale` and `zero` buffers);
   * bf16 inputs of 1..MAX_M rows run the kernel, then the bias is added as a separate op;
   * empty inputs return an empty tensor;
   * larger inputs (prefill) and non-bf16 activations (the fp32 exactness runs) use the weights
@@ -26,8 +26,6 @@ class SkinnyLinear(nn.Module):
         super().__init__()
         if scheme not in ("bf16_wo", "int8_wo", "int4_wo"):
             raise ValueError(f"unknown scheme {scheme!r}")
-        if scheme == "int4_wo":
-            raise NotImplementedError("int4_wo (the int4 tile-major format) is not built in byteprof_b200 yet")
         self.scheme = scheme
         self.in_features, self.out_features = lin.in_features, lin.out_features
         self.bias = lin.bias
@@ -37,13 +35,19 @@ class SkinnyLinear(nn.Module):
             self.scale = self.zero = None
             return
         self.weight = nn.Parameter(torch.empty(0, dtype=w.dtype, device=w.device), requires_grad=False)
-        q, scale = quantize_rowwise_int8(w)
-        self.register_buffer("q", q)
-        self.register_buffer("scale", scale)
-        self.zero = None
+        if scheme == "int8_wo":
+            q, scale = quantize_rowwise_int8(w)
+            self.register_buffer("q", q)
+            self.register_buffer("scale", scale)
+            self.zero = None
+        else:
+            packed, scale, zero = skinny.quantize_int4(w)
+            self.register_buffer("q", packed)
+            self.register_buffer("scale", scale)
+            self.register_buffer("zero", zero)
 
     def _kind(self) -> str:
-        return {"bf16_wo": "bf16", "int8_wo": "int8"}[self.scheme]
+        return {"bf16_wo": "bf16", "int8_wo": "int8", "int4_wo": "int4"}[self.scheme]
 
     def dequantized(self, dtype: torch.dtype) -> torch.Tensor:
         if self.scheme == "bf16_wo":

@@ -11,6 +11,7 @@
  *   bp_skinny_mm        byteprof/optim/skinny.py:136-166   skinny_mm (bf16 and int8 weight kinds)
  *                       byteprof/optim/skinny.py:111-129   _launch (+ _split_reduce, skinny.py:83-90)
  *   bp_gemv_int8        byteprof/quant/triton_int8.py:40-47 gemv_int8
+ *   bp_skinny_mm_int4   byteprof/optim/skinny.py:46-63, 136-166 skinny_mm (int4 g128 weight kind)
  *   bp_mlstm_scan       byteprof/optim/mlstm_multistep.py:33-85  multistep_fw_kernel
  *                       byteprof/optim/mlstm_multistep.py:89-133 lazy_commit_kernel
  *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
@@ -104,6 +105,21 @@ int bp_skinny_mm_static_scratch(const void* x, long long ldx, const void* w, int
  */
 int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,
                  void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Skinny linear with int4 weights in groups of 128 along K, in byteprof's tile-major format:
+ *   y[m, n] = sum_g scale[g, n] * sum_{k in group g} (q[n, k] - zero[g, n]) * x[m, k].
+ *   w_packed  uint8 [ceil(N / tile_rows), K / 128, tile_rows, 64]: inside a group, byte j of a row holds
+ *             code j (low nibble) and code j + 64 (high nibble); padding rows are zero
+ *   scale     bf16 [K / 128, N];  zero  fp16 [K / 128, N]
+ *   x         bf16, 16-byte aligned, ldx a multiple of 8; y as in bp_skinny_mm (bf16 or fp32)
+ * K must be a multiple of 128 and tile_rows 32 (the format's default; other values return
+ * BP_ERR_UNSUPPORTED). Any M (16 rows per launch). No workspace: split-K partials meet in
+ * distributed shared memory. Replaces skinny_mm with uint8 weights / _skinny_kernel MODE 3
+ * (byteprof/optim/skinny.py:1-19, 46-63, 136-166).
+ */
+int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_packed, const void* scale, const void* zero,
+                      void* y, long long ldy, int y_dtype, int M, int N, int K, int tile_rows, void* stream);
 
 /*
  * Fused mLSTM recurrence over T positions (exponential gating with the max stabiliser m), one head

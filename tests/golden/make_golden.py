@@ -8,6 +8,10 @@ What it runs (paths inside the byteprof project):
   * byteprof/quant/triton_int8.py:50-55  quantize_rowwise_int8 on seeded bf16 weights (torch, CPU)
   * byteprof/optim/skinny.py:209-217     dequantize, and the fp32 dequantize-then-matmul reference of
                                          tests/test_skinny.py:38 (torch, CPU)
+  * byteprof/optim/skinny.py:172-206     quantize_int4, pack_int4 (R = 32 and 16), unpack_int4 and the
+                                         int4 dequantizer (torch, CPU). The Triton int4 kernel itself is not
+                                         run: under the CPU interpreter its bit-cast of the nibbles into fp32
+                                         gives wrong values, so kernel parity rests on the fp32 reference.
   * byteprof/quant/triton_int8.py:15-47  the Triton int8 GEMV, under the Triton CPU interpreter
   * byteprof/optim/mlstm_multistep.py    multistep_fw_kernel and lazy_commit_kernel with fp32 inputs
                                          (the interpreter has no bf16), and accept_kernel, under
@@ -55,6 +59,21 @@ def main() -> None:
     q, s = Q.quantize_rowwise_int8(w)
     g["q8_w"], g["q8_q"], g["q8_scale"] = bits(w), q.numpy().copy(), bits(s)
     g["q8_deq"] = S.dequantize("int8", q, s).numpy().copy()
+
+    # ---- int4 group quantizer, packing, dequantizer -------------------------------------------------
+    gen = torch.Generator().manual_seed(4444)
+    w4 = (torch.randn(40, 384, generator=gen) * 0.03).to(torch.bfloat16)
+    w4[5] = 0  # an all-zero row: scale clamped at 1e-6, zero -0
+    w4[9, 130:136] = torch.tensor([0.9, -0.8, 0.7, 1e-4, -1e-4, 0.0], dtype=torch.bfloat16)  # a wide group
+    g["q4_w"] = bits(w4)
+    for r in (32, 16):
+        packed, scale4, zero4 = S.quantize_int4(w4, tile_rows=r)
+        g[f"q4_r{r}_packed"], g[f"q4_r{r}_scale"], g[f"q4_r{r}_zero"] = packed.numpy().copy(), bits(scale4), bits(zero4)
+        g[f"q4_r{r}_codes"] = S.unpack_int4(packed, 40).numpy().copy()
+        g[f"q4_r{r}_deq"] = S.dequantize("int4", packed, scale4, zero4).numpy().copy()
+    x4 = torch.randn(5, 384, generator=gen).to(torch.bfloat16)
+    g["q4lin_x"] = bits(x4)
+    g["q4lin_y"] = (x4.float() @ S.dequantize("int4", *S.quantize_int4(w4)).T).numpy().copy()
 
     # ---- fp32 dequantize-then-matmul reference (the reference tests' oracle) -------------------------
     for kind, (n, k), m in (("bf16", (70, 384), 3), ("int8", (37, 256), 5), ("bf16", (129, 640), 17)):

@@ -16,13 +16,18 @@ def to_np(t: torch.Tensor) -> np.ndarray:
 
 def make_weights(kind: str, n: int, k: int, seed: int = 0, device: str = "cuda", std: float = 0.02):
     """W ~ N(0, std) in bf16 from a seeded generator (the reference tests' `make`,
-    tests/test_skinny.py:23-31); int8 adds the per-row quantization. Returns (w_bf16, args)."""
+    tests/test_skinny.py:23-31); int8 adds the per-row quantization, int4 the group-128 quantization
+    in the tile-major format. Returns (w_bf16, args)."""
     from byteprof_b200.quant.int8 import quantize_rowwise_int8
+
+    from byteprof_b200.optim.skinny import quantize_int4
 
     g = torch.Generator(device=device).manual_seed(seed)
     w = (torch.randn(n, k, generator=g, device=device) * std).to(torch.bfloat16)
     if kind == "bf16":
         return w, (w,)
+    if kind == "int4":
+        return w, quantize_int4(w)
     q, s = quantize_rowwise_int8(w)
     return w, (q, s)
 
@@ -32,6 +37,8 @@ def deq_np(kind: str, args) -> np.ndarray:
 
     if kind == "bf16":
         return skinny_ref.dequantize("bf16", to_np(args[0]))
+    if kind == "int4":
+        return skinny_ref.dequantize("int4", args[0].cpu().numpy(), to_np(args[1]), args[2].cpu().numpy())
     return skinny_ref.dequantize("int8", to_np(args[0]), to_np(args[1]))
 
 

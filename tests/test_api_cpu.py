@@ -1,6 +1,7 @@
 """Host-side logic of the operator API, on the CPU: argument validation (same errors as the
-reference), the int8 quantizer against the oracle, the module selection rules, the module swap, and
-that CPU tensors are refused (there is no CPU path)."""
+reference), the int8 and int4 weight preparation against the oracle (and the reference's own format
+tests, tests/test_skinny.py:46-68), the module selection rules, the module swap, and that CPU tensors
+are refused (there is no CPU path)."""
 
 import numpy as np
 import pytest
@@ -26,6 +27,42 @@ def test_quantizer_matches_oracle_bit_for_bit():
     assert np.array_equal(q.numpy(), qo) and np.array_equal(to_np(s), so)
 
 
+@pytest.mark.parametrize("r", [32, 16])
+def test_int4_preparation_matches_oracle_bit_for_bit(r):
+    g = torch.Generator().manual_seed(11)
+    w = (torch.randn(70, 384, generator=g) * 0.03).to(torch.bfloat16)
+    w[3] = 0
+    packed, scale, zero = skinny.quantize_int4(w, tile_rows=r)
+    po, so, zo = skinny_ref.quantize_int4(to_np(w), tile_rows=r)
+    assert packed.dtype == torch.uint8 and scale.dtype == torch.bfloat16 and zero.dtype == torch.float16
+    assert np.array_equal(packed.numpy(), po) and np.array_equal(to_np(scale), so)
+    assert np.array_equal(zero.numpy(), zo)
+    assert np.array_equal(skinny.unpack_int4(packed, 70).numpy(), skinny_ref.unpack_int4(po, 70))
+    assert np.array_equal(to_np(skinny.dequantize("int4", packed, scale, zero)), skinny_ref.dequantize("int4", po, so, zo))
+
+
+@pytest.mark.parametrize("n,rows", [(32, 32), (37, 32), (5, 16), (64, 16)])
+def test_int4_pack_round_trip(n, rows):
+    q = torch.randint(0, 16, (n, 384), dtype=torch.uint8)
+    packed = skinny.pack_int4(q, rows)
+    assert packed.shape == (-(-n // rows), 3, rows, 64) and packed.dtype == torch.uint8
+    assert torch.equal(skinny.unpack_int4(packed, n), q)
+    # byte j of a group holds code j (low nibble) and code j + 64 (high nibble)
+    assert int(packed[0, 1, 0, 5]) == int(q[0, 128 + 5]) | (int(q[0, 128 + 64 + 5]) << 4)
+
+
+def test_int4_quantization_error_is_at_most_half_a_step():
+    w = (torch.randn(24, 256) * 0.05).to(torch.bfloat16)
+    packed, scale, zero = skinny.quantize_int4(w)
+    assert scale.shape == zero.shape == (2, 24)
+    deq = skinny.dequantize("int4", packed, scale, zero)
+    step = scale.float().t().repeat_interleave(128, dim=1)
+    assert ((deq - w.float()).abs() <= 0.55 * step + 1e-3).all()
+    assert skinny.unpack_int4(packed, 24).max() <= 15
+    with pytest.raises(ValueError):
+        skinny.quantize_int4(torch.zeros(4, 100, dtype=torch.bfloat16))
+
+
 def test_rowwise_quantization_error_bound():
     w = torch.randn(16, 256, dtype=torch.bfloat16)
     q, s = quantize_rowwise_int8(w)
@@ -44,8 +81,13 @@ def test_skinny_mm_validation_matches_the_reference_errors():
         skinny.skinny_mm(torch.zeros(2, 128, dtype=torch.bfloat16), torch.zeros(8, 128, dtype=torch.int8))  # no scale
     with pytest.raises(ValueError):
         skinny.skinny_mm(torch.zeros(2, 128, dtype=torch.bfloat16), torch.zeros(8, 128, dtype=torch.float16))
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError):  # int4 without scale / zero
         skinny.skinny_mm(torch.zeros(2, 128, dtype=torch.bfloat16), torch.zeros(1, 1, 32, 64, dtype=torch.uint8))
+    packed, sc, z = skinny.quantize_int4(torch.zeros(8, 256, dtype=torch.bfloat16))
+    with pytest.raises(ValueError):  # K does not match the packed groups
+        skinny.skinny_mm(torch.zeros(2, 128, dtype=torch.bfloat16), packed, sc, z)
+    with pytest.raises(ValueError):  # scale with the wrong group count
+        skinny.skinny_mm(torch.zeros(2, 256, dtype=torch.bfloat16), packed, sc[:1], z[:1])
 
 
 def test_skinny_mm_empty_shapes_need_no_device():
@@ -131,14 +173,23 @@ class _Toy(nn.Module):
 
 
 @pytest.mark.parametrize("kernel,scheme,cls", [("skinny", "bf16_wo", SkinnyLinear), ("skinny", "int8_wo", SkinnyLinear),
-                                               ("default", "int8_wo", Int8Linear)])
+                                               ("skinny", "int4_wo", SkinnyLinear), ("default", "int8_wo", Int8Linear)])
 def test_apply_quantization_swaps_the_selected_linears(kernel, scheme, cls):
-    m = _Toy().to(torch.bfloat16)
+    m = _Toy(128 if scheme == "int4_wo" else 64).to(torch.bfloat16)  # int4 groups need K % 128 == 0
     stats = apply_quantization(m, "blocks", scheme, 128, None, None, kernel)
     assert stats["n_linears"] == 14
     assert ("kernel" in stats) == (kernel != "default")
     assert sum(isinstance(x, cls) for x in m.modules()) == 14
     assert isinstance(m.lm_head, nn.Linear)
+
+
+def test_int4_skinny_linear_holds_the_packed_format():
+    lin = nn.Linear(256, 40, bias=False).to(torch.bfloat16)
+    sl = SkinnyLinear(lin, "int4_wo")
+    packed, scale, zero = skinny.quantize_int4(lin.weight.data)
+    assert torch.equal(sl.q, packed) and torch.equal(sl.scale, scale) and torch.equal(sl.zero, zero)
+    assert sl.weight.numel() == 0 and sl.weight.dtype == torch.bfloat16
+    assert torch.equal(sl.dequantized(torch.float32), skinny.dequantize("int4", packed, scale, zero))
 
 
 def test_default_kernel_rejects_skinny_only_and_torchao_schemes():

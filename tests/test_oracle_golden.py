@@ -42,6 +42,25 @@ def test_fp32_reference_matmul(key):
     assert skinny_ref.rel_normwise(y, G[key + "_y"]) < 1e-6
 
 
+@pytest.mark.parametrize("r", [32, 16])
+def test_int4_quantizer_packing_and_dequantizer_are_bit_exact(r):
+    w = bf16_bits_to_f32(G["q4_w"])
+    packed, scale, zero = skinny_ref.quantize_int4(w, tile_rows=r)
+    assert np.array_equal(packed, G[f"q4_r{r}_packed"])
+    assert np.array_equal(f32_to_bf16_bits(scale), G[f"q4_r{r}_scale"])
+    assert np.array_equal(zero.view(np.uint16), G[f"q4_r{r}_zero"])
+    assert np.array_equal(skinny_ref.unpack_int4(packed, w.shape[0]), G[f"q4_r{r}_codes"])
+    assert np.array_equal(skinny_ref.pack_int4(G[f"q4_r{r}_codes"], r), packed)
+    assert np.array_equal(skinny_ref.dequantize("int4", packed, scale, zero), G[f"q4_r{r}_deq"])
+
+
+def test_int4_fp32_reference_matmul():
+    w = bf16_bits_to_f32(G["q4_w"])
+    wd = skinny_ref.dequantize("int4", *skinny_ref.quantize_int4(w))
+    y = skinny_ref.linear_ref(bf16_bits_to_f32(G["q4lin_x"]), wd, exact=True)
+    assert skinny_ref.rel_normwise(y, G["q4lin_y"]) < 1e-6
+
+
 @pytest.mark.parametrize("key", sorted(k[:-2] for k in G.files if k.startswith("gemv_") and k.endswith("_y")))
 def test_int8_gemv_golden(key):
     x = bf16_bits_to_f32(G[key + "_x"])
