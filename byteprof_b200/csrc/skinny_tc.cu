@@ -14,12 +14,13 @@
 //  * TMA streams 128-row weight tiles (16 KB per stage, 128-byte swizzle, L2 evict-first) and the
 //    matching activation tile (rows beyond M zero-filled by TMA) into a shared-memory ring.
 //  * Two work partitions, chosen from (N, K) only (never from M):
-//     - stream-K (many tiles): a persistent grid of one CTA per SM; CTA c owns the contiguous unit range
+//     - stream-K (many tiles): a persistent grid of two CTAs per SM; CTA c owns the contiguous unit range
 //       [c U / P, (c + 1) U / P) of the U = tiles x k-blocks units, so every SM streams the same number
 //       of bytes. A tile split between CTAs is finished by the CTA that arrives last (atomic counter per
 //       tile, reset by that CTA), adding the partials in CTA order: deterministic, and no CTA waits.
-//     - cluster split-K (few tiles): the S CTAs of a thread-block cluster split one tile's K range and
-//       add their partials through distributed shared memory, in rank order.
+//     - cluster split-K (few tiles): the S CTAs of a thread-block cluster split one tile's K range; each
+//       stores its partial of every row into a slot of the CTA owning that row (distributed shared
+//       memory), and after one cluster barrier the owner adds the slots in rank order.
 //  * Warp roles: warp 0 issues TMA, warp 1 issues tcgen05.mma (and owns the TMEM allocation), the
 //    epilogue warps drain TMEM (two accumulator buffers, so draining overlaps the next tile's MMAs).
 //  * Programmatic dependent launch: every CTA lets the next kernel in the stream launch at once, and
@@ -39,7 +40,7 @@ constexpr int kBM = 128;  // weight rows per tile (MMA M)
 constexpr int kNP = 16;   // activation rows per launch (MMA N)
 constexpr int kEpiThreads = 128;
 constexpr int kBK = 64;   // K elements per stage (one 128-byte swizzle row)
-constexpr int kStages = 6;
+constexpr int kMaxClusterSplit = 8;  // portable cluster size
 constexpr int kABytes = kBM * kBK * 2;
 constexpr int kBBytes = kNP * kBK * 2;
 constexpr int kThreads = 192;  // TMA, MMA, 4 epilogue warps
@@ -60,11 +61,22 @@ struct TcArgs {
   float* partials;  // stream-K: [P][2][kNP][kBM]
 };
 
+// Stream-K: a 6-stage ring. Cluster split-K: 5 stages and the slots where the cluster's CTAs store their
+// partials of this CTA's rows ([source rank][activation row][row of this CTA's share]), so that two CTAs
+// still fit per SM.
+template <bool kCluster>
+struct TcCfg {
+  static constexpr int kStages = kCluster ? 5 : 6;
+  static constexpr int kRedElems = kCluster ? kNP * (kBM + kMaxClusterSplit) : 4;
+};
+
+template <bool kCluster>
 struct __align__(1024) TcSmem {
-  uint8_t a[kStages][kABytes];
-  uint8_t b[kStages][kBBytes];
-  uint64_t full[kStages];
-  uint64_t empty[kStages];
+  uint8_t a[TcCfg<kCluster>::kStages][kABytes];
+  uint8_t b[TcCfg<kCluster>::kStages][kBBytes];
+  float red[TcCfg<kCluster>::kRedElems];
+  uint64_t full[TcCfg<kCluster>::kStages];
+  uint64_t empty[TcCfg<kCluster>::kStages];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t mma_done;
@@ -73,10 +85,13 @@ struct __align__(1024) TcSmem {
   int last_flag;
 };
 
-constexpr size_t kSmemBytes = sizeof(TcSmem) + 1024;  // + slack to align the base to 1024 bytes
+template <bool kCluster>
+constexpr size_t smem_bytes() {
+  return sizeof(TcSmem<kCluster>) + 1024;  // + slack to align the base to 1024 bytes
+}
 // Two CTAs per SM (so that the next kernel's CTAs start under this one's tail): 228 KB per SM, 1 KB of
 // it reserved per CTA.
-static_assert(kSmemBytes <= 115712, "two CTAs per SM must fit");
+static_assert(smem_bytes<false>() <= 115712 && smem_bytes<true>() <= 115712, "two CTAs per SM must fit");
 
 __host__ __device__ __forceinline__ long long unit_start(int c, long long U, int P) {
   return static_cast<long long>(c) * U / P;
@@ -117,8 +132,10 @@ __device__ __forceinline__ void store_rows(const TcArgs& a, int row, const float
 template <bool kCluster>
 __global__ void __launch_bounds__(kThreads, 2)
     skinny_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const TcArgs a) {
+  constexpr int kStages = TcCfg<kCluster>::kStages;
   extern __shared__ uint8_t smem_raw[];
-  TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  TcSmem<kCluster>& s =
+      *reinterpret_cast<TcSmem<kCluster>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
   const long long U = a.units;
@@ -245,12 +262,15 @@ __global__ void __launch_bounds__(kThreads, 2)
       tc_fence_before_sync();
       mbar_arrive(&s.tempty[buf]);
       if constexpr (kCluster) {
-        // one tile per CTA: the partial goes to this CTA's shared memory (stage 0 is free: every MMA that
-        // read it has finished) for the cluster reduction below
-        float* red = reinterpret_cast<float*>(s.a[0]);
+        // one tile per CTA: row r's partial goes to the slot for this rank in the CTA that owns row r
+        const int R = (kBM + a.S - 1) / a.S;
+        const int own = r / R;
+        const uint32_t dst = mapa_shared(smem_addr(&s.red[rank * kNP * R + (r - own * R)]), static_cast<uint32_t>(own));
 #pragma unroll
         for (int m = 0; m < kNP; ++m)
-          if (m < a.M) red[m * kBM + r] = acc[m];
+          if (m < a.M)
+            asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst + static_cast<uint32_t>(m * R * 4)), "f"(acc[m])
+                         : "memory");
         continue;
       }
       const int row = t * kBM + r;
@@ -314,32 +334,24 @@ __global__ void __launch_bounds__(kThreads, 2)
   }
 
   if constexpr (kCluster) {
-    // Split-K through distributed shared memory: CTA `rank` finishes rows [rank R, rank R + R) of the
-    // tile, adding the S partials in rank order (deterministic), then stores them.
-    cluster_sync_unaligned();  // every CTA's partial is in its shared memory
+    // Split-K through distributed shared memory: every CTA of the cluster has stored its partials of
+    // rows [rank R, rank R + R) into this CTA's slots; one barrier, then this CTA adds them in rank order
+    // (deterministic) and stores the rows. Nothing reads another CTA's memory after the barrier.
+    cluster_sync_unaligned();  // release / acquire: every remote store has landed
     const int S = a.S;
     const int R = (kBM + S - 1) / S;
     const int r0 = rank * R;
     const int nrows = r0 >= kBM ? 0 : (r0 + R <= kBM ? R : kBM - r0);
     const int t = static_cast<int>(cluster_id_x());
-    const uint32_t red = smem_addr(s.a[0]);
     if (!*abort) {
       for (int item = threadIdx.x; item < nrows * a.M; item += kThreads) {
         const int m = item / nrows, lr = item - m * nrows;
-        const int rr = r0 + lr;
-        const uint32_t off = red + static_cast<uint32_t>((m * kBM + rr) * 4);
-        float part[16];
-#pragma unroll
-        for (int qq = 0; qq < 16; ++qq) part[qq] = qq < S ? ld_shared_cluster_f32(mapa_shared(off, qq)) : 0.0f;
         float v = 0.0f;
-#pragma unroll
-        for (int qq = 0; qq < 16; ++qq)
-          if (qq < S) v += part[qq];
-        const int row = t * kBM + rr;
+        for (int src = 0; src < S; ++src) v += s.red[(src * kNP + m) * R + lr];
+        const int row = t * kBM + r0 + lr;
         if (row < a.N) store_value(a, m, row, v);
       }
     }
-    cluster_sync_unaligned();  // peers have finished reading this CTA's shared memory
   }
 
   tc_fence_before_sync();
@@ -369,13 +381,12 @@ int ensure_attrs() {
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && done[dev]) return BP_OK;
   cudaError_t e = cudaFuncSetAttribute(skinny_tc_kernel<kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kSmemBytes));
-  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "cudaFuncSetAttribute(smem %zu): %s", kSmemBytes, cudaGetErrorString(e));
+                                       static_cast<int>(smem_bytes<kCluster>()));
+  if (e != cudaSuccess)
+    return fail(BP_ERR_CUDA, "cudaFuncSetAttribute(smem %zu): %s", smem_bytes<kCluster>(), cudaGetErrorString(e));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return BP_OK;
 }
-
-constexpr int kMaxClusterSplit = 8;  // portable cluster size
 
 // Work partition; depends on (N, K) and the SM count only, never on M.
 struct Partition {
@@ -397,8 +408,9 @@ Partition partition(int N, int K) {
     p.S = S < 1 ? 1 : S;
     p.P = p.tiles * p.S;
   } else {
+    // two CTAs per SM, each with its own 6-stage ring: twice the weight bytes in flight per SM
     p.S = 0;
-    p.P = static_cast<int>(p.units < sms ? p.units : sms);
+    p.P = static_cast<int>(p.units < 2 * sms ? p.units : 2 * sms);
   }
   return p;
 }
@@ -452,7 +464,7 @@ int launch_skinny_bf16(const void* x, long long ldx, const void* w, void* y, lon
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.P, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = p.S > 0 ? smem_bytes<true>() : smem_bytes<false>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int na = 0;
