@@ -274,6 +274,35 @@ def int4_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
     return out
 
 
+VERIFY_KS = (0, 1, 3, 7, 15, 32)
+
+
+def verify_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
+    """The drafting verify round of a Bolmo-shaped local model (encoder + decoder mLSTM layer, LM head):
+    one CUDA graph per K, S = K + 1 positions; device time per round and the weight bytes it streams."""
+    from byteprof_b200.optim.bolmo_local import BolmoLocal
+
+    m = BolmoLocal(device=device, seed=0)
+    wbytes = sum(t.numel() * t.element_size() for layer in (m.enc, m.dec)
+                 for t in (layer.w_qkvo, layer.w_if, layer.w_out, layer.w_gu, layer.w_down))
+    wbytes += (m.w_in.numel() + m.lm_head.numel()) * 2
+    m.capture(VERIFY_KS)
+    g0 = torch.Generator(device=device).manual_seed(8)
+    m.ids.copy_(torch.randint(0, m.vocab, (m.smax,), generator=g0, device=device))
+    out = {}
+    for k in VERIFY_KS:
+        g = m.graphs[k + 1]
+        time_graph_replays(g, 3)
+        us = time_graph_replays(g, reps) * 1e3 / reps
+        gbs = wbytes / (us * 1e-6) / 1e9
+        out[f"K{k}"] = {"us": round(us, 2), "positions_per_s": round((k + 1) / (us * 1e-6), 1),
+                        "weight_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    out["weight_bytes"] = wbytes
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
 def scan_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
     """NH=4, dk=dv=512, T positions from a zero state, h and the final state."""
     from byteprof_b200.optim.draft_core import mlstm_scan
@@ -435,6 +464,7 @@ def run_ours(args) -> int:
         extras["int8"] = int8_cells(device, peak)
         extras["int4"] = int4_cells(device, peak)
         extras["scan"] = scan_cells(device, peak)
+        extras["verify"] = verify_cells(device, peak)
 
     if rank == 0:
         # dominant kernel = the sweep cell with the largest device time per step

@@ -12,6 +12,7 @@
  *                       byteprof/optim/skinny.py:111-129   _launch (+ _split_reduce, skinny.py:83-90)
  *   bp_gemv_int8        byteprof/quant/triton_int8.py:40-47 gemv_int8
  *   bp_skinny_mm_int4   byteprof/optim/skinny.py:46-63, 136-166 skinny_mm (int4 g128 weight kind)
+ *   bp_rmsnorm          byteprof/optim/bolmo_draft.py:74-100 the local layers' norms (K + 1 rows)
  *   bp_mlstm_scan       byteprof/optim/mlstm_multistep.py:33-85  multistep_fw_kernel
  *                       byteprof/optim/mlstm_multistep.py:89-133 lazy_commit_kernel
  *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
@@ -120,6 +121,17 @@ int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, i
  */
 int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_packed, const void* scale, const void* zero,
                       void* y, long long ldy, int y_dtype, int M, int N, int K, int tile_rows, void* stream);
+
+/*
+ * Row-wise RMSNorm, bf16 in and out, fp32 arithmetic: y[r, :] = x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * w.
+ * One warp per row with a fixed summation order, so a row's result does not depend on how many rows
+ * the call holds (verifying K drafts at once gives the bits of K single steps). cols a multiple of 8,
+ * rows 16-byte aligned, strides multiples of 8 elements. Replaces the pre-norms, the per-head output
+ * norm and the final norm of the local layers run by byteprof's drafting engine
+ * (byteprof/optim/bolmo_draft.py:74-100).
+ */
+int bp_rmsnorm(const void* x, long long ldx, const void* w, void* y, long long ldy, int rows, int cols, float eps,
+               void* stream);
 
 /*
  * Fused mLSTM recurrence over T positions (exponential gating with the max stabiliser m), one head
