@@ -303,6 +303,55 @@ def verify_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
     return out
 
 
+DECODE_PROMPT, DECODE_NEW = 256, 512
+
+
+def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 20) -> dict:
+    """greedy decoding of the random-init Bolmo-1B-shaped byte model, batch 1. The
+    prompt (256 uniform-random bytes) is fed byte by byte through the same loop; the 511 steps after it
+    produce the remaining generated bytes and are timed on the wall clock (each step ends with its host
+    synchronisation, so wall time is the loop's real rate). Per-piece device times come from replaying
+    each CUDA graph alone afterwards."""
+    from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+
+    m = BolmoDecoder(device=device, seed=seed)
+    m.capture()
+    prompt = torch.randint(0, 256, (DECODE_PROMPT,), generator=torch.Generator().manual_seed(seed)).tolist()
+    m.reset()
+    tok, new_patch = 0, True
+    for b in prompt:
+        tok, new_patch = m.feed(b, new_patch)
+    prompt_patches = m.patches
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(DECODE_NEW - 1):
+        tok, new_patch = m.feed(tok, new_patch)
+    wall = time.perf_counter() - t0
+    gen_patches = m.patches - prompt_patches
+    w = m.weights()
+    local_bytes = sum(t.numel() * t.element_size() for k, t in w.items()
+                      if not k.startswith("glob") and k != "embed") + 2 * m.d  # + the embedding row
+    glob_bytes = sum(t.numel() * t.element_size() for k, t in w.items() if k.startswith("glob"))
+    per = {}
+    for name in ("enc0", "dec0", "glob"):
+        g = m.graphs[name]
+        time_graph_replays(g, 2)
+        per[name] = round(time_graph_replays(g, reps) * 1e3 / reps, 2)
+    steps = DECODE_NEW - 1
+    streamed = local_bytes * steps + glob_bytes * gen_patches
+    out = {
+        "bytes_per_s": round(steps / wall, 1), "ms_per_byte": round(wall / steps * 1e3, 4),
+        "generated": DECODE_NEW, "timed_steps": steps, "patches_in_timed_steps": gen_patches,
+        "prompt_patches": prompt_patches, "device_us": per,
+        "weight_bytes": {"local_per_byte": local_bytes, "global_per_patch": glob_bytes},
+        "weight_gbs": round(streamed / wall / 1e9, 1), "frac": round(streamed / wall / 1e9 / peak, 4),
+        "graphs_per_byte": "enc + dec, + glob on a patch start; one host sync per byte",
+    }
+    del m
+    torch.cuda.empty_cache()
+    return out
+
+
 def scan_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
     """NH=4, dk=dv=512, T positions from a zero state, h and the final state."""
     from byteprof_b200.optim.draft_core import mlstm_scan
@@ -465,6 +514,7 @@ def run_ours(args) -> int:
         extras["int4"] = int4_cells(device, peak)
         extras["scan"] = scan_cells(device, peak)
         extras["verify"] = verify_cells(device, peak)
+        extras["decode"] = decode_cells(device, peak, seed=rank)
 
     if rank == 0:
         # dominant kernel = the sweep cell with the largest device time per step

@@ -34,6 +34,15 @@ _SIGNATURES = {
     "bp_skinny_mm_int4": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_int,
                                   c_int, c_int, c_int, c_int, c_void_p]),
     "bp_rmsnorm": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_longlong, c_int, c_int, c_float, c_void_p]),
+    "bp_rmsnorm_ex": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_longlong, c_void_p, c_longlong,
+                              c_void_p, c_longlong, c_int, c_int, c_float, c_int, c_void_p]),
+    "bp_swiglu": (c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int, c_void_p]),
+    "bp_gate_softcap": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_longlong, c_int, c_int, c_float,
+                                c_void_p]),
+    "bp_decode_attention_workspace_bytes": (c_size_t, [c_int, c_int]),
+    "bp_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_int, c_int, c_int, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+    "bp_decode_finish": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "bp_mlstm_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_int, c_int, c_int, c_int, c_longlong, c_longlong, c_longlong, c_longlong,

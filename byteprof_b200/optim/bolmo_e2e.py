@@ -1,0 +1,212 @@
+"""End-to-end greedy byte decoding of a random-init Bolmo-1B-shaped model on the sm_100a kernels.
+
+Bolmo's remote model code and weights are not part of byteprof, so the model is defined here, with
+the shapes of the end-to-end benchmark configuration and weights ~ N(0, 0.02) (norm weights 1 + N(0, 0.02)):
+  * local encoder: byte embedding 512 x 2048 -> one mLSTM layer (bolmo_local.LocalLayer: 4 heads x 512,
+    forget bias +3, gate soft cap 15, SwiGLU 2816) -> RMSNorm -> e;
+  * boundary predictor: sigmoid(w_b . e) >= 0.5 (a 2048 -> 1 linear); patch vector P = W_p e;
+  * global model, once per patch on P at patch position t: 16 OLMo-2 blocks (d 2048, 16 heads x 128; q and
+    k RMSNorm over d; rotary embedding, theta 500000; attention over a static KV cache; the attention and
+    MLP outputs RMS-normalised before each residual add; SwiGLU 8192), then the decoder's initial RMSNorm
+    gives the patch value (byteprof/optim/bolmo_loop.py:58-61 does the same with dec.initial_norm);
+  * local decoder: W_in e + patch value -> one mLSTM layer -> RMSNorm -> LM head 2048 -> 512 -> argmax.
+The loop is byteprof's minimal loop (byteprof/optim/bolmo_loop.py:1-20, 182-207; bolmo.py:47-136): per
+byte the encoder graph, the global graph only when the previous step flagged a boundary (the first
+byte opens a patch), the decoder graph, then one device-to-host read of (token, boundary flag): the
+only synchronisation. Every projection is a skinny GEMM of this library (M = 1), the mLSTM steps are
+the fused scan, and the glue between them is the fused kernels of `decode_ops`.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .bolmo_local import LocalLayer, rmsnorm
+from .decode_ops import DecodeAttention, add_norm, decode_finish, norm_add, rope_tables, swiglu
+from .skinny import skinny_mm
+
+EPS = 1e-6
+
+
+def _rnd(gen, device, *shape, std=0.02):
+    return (torch.randn(*shape, generator=gen, device=device) * std).to(torch.bfloat16)
+
+
+def _norm_w(gen, device, *shape):
+    return (1.0 + torch.randn(*shape, generator=gen, device=device) * 0.02).to(torch.bfloat16)
+
+
+class GlobalBlock:
+    """One OLMo-2 block for single-position decoding with a static KV cache."""
+
+    def __init__(self, d: int, nh: int, ffn: int, max_pos: int, gen: torch.Generator, device: torch.device,
+                 workspace: torch.Tensor):
+        self.d, self.nh, self.ffn = d, nh, ffn
+        self.w_qkv = _rnd(gen, device, 3 * d, d)
+        self.q_norm = _norm_w(gen, device, d)
+        self.k_norm = _norm_w(gen, device, d)
+        self.w_o = _rnd(gen, device, d, d)
+        self.attn_norm = _norm_w(gen, device, d)
+        self.w_gu = _rnd(gen, device, 2 * ffn, d)
+        self.w_down = _rnd(gen, device, d, ffn)
+        self.mlp_norm = _norm_w(gen, device, d)
+        self.attn = DecodeAttention(nh, d // nh, max_pos, device, workspace)
+
+    def step(self, x: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+        """x [1, d] bf16 at patch position `pos` (device int64) -> the block's output [1, d]."""
+        att = self.attn(skinny_mm(x, self.w_qkv), self.q_norm, self.k_norm, cos, sin, pos, EPS)
+        h = add_norm(skinny_mm(att, self.w_o), x, self.attn_norm, EPS)
+        dn = skinny_mm(swiglu(skinny_mm(h, self.w_gu)), self.w_down)
+        return add_norm(dn, h, self.mlp_norm, EPS)
+
+
+class BolmoDecoder:
+    """The byte model with its per-byte CUDA graphs and the greedy decode loop (batch 1)."""
+
+    def __init__(self, device: torch.device | str = "cuda", seed: int = 0, d: int = 2048, vocab: int = 512,
+                 local_heads: int = 4, local_dh: int = 512, local_ffn: int = 2816, global_layers: int = 16,
+                 global_heads: int = 16, global_ffn: int = 8192, max_patches: int = 1024,
+                 rope_theta: float = 500000.0):
+        device = torch.device(device)
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.device, self.d, self.vocab, self.max_patches = device, d, vocab, max_patches
+        self.embed = _rnd(gen, device, vocab, d)
+        self.enc = LocalLayer(d, local_heads, local_dh, local_ffn, gen, device, smax=1)
+        self.enc_norm = _norm_w(gen, device, d)
+        self.w_boundary = _rnd(gen, device, 1, d)
+        self.w_patch = _rnd(gen, device, d, d)
+        ws = DecodeAttention.workspace_for(global_heads, max_patches, device)
+        self.blocks = [GlobalBlock(d, global_heads, global_ffn, max_patches, gen, device, ws)
+                       for _ in range(global_layers)]
+        self.dec_in_norm = _norm_w(gen, device, d)
+        self.w_in = _rnd(gen, device, d, d)
+        self.dec = LocalLayer(d, local_heads, local_dh, local_ffn, gen, device, smax=1)
+        self.final_norm = _norm_w(gen, device, d)
+        self.lm_head = _rnd(gen, device, vocab, d)
+        self.cos, self.sin = rope_tables(max_patches, d // global_heads, rope_theta, device)
+        # per-byte device buffers (graph inputs and outputs)
+        self.byte = torch.zeros(1, dtype=torch.long, device=device)
+        self.pos = torch.zeros(1, dtype=torch.long, device=device)  # the next patch position
+        self.e = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
+        self.patch = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
+        self.value = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
+        self.boundary_logit = torch.zeros(1, 1, dtype=torch.float32, device=device)
+        self.logits = torch.zeros(1, vocab, dtype=torch.float32, device=device)
+        self.out = torch.zeros(2, dtype=torch.long, device=device)  # [token, boundary flag]
+        self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
+        self.parity = 0  # which n / m buffers of the local layers hold the current state
+        self.patches = 0  # patch positions used (host count)
+        self._pin_byte = torch.zeros(1, dtype=torch.long).pin_memory()
+        self._pin_out = torch.zeros(2, dtype=torch.long).pin_memory()
+
+    def weights(self) -> dict[str, torch.Tensor]:
+        """Every parameter by name (the CPU oracle rebuilds the model from these)."""
+        w = {"embed": self.embed, "enc_norm": self.enc_norm, "w_boundary": self.w_boundary, "w_patch": self.w_patch,
+             "dec_in_norm": self.dec_in_norm, "w_in": self.w_in, "final_norm": self.final_norm,
+             "lm_head": self.lm_head}
+        for name, layer in (("enc", self.enc), ("dec", self.dec)):
+            for a in ("norm1", "w_qkvo", "w_if", "b_if", "mh_norm", "w_out", "norm2", "w_gu", "w_down"):
+                w[f"{name}.{a}"] = getattr(layer, a)
+        for i, b in enumerate(self.blocks):
+            for a in ("w_qkv", "q_norm", "k_norm", "w_o", "attn_norm", "w_gu", "w_down", "mlp_norm"):
+                w[f"glob{i}.{a}"] = getattr(b, a)
+        return w
+
+    # ---- the three per-byte pieces (device only, graph-capturable) ----
+    def enc_step(self, parity: int) -> None:
+        h = self.embed.index_select(0, self.byte)
+        _, e = self.enc.step(h, rmsnorm(h, self.enc.norm1, EPS), parity, out_norm=self.enc_norm, want_sum=False)
+        self.e.copy_(e)
+        skinny_mm(e, self.w_patch, out=self.patch)
+        skinny_mm(e, self.w_boundary, out=self.boundary_logit)
+
+    def glob_step(self) -> None:
+        x = self.patch
+        for blk in self.blocks:
+            x = blk.step(x, self.pos, self.cos, self.sin)
+        rmsnorm(x, self.dec_in_norm, EPS, out=self.value)
+        self.pos.add_(1)
+
+    def dec_step(self, parity: int) -> None:
+        h, x = norm_add(skinny_mm(self.e, self.w_in), self.value, self.dec.norm1, EPS)
+        _, xf = self.dec.step(h, x, parity, out_norm=self.final_norm, want_sum=False)
+        skinny_mm(xf, self.lm_head, out=self.logits)
+        decode_finish(self.logits, self.boundary_logit, self.out)
+
+    # ---- state ----
+    def reset(self) -> None:
+        self.enc.reset()
+        self.dec.reset()
+        self.pos.zero_()
+        self.value.zero_()
+        for blk in self.blocks:
+            blk.attn.reset()
+        self.parity = 0
+        self.patches = 0
+
+    def _pieces(self):
+        return (("enc0", lambda: self.enc_step(0)), ("enc1", lambda: self.enc_step(1)), ("glob", self.glob_step),
+                ("dec0", lambda: self.dec_step(0)), ("dec1", lambda: self.dec_step(1)))
+
+    def capture(self) -> None:
+        """One CUDA graph per piece and state parity. The warm-up runs go through the same buffers and
+        are undone by `reset` (capture before decoding)."""
+        s_ = torch.cuda.Stream()
+        s_.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_):
+            for _, fn in self._pieces():
+                fn()
+        torch.cuda.current_stream().wait_stream(s_)
+        for name, fn in self._pieces():
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            self.graphs[name] = g
+        torch.cuda.synchronize()
+        self.reset()
+
+    def _run(self, name: str, fn) -> None:
+        g = self.graphs.get(name)
+        if g is not None:
+            g.replay()
+        else:
+            fn()
+
+    def launch(self, b: int, new_patch: bool) -> None:
+        """Queue one byte (encoder, the global model if a patch starts here, decoder); no sync."""
+        if not 0 <= b < self.vocab:
+            raise ValueError(f"byte id {b} outside the vocabulary")
+        if new_patch and self.patches >= self.max_patches:
+            raise RuntimeError(f"more than {self.max_patches} patches: the static KV cache is full")
+        p = self.parity
+        self._pin_byte[0] = b
+        self.byte.copy_(self._pin_byte, non_blocking=True)
+        self._run(f"enc{p}", lambda: self.enc_step(p))
+        if new_patch:
+            self._run("glob", self.glob_step)
+            self.patches += 1
+        self._run(f"dec{p}", lambda: self.dec_step(p))
+        self._pin_out.copy_(self.out, non_blocking=True)
+        self.parity = 1 - p
+
+    def feed(self, b: int, new_patch: bool) -> tuple[int, bool]:
+        """One byte, then the step's single synchronisation; returns (greedy token, boundary flag)."""
+        self.launch(b, new_patch)
+        torch.cuda.current_stream().synchronize()
+        return int(self._pin_out[0]), bool(self._pin_out[1])
+
+    @torch.no_grad()
+    def generate(self, prompt: list[int], n_new: int) -> tuple[list[int], list[bool]]:
+        """Greedy decoding from the current state: the prompt bytes in order, then each predicted byte.
+        Returns the n_new generated bytes and, for every byte fed, whether it opened a patch."""
+        new_patch, opened, tok = True, [], 0
+        for b in prompt:
+            opened.append(new_patch)
+            tok, new_patch = self.feed(b, new_patch)
+        out = []
+        for i in range(n_new):
+            out.append(tok)
+            if i + 1 < n_new:
+                opened.append(new_patch)
+                tok, new_patch = self.feed(tok, new_patch)
+        return out, opened

@@ -17,7 +17,8 @@ Bolmo-1B's local shapes, one mLSTM layer each for the encoder and the decoder:
     -> RMSNorm -> SwiGLU MLP (width 2816: gate and up as one [2 * 2816, d] GEMM, down [d, 2816]) ->
     residual;
   * final RMSNorm and LM head 512 x d; greedy argmax.
-Every step is row-independent (the skinny kernels' K partition depends on (N, K) only, the norms sum
+The steps between the GEMMs (RMSNorm with its residual add, the per-head output gate, SwiGLU, the gate
+soft cap) are the fused kernels of `decode_ops`. Every step is row-independent (the skinny kernels' K partition depends on (N, K) only, the norms sum
 each row in a fixed order, the scan computes position t the same way for any number of positions), so
 a round that verifies K correct drafts yields the bits of K + 1 single-position rounds.
 """
@@ -25,10 +26,11 @@ a round that verifies K correct drafts yields the bits of K + 1 single-position 
 from __future__ import annotations
 
 import torch
-import torch.nn.functional as F
 
 from .. import _lib
 from . import draft_fused
+from .decode_ops import gate_softcap, norm_add, norm_gate, swiglu
+from .draft_core import mlstm_scan
 from .skinny import skinny_mm
 
 
@@ -47,12 +49,14 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     return y
 
 
-def _soft_cap(g: torch.Tensor, cap: float) -> torch.Tensor:
-    return cap * torch.tanh(g / cap)
-
-
 class LocalLayer:
-    """One Bolmo-shaped mLSTM block with its recurrent state (c, n, m) and the start n / m of a round."""
+    """One Bolmo-shaped mLSTM block with its recurrent state (c, n, m).
+
+    `forward` runs S positions for a verify round (the state is read, not changed; `commit` applies
+    positions 0..L later). `step` runs one position of the decode loop and advances the state: c is
+    updated in place, n and m alternate between two buffers (the scan's CTAs all read n and m, so they
+    cannot be written in place); `parity` names the buffer holding the current n and m.
+    """
 
     def __init__(self, d: int, nh: int, dh: int, ffn: int, gen: torch.Generator, device: torch.device,
                  smax: int, std: float = 0.02, gate_cap: float = 15.0, norm_eps: float = 1e-6,
@@ -73,40 +77,64 @@ class LocalLayer:
         self.w_down = rnd(d, ffn)
         f32 = dict(dtype=torch.float32, device=device)
         self.state = (torch.zeros(1, nh, dh, dh, **f32), torch.zeros(1, nh, dh, **f32), torch.zeros(1, nh, 1, **f32))
+        self.nm = ((self.state[1], self.state[2]), (torch.zeros(1, nh, dh, **f32), torch.zeros(1, nh, 1, **f32)))
         self.nstart = torch.zeros(nh, dh, **f32)
         self.mstart = torch.zeros(nh, **f32)
         self.hbuf = torch.zeros(smax, nh, dh, dtype=torch.bfloat16, device=device)
         self.saved: dict[int, tuple[torch.Tensor, ...]] = {}
 
     def reset(self) -> None:
-        for t in self.state:
+        for t in (*self.state, *self.nm[1]):
             t.zero_()
 
-    def forward(self, h: torch.Tensor) -> torch.Tensor:
-        """h [S, d] bf16 (contiguous) -> [S, d]; the state is read, not changed (see `commit`)."""
-        s, d, nh, dh = h.shape[0], self.d, self.nh, self.dh
-        x = rmsnorm(h, self.norm1, self.norm_eps)
+    def current_state(self, parity: int = 0) -> tuple[torch.Tensor, ...]:
+        return (self.state[0], *self.nm[parity])
+
+    def _project(self, x: torch.Tensor):
+        s, d, nh, dh = x.shape[0], self.d, self.nh, self.dh
         y = skinny_mm(x, self.w_qkvo)  # [S, 4d]: q | k | v | o
-        g = skinny_mm(x, self.w_if, out=torch.empty(s, 2 * nh, dtype=torch.float32, device=h.device)) + self.b_if
-        g = _soft_cap(g, self.gate_cap)
-        q, k, v, o = (y[:, j * d:(j + 1) * d].view(s, nh, dh) for j in range(4))
-        i_pre, f_pre = g[:, :nh].reshape(s, nh, 1), g[:, nh:].reshape(s, nh, 1)
+        g = skinny_mm(x, self.w_if, out=torch.empty(s, 2 * nh, dtype=torch.float32, device=x.device))
+        gate_softcap(g, self.b_if, self.gate_cap)
+        q, k, v = (y[:, j * d:(j + 1) * d].view(s, nh, dh) for j in range(3))
+        return y, q, k, v, g[:, :nh].reshape(s, nh, 1), g[:, nh:].reshape(s, nh, 1)
+
+    def _tail(self, h: torch.Tensor, y: torch.Tensor, s: int, out_norm: torch.Tensor | None, want_sum: bool):
+        d, eps = self.d, self.norm_eps
+        z = norm_gate(self.hbuf[:s], y[:, 3 * d:], self.mh_norm, eps,
+                      out=torch.empty(s, d, dtype=torch.bfloat16, device=h.device))
+        h2, x2 = norm_add(skinny_mm(z, self.w_out), h, self.norm2, eps)
+        dn = skinny_mm(swiglu(skinny_mm(x2, self.w_gu)), self.w_down)
+        if out_norm is None:
+            return h2 + dn, None
+        return norm_add(dn, h2, out_norm, eps, want_sum)
+
+    def forward(self, h: torch.Tensor, x: torch.Tensor | None = None, out_norm: torch.Tensor | None = None,
+                want_sum: bool = True):
+        """h [S, d] bf16 (contiguous) -> (h_out [S, d], rmsnorm(h_out) * out_norm or None). x is
+        rmsnorm(h) * norm1 when the caller has it already (fused with the add that made h). The state is
+        read, not changed (see `commit`)."""
+        s = h.shape[0]
+        if x is None:
+            x = rmsnorm(h, self.norm1, self.norm_eps)
+        y, q, k, v, i_pre, f_pre = self._project(x)
         draft_fused.multistep_fw(self.state, q, k, v, i_pre, f_pre, self.hbuf, self.nstart, self.mstart,
                                  eps=self.mlstm_eps)
         self.saved[s] = (k, v, i_pre, f_pre)
-        hn = torch.empty(s, d, dtype=torch.bfloat16, device=h.device)
-        for j in range(nh):  # per-head norm: head j of every position, its own weight
-            rmsnorm(self.hbuf[:s, j, :], self.mh_norm[j], self.norm_eps, out=hn[:, j * dh:(j + 1) * dh])
-        z = torch.sigmoid(y[:, 3 * d:]) * hn
-        h2 = h + skinny_mm(z, self.w_out)
-        gu = skinny_mm(rmsnorm(h2, self.norm2, self.norm_eps), self.w_gu)
-        a = F.silu(gu[:, :self.ffn]) * gu[:, self.ffn:]
-        return h2 + skinny_mm(a, self.w_down)
+        return self._tail(h, y, s, out_norm, want_sum)
 
     def commit(self, length: torch.Tensor, s: int) -> None:
         """state <- the state after positions 0..L of the last S-position forward (L on the device)."""
         k, v, i_pre, f_pre = self.saved[s]
         draft_fused.lazy_commit(self.state, k, v, i_pre, f_pre, length, self.nstart, self.mstart)
+
+    def step(self, h: torch.Tensor, x: torch.Tensor, parity: int, out_norm: torch.Tensor | None = None,
+             want_sum: bool = True):
+        """One position ([1, d]) of the decode loop; the state advances (n, m from buffer `parity` to
+        buffer 1 - parity). Returns as `forward`."""
+        y, q, k, v, i_pre, f_pre = self._project(x)
+        mlstm_scan(self.current_state(parity), q, k, v, i_pre, f_pre, self.hbuf, self.current_state(1 - parity),
+                   self.mlstm_eps)
+        return self._tail(h, y, 1, out_norm, want_sum)
 
 
 class BolmoLocal:
@@ -137,10 +165,10 @@ class BolmoLocal:
 
     def round(self, s: int) -> None:
         """One verify round over ids[:s] on the device: tokens, acceptance and the state commit."""
-        h = self.enc.forward(self.embed.index_select(0, self.ids[:s]))
-        hd = self.dec.forward(skinny_mm(h, self.w_in) + self.last_value)
-        logits = skinny_mm(rmsnorm(hd, self.final_norm, 1e-6), self.lm_head,
-                           out=torch.empty(s, self.vocab, dtype=torch.float32, device=self.device))
+        h, _ = self.enc.forward(self.embed.index_select(0, self.ids[:s]))
+        hd, x = norm_add(skinny_mm(h, self.w_in), self.last_value, self.dec.norm1, self.dec.norm_eps)
+        _, xf = self.dec.forward(hd, x, out_norm=self.final_norm, want_sum=False)
+        logits = skinny_mm(xf, self.lm_head, out=torch.empty(s, self.vocab, dtype=torch.float32, device=self.device))
         self.tok[:s].copy_(torch.argmax(logits, dim=-1))
         draft_fused.accept(self.ids, self.tok, self.out, s, self.smax)
         length = self.out[self.smax:]

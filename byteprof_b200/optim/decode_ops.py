@@ -1,0 +1,171 @@
+"""Fused glue operators of the batch-1 byte decoder, on the sm_100a kernels of csrc/decode.cu.
+
+They replace the chains of small torch ops that byteprof's minimal Bolmo loop runs between its
+GEMMs (byteprof/optim/bolmo.py:32-136, bolmo_loop.py:36-64):
+  * norm_add(x, res, w)      h = bf16(x + res), returns (h, rmsnorm(h) * w)   (pre-norm residual add)
+  * add_norm(x, res, w)      res + rmsnorm(x) * w                              (OLMo-2 norm-after block)
+  * norm_gate(h, o, w)       sigmoid(o) * rmsnorm(h) * w per head              (mLSTM output gate)
+  * swiglu(gu)               silu(gate) * up
+  * gate_softcap(g, b, cap)  cap * tanh((g + b) / cap), in place
+  * DecodeAttention          one query position over a static KV cache (q/k RMSNorm, rotary
+                             embedding, cache write, split attention)
+  * decode_finish(logits, b, out)  out = [argmax(logits), sigmoid(b) >= 0.5]
+Every bf16 intermediate is rounded where a bf16 torch tensor would hold it. CUDA tensors only; a
+missing library raises.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+NORM_PLAIN, NORM_ADD_FIRST, NORM_ADD_AFTER, NORM_GATE = 0, 1, 2, 3
+
+
+def _bf16(*ts: torch.Tensor) -> None:
+    for t in ts:
+        if t is not None and t.dtype != torch.bfloat16:
+            raise ValueError("bf16 tensors expected")
+
+
+def _rows(t: torch.Tensor) -> tuple[int, int]:
+    if t.dim() != 2 or t.stride(1) != 1:
+        raise ValueError("2-D tensors with unit column stride expected")
+    return t.shape[0], t.stride(0)
+
+
+def rmsnorm_ex(x: torch.Tensor, w: torch.Tensor, eps: float, mode: int = NORM_PLAIN, res: torch.Tensor | None = None,
+               s_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The general form on [rows, cols] bf16 tensors with one weight row (w [cols])."""
+    rows, ldx = _rows(x)
+    cols = x.shape[1]
+    y = out if out is not None else torch.empty(rows, cols, dtype=torch.bfloat16, device=x.device)
+    ldres = 0
+    if res is not None:
+        if res.shape[-1] != cols:
+            raise ValueError("res must have cols columns")
+        ldres = 0 if res.dim() == 1 or res.shape[0] == 1 else _rows(res)[1]
+    lds = _rows(s_out)[1] if s_out is not None else 0
+    _bf16(x, w, res, s_out, y)
+    if w.numel() != cols:
+        raise ValueError("w must hold cols values")
+    _lib.require_cuda(x, w, res, s_out, y)
+    with torch.cuda.device(x.device):
+        _lib.call("bp_rmsnorm_ex", x.data_ptr(), ldx, w.data_ptr(), 1, _lib.ptr(res), ldres, _lib.ptr(s_out), lds,
+                  y.data_ptr(), _rows(y)[1], rows, cols, eps, mode, _lib.stream_of(x))
+    return y
+
+
+def norm_add(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float,
+             want_sum: bool = True) -> tuple[torch.Tensor | None, torch.Tensor]:
+    """(h, n) with h = bf16(x + res) and n = rmsnorm(h) * w; res may be one row (broadcast)."""
+    s = torch.empty_like(x) if want_sum else None
+    return s, rmsnorm_ex(x, w, eps, NORM_ADD_FIRST, res=res, s_out=s)
+
+
+def add_norm(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """res + rmsnorm(x) * w (both roundings to bf16 as torch would do them)."""
+    return rmsnorm_ex(x, w, eps, NORM_ADD_AFTER, res=res)
+
+
+def norm_gate(h: torch.Tensor, o: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor) -> torch.Tensor:
+    """Per-head output gate of the mLSTM layer: h [S, NH, DH] (contiguous head rows), o [S, >= NH * DH]
+    the o-gate pre-activations (row stride free), w [NH, DH]; out[s, j*DH:(j+1)*DH] = bf16(bf16(sigmoid(o))
+    * rmsnorm(h[s, j]) * w[j])."""
+    s, nh, dh = h.shape
+    if h.stride(2) != 1 or h.stride(1) != dh or tuple(w.shape) != (nh, dh) or not w.is_contiguous():
+        raise ValueError("h needs contiguous (NH, DH) rows and w must be a contiguous [NH, DH]")
+    if o.stride(1) != 1 or out.stride(1) != 1 or o.shape[0] < s or out.shape[0] < s:
+        raise ValueError("o and out need unit column strides and S rows")
+    _bf16(h, o, w, out)
+    _lib.require_cuda(h, o, w, out)
+    with torch.cuda.device(h.device):
+        _lib.call("bp_rmsnorm_ex", h.data_ptr(), h.stride(0), w.data_ptr(), nh, o.data_ptr(), o.stride(0), None, 0,
+                  out.data_ptr(), out.stride(0), s * nh, dh, eps, NORM_GATE, _lib.stream_of(h))
+    return out
+
+
+def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """gu [rows, 2 * ffn] bf16 (gate | up) -> bf16(bf16(silu(gate)) * up) [rows, ffn]."""
+    rows, ld = _rows(gu)
+    ffn = gu.shape[1] // 2
+    y = out if out is not None else torch.empty(rows, ffn, dtype=torch.bfloat16, device=gu.device)
+    _bf16(gu, y)
+    _lib.require_cuda(gu, y)
+    with torch.cuda.device(gu.device):
+        _lib.call("bp_swiglu", gu.data_ptr(), ld, y.data_ptr(), _rows(y)[1], rows, ffn, _lib.stream_of(gu))
+    return y
+
+
+def gate_softcap(g: torch.Tensor, bias: torch.Tensor | None, cap: float) -> torch.Tensor:
+    """In place on g [rows, n] fp32: g <- cap * tanh((g + bias) / cap)."""
+    rows, ld = _rows(g)
+    if g.dtype != torch.float32 or (bias is not None and (bias.dtype != torch.float32 or bias.numel() != g.shape[1])):
+        raise ValueError("fp32 g and bias of n values expected")
+    _lib.require_cuda(g, bias)
+    with torch.cuda.device(g.device):
+        _lib.call("bp_gate_softcap", g.data_ptr(), ld, _lib.ptr(bias), g.data_ptr(), ld, rows, g.shape[1], cap,
+                  _lib.stream_of(g))
+    return g
+
+
+def decode_finish(logits: torch.Tensor, boundary_logit: torch.Tensor | None, out: torch.Tensor) -> torch.Tensor:
+    """out[0] = argmax(logits) (torch order), out[1] = sigmoid(boundary_logit) >= 0.5; int64 out."""
+    if logits.dtype != torch.float32 or not logits.is_contiguous() or out.dtype != torch.int64 or out.numel() < 2:
+        raise ValueError("contiguous fp32 logits and an int64 out of >= 2 values expected")
+    if boundary_logit is not None and boundary_logit.dtype != torch.float32:
+        raise ValueError("fp32 boundary logit expected")
+    _lib.require_cuda(logits, boundary_logit, out)
+    with torch.cuda.device(logits.device):
+        _lib.call("bp_decode_finish", logits.data_ptr(), logits.numel(), _lib.ptr(boundary_logit), out.data_ptr(),
+                  _lib.stream_of(logits))
+    return out
+
+
+def rope_tables(max_pos: int, head_dim: int, theta: float, device: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """cos / sin [max_pos, head_dim / 2] fp32 of angle p * theta^(-2i / head_dim), computed in float64 on
+    the host."""
+    inv = 1.0 / theta ** (torch.arange(0, head_dim // 2, dtype=torch.float64) * 2 / head_dim)
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cos(ang).float().to(device), torch.sin(ang).float().to(device)
+
+
+class DecodeAttention:
+    """Static KV caches of one layer plus the shared split-attention workspace."""
+
+    def __init__(self, nh: int, head_dim: int, max_pos: int, device: torch.device,
+                 workspace: torch.Tensor | None = None):
+        self.nh, self.hd, self.max_pos = nh, head_dim, max_pos
+        self.k_cache = torch.zeros(max_pos, nh, head_dim, dtype=torch.bfloat16, device=device)
+        self.v_cache = torch.zeros(max_pos, nh, head_dim, dtype=torch.bfloat16, device=device)
+        need = int(_lib.lib().bp_decode_attention_workspace_bytes(nh, max_pos))
+        if workspace is None or workspace.numel() < need:
+            workspace = torch.zeros(need, dtype=torch.uint8, device=device)
+        self.workspace = workspace
+
+    @staticmethod
+    def workspace_for(nh: int, max_pos: int, device: torch.device) -> torch.Tensor:
+        need = int(_lib.lib().bp_decode_attention_workspace_bytes(nh, max_pos))
+        return torch.zeros(need, dtype=torch.uint8, device=device)
+
+    def reset(self) -> None:
+        self.k_cache.zero_()
+        self.v_cache.zero_()
+
+    def __call__(self, qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor, cos: torch.Tensor,
+                 sin: torch.Tensor, pos: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+        d = self.nh * self.hd
+        if qkv.dtype != torch.bfloat16 or qkv.numel() != 3 * d or not qkv.is_contiguous():
+            raise ValueError("qkv must be a contiguous bf16 [1, 3 * nh * head_dim]")
+        if pos.dtype != torch.int64 or cos.shape != (self.max_pos, self.hd // 2) or sin.shape != cos.shape:
+            raise ValueError("int64 pos and cos / sin tables [max_pos, head_dim / 2] expected")
+        y = out if out is not None else torch.empty(1, d, dtype=torch.bfloat16, device=qkv.device)
+        _bf16(q_norm, k_norm, y)
+        _lib.require_cuda(qkv, q_norm, k_norm, cos, sin, pos, y)
+        with torch.cuda.device(qkv.device):
+            _lib.call("bp_decode_attention", qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(),
+                      sin.data_ptr(), pos.data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(), y.data_ptr(),
+                      self.nh, self.hd, self.max_pos, eps, self.hd ** -0.5, self.workspace.data_ptr(),
+                      self.workspace.numel(), _lib.stream_of(qkv))
+        return y

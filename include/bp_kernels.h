@@ -17,6 +17,10 @@
  *                       byteprof/optim/mlstm_multistep.py:89-133 lazy_commit_kernel
  *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
  *   bp_mlstm_accept     byteprof/optim/mlstm_multistep.py:136-146 accept_kernel
+ *   bp_rmsnorm_ex, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish
+ *                       the per-byte pieces of the minimal Bolmo loop: byteprof/optim/bolmo.py:32-136
+ *                       (_layer_step, LocalLoop.enc_step / dec_step, GlobalStep.step) and
+ *                       byteprof/optim/bolmo_loop.py:36-64 (MinimalPieces: norm, lm_head, argmax)
  */
 #ifndef BP_KERNELS_H
 #define BP_KERNELS_H
@@ -132,6 +136,64 @@ int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_packed, con
  */
 int bp_rmsnorm(const void* x, long long ldx, const void* w, void* y, long long ldy, int rows, int cols, float eps,
                void* stream);
+
+/*
+ * RMSNorm fused with the step around it; bf16 in and out, fp32 arithmetic, one warp per row with
+ * bp_rmsnorm's summation order. n(v) = bf16(v * rsqrt(mean(v^2) + eps) * w):
+ *   BP_NORM_PLAIN      y = n(x)
+ *   BP_NORM_ADD_FIRST  s = bf16(x + res); y = n(s)     (s_out receives s when not NULL)
+ *   BP_NORM_ADD_AFTER  y = bf16(res + n(x))
+ *   BP_NORM_GATE       y = bf16(bf16(sigmoid(res)) * n(x))
+ * Rows come in groups of w_rows, the rows of w ([w_rows, cols]): row r = g * w_rows + j uses weight
+ * row j and lives at element g * ld + j * cols of x, res, s_out and y (w_rows = 1: row r at r * ld).
+ * ldres = 0 broadcasts one res row. cols and strides multiples of 8, 16-byte aligned bases.
+ * Replaces the RMSNorm + residual add, RMSNorm + add (OLMo-2) and output-gate steps of the layers the
+ * minimal Bolmo loop runs (byteprof/optim/bolmo.py:32-44, 100-136).
+ */
+enum { BP_NORM_PLAIN = 0, BP_NORM_ADD_FIRST = 1, BP_NORM_ADD_AFTER = 2, BP_NORM_GATE = 3 };
+int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_rows, const void* res, long long ldres,
+                  void* s_out, long long lds, void* y, long long ldy, int rows, int cols, float eps, int mode,
+                  void* stream);
+
+/*
+ * SwiGLU: out[r, j] = bf16(bf16(silu(gu[r, j])) * gu[r, ffn + j]) for j < ffn (gate | up halves of one
+ * GEMM output, bf16). ffn and strides multiples of 8, 16-byte aligned. Replaces act_fn(gate) * up of
+ * the MLPs in the Bolmo layers (byteprof/optim/bolmo.py:32-44).
+ */
+int bp_swiglu(const void* gu, long long ldgu, void* out, long long ldo, int rows, int ffn, void* stream);
+
+/*
+ * mLSTM gate pre-activations: out[r, c] = cap * tanh((g[r, c] + bias[c]) / cap), fp32 (bias may be
+ * NULL; out may equal g). Replaces the soft cap of the xLSTM layer's input / forget gates.
+ */
+int bp_gate_softcap(const float* g, long long ldg, const float* bias, float* out, long long ldo, int rows, int n,
+                    float cap, void* stream);
+
+/*
+ * One query position of an OLMo-2 attention layer against a static KV cache, position p = *pos read on
+ * the device (so a CUDA graph replays it at every position):
+ *   qkv [3 * nh * head_dim] bf16 = q | k | v of the position; q and k are RMS-normalised over the
+ *   whole width (weights q_norm_w, k_norm_w, eps), rotated (rotary halves; cos_t / sin_t fp32
+ *   [max_pos, head_dim / 2]), k and v written to k_cache / v_cache [max_pos, nh, head_dim] bf16 at p;
+ *   out [nh * head_dim] bf16 = softmax(q . k_j * scale) over j <= p, times v_j.
+ * Work is split over 64-position chunks per head; the last chunk to finish combines them in chunk
+ * order (deterministic). workspace: the bytes bp_decode_attention_workspace_bytes returns for nh and
+ * max_pos, zero-filled before first use and left zero-filled. head_dim 128. A position outside [0, max_pos) writes NaN.
+ * Replaces GlobalStep.step's attention over the StaticCache (byteprof/optim/bolmo.py:100-136).
+ */
+size_t bp_decode_attention_workspace_bytes(int nh, int max_pos);
+int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos_t,
+                        const float* sin_t, const int64_t* pos, void* k_cache, void* v_cache, void* out, int nh,
+                        int head_dim, int max_pos, float eps, float scale, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/*
+ * End of a decode step: out[0] = argmax(logits[0:n]) (torch.argmax order: NaN largest, lowest index on
+ * ties), out[1] = sigmoid(*boundary_logit) >= 0.5 (0 when boundary_logit is NULL); out int64.
+ * Replaces the argmax and the boundary test of the minimal Bolmo loop (byteprof/optim/bolmo_loop.py:48-53,
+ * 182-190).
+ */
+int bp_decode_finish(const float* logits, int n, const float* boundary_logit, int64_t* out, void* stream);
 
 /*
  * Fused mLSTM recurrence over T positions (exponential gating with the max stabiliser m), one head

@@ -1,0 +1,124 @@
+"""End-to-end greedy byte decoding of the Bolmo-shaped model (byteprof_b200.optim.bolmo_e2e) against the
+CPU oracle (oracle/bolmo_ref.py), at the benchmark configuration's shapes (d 2048, 16 global layers,
+local mLSTM layers of 4 x 512 heads, vocabulary 512).
+
+With random weights and bf16 activations the model amplifies a single bf16 rounding step: some
+heads' mLSTM readout q.C nearly cancels, so their output is mostly rounding noise, and the per-head
+RMSNorm scales that noise to O(1). Two implementations whose sums run in different orders (tensor-core
+GEMMs against float32 BLAS) therefore drift apart by a few percent of the logits' RMS and, at near-ties,
+pick different greedy bytes -- as the reference saw when it swapped its own kernels for cuBLAS. Every
+op is checked on equal inputs elsewhere (tests/test_decode_ops_gpu.py, the skinny and scan tests); here
+the oracle is driven with the GPU's inputs (teacher forcing: the same bytes and patch decisions) and the
+whole model is checked statistically: the logits of every step strongly correlated with the oracle's,
+their deviation a small fraction of their RMS, and the greedy byte and boundary decision agreeing at
+most steps, every disagreement at a small top-2 gap. The first divergence of the free-running greedy
+sequences is reported. CUDA-graph decoding gives exactly the bits of eager decoding, and decoding is
+deterministic."""
+
+import numpy as np
+import pytest
+import torch
+
+from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+from helpers import to_np
+from oracle import bolmo_ref
+
+pytestmark = pytest.mark.gpu
+MIN_CORR = 0.9        # per-step correlation of the logits with the oracle's
+MAX_MEDIAN_DEV = 0.1  # median over steps of max |logit - oracle| / RMS(oracle logits)
+MIN_TOKEN_AGREE = 0.75
+MIN_BOUNDARY_AGREE = 0.9
+
+
+@pytest.fixture(scope="module")
+def model():
+    m = BolmoDecoder(seed=11)
+    m.capture()
+    return m
+
+
+@pytest.fixture(scope="module")
+def ref(model):
+    return bolmo_ref.BolmoRef({k: to_np(v) for k, v in model.weights().items()})
+
+
+def _prompt(n, seed):
+    return np.random.default_rng(seed).integers(0, 256, size=n).tolist()
+
+
+def _teacher_forced(model, ref, prompt, n_new):
+    model.reset()
+    ref.reset()
+    fed, rows, new_patch = list(prompt), [], True
+    i = 0
+    while i < len(fed):
+        b = fed[i]
+        tok, bnd = model.feed(b, new_patch)
+        lg = to_np(model.logits)[0]
+        rl, rb, rbl = ref.feed(b, new_patch)
+        rows.append((tok, bnd, lg, rl, rb, rbl, new_patch))
+        if i + 1 >= len(prompt) and len(fed) < len(prompt) + n_new - 1:
+            fed.append(tok)
+        new_patch = bnd
+        i += 1
+    return fed, rows
+
+
+def _check(rows):
+    """Statistics of a teacher-forced run; asserts the bars and returns them."""
+    devs, corrs, tok_ok, bnd_ok, gaps, first = [], [], 0, 0, [], None
+    for t, (tok, bnd, lg, rl, rb, rbl, opened) in enumerate(rows):
+        rms = float(np.sqrt(np.mean(rl.astype(np.float64) ** 2)))
+        devs.append(float(np.abs(lg - rl).max()) / rms)
+        corrs.append(float(np.corrcoef(lg, rl)[0, 1]))
+        if tok == int(np.argmax(rl)):
+            tok_ok += 1
+        else:
+            gaps.append(bolmo_ref.top2_gap(rl) / rms)
+            first = t if first is None else first
+        bnd_ok += bnd == rb
+    n = len(rows)
+    stats = {"steps": n, "min_corr": min(corrs), "median_dev": float(np.median(devs)), "max_dev": max(devs),
+             "token_agree": tok_ok / n, "boundary_agree": bnd_ok / n, "first_token_divergence": first,
+             "max_gap_at_disagreement": max(gaps) if gaps else None, "patches": sum(r[6] for r in rows)}
+    print(stats)
+    assert stats["min_corr"] >= MIN_CORR, stats
+    assert stats["median_dev"] <= MAX_MEDIAN_DEV, stats
+    assert stats["token_agree"] >= MIN_TOKEN_AGREE and stats["boundary_agree"] >= MIN_BOUNDARY_AGREE, stats
+    assert not gaps or max(gaps) <= 2 * stats["max_dev"], stats  # disagreements only at near-ties
+    return stats
+
+
+def test_graphs_give_the_bits_of_eager_decoding(model):
+    prompt = _prompt(12, 1)
+    model.reset()
+    tg, og = model.generate(prompt, 20)
+    lg = model.logits.clone()
+    graphs, model.graphs = model.graphs, {}
+    try:
+        model.reset()
+        te, oe = model.generate(prompt, 20)
+        assert tg == te and og == oe
+        assert torch.equal(lg, model.logits)
+    finally:
+        model.graphs = graphs
+    model.reset()
+    assert model.generate(prompt, 20) == (tg, og)  # deterministic across runs
+
+
+def test_short_decode_tracks_the_oracle(model, ref):
+    fed, rows = _teacher_forced(model, ref, _prompt(32, 2), 32)
+    stats = _check(rows)
+    assert 0 < stats["patches"] <= len(rows)
+
+
+def test_benchmark_configuration_decode_tracks_the_oracle(model, ref):
+    """Prompt of 256 uniform-random bytes, 512 bytes generated (the benchmark's decode)."""
+    prompt = _prompt(256, 3)
+    fed, rows = _teacher_forced(model, ref, prompt, 512)
+    assert len(rows) == 256 + 511
+    stats = _check(rows)
+    model.reset()
+    gen, opened = model.generate(prompt, 512)
+    assert gen == fed[256:] + [rows[-1][0]]  # the free-running decode is the teacher-forced one
+    assert sum(opened) == stats["patches"]

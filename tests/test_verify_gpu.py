@@ -99,7 +99,7 @@ def test_one_layer_against_an_fp32_restatement():
     gen = torch.Generator(device="cuda").manual_seed(5)
     layer = LocalLayer(2048, 4, 512, 2816, gen, torch.device("cuda"), smax=9)
     h = (torch.randn(9, 2048, generator=gen, device="cuda")).to(torch.bfloat16)
-    out = layer.forward(h).float()
+    out = layer.forward(h)[0].float()
 
     def norm(x, w):
         return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
