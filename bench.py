@@ -306,47 +306,234 @@ def verify_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
 DECODE_PROMPT, DECODE_NEW = 256, 512
 
 
-def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 20) -> dict:
-    """greedy decoding of the random-init Bolmo-1B-shaped byte model, batch 1. The
-    prompt (256 uniform-random bytes) is fed byte by byte through the same loop; the 511 steps after it
-    produce the remaining generated bytes and are timed on the wall clock (each step ends with its host
-    synchronisation, so wall time is the loop's real rate). Per-piece device times come from replaying
-    each CUDA graph alone afterwards."""
-    from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+class TorchDecoder:
+    """The same model (the same weight tensors) and the same loop on stock PyTorch ops: cuBLAS F.linear,
+    RMSNorm as HF's OLMo-2 module computes it, scaled_dot_product_attention over a static cache in HF's
+    layout, torch rotary embedding, and the mLSTM step written in torch ops (fp32 state). The three
+    per-byte pieces are CUDA graphs and each byte ends with one host synchronisation, as in byteprof's
+    minimal Bolmo loop (byteprof/optim/bolmo_loop.py:182-207), which runs HF modules on cuBLAS. It is the
+    comparison arm for that GPU path (whose HF model code is not available here); none of this
+    repository's kernels run in it. (The reference's loop runs the mLSTM step as one fused Triton kernel;
+    here it is several torch kernels.)"""
 
-    m = BolmoDecoder(device=device, seed=seed)
-    m.capture()
+    def __init__(self, m):
+        import torch.nn.functional as F
+
+        self.F, self.m, self.dev = F, m, m.device
+        self.d, self.vocab = m.d, m.vocab
+        blk = m.blocks[0]
+        self.nh, self.hd = blk.nh, blk.d // blk.nh
+        self.max_pos = m.max_patches
+        z = dict(dtype=torch.bfloat16, device=self.dev)
+        self.kc = [torch.zeros(1, self.nh, self.max_pos, self.hd, **z) for _ in m.blocks]
+        self.vc = [torch.zeros(1, self.nh, self.max_pos, self.hd, **z) for _ in m.blocks]
+        self.states = {}
+        for name, L in (("enc", m.enc), ("dec", m.dec)):
+            f32 = dict(dtype=torch.float32, device=self.dev)
+            self.states[name] = (torch.zeros(L.nh, L.dh, L.dh, **f32), torch.zeros(L.nh, L.dh, **f32),
+                                 torch.zeros(L.nh, **f32))
+        self.cos, self.sin = m.cos, m.sin
+        self.slots = torch.arange(self.max_pos, device=self.dev)
+        self.byte = torch.zeros(1, dtype=torch.long, device=self.dev)
+        self.pos = torch.zeros(1, dtype=torch.long, device=self.dev)
+        self.e = torch.zeros(1, self.d, **z)
+        self.patch = torch.zeros(1, self.d, **z)
+        self.value = torch.zeros(1, self.d, **z)
+        self.bl = torch.zeros(1, 1, dtype=torch.float32, device=self.dev)
+        self.out = torch.zeros(2, dtype=torch.long, device=self.dev)
+        self.graphs: dict[str, torch.cuda.CUDAGraph] = {}
+        self.patches = 0
+        self._pin_byte = torch.zeros(1, dtype=torch.long).pin_memory()
+        self._pin_out = torch.zeros(2, dtype=torch.long).pin_memory()
+
+    @staticmethod
+    def rms(x, w, eps=1e-6):
+        xf = x.float()
+        xf = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+        return w * xf.to(x.dtype)
+
+    def local(self, L, state, h):
+        F, d, nh, dh = self.F, self.d, L.nh, L.dh
+        x = self.rms(h, L.norm1)
+        y = F.linear(x, L.w_qkvo)
+        g = F.linear(x, L.w_if).float() + L.b_if
+        g = L.gate_cap * torch.tanh(g / L.gate_cap)
+        q, k, v, o = y.split(d, dim=-1)
+        i, f = g[0, :nh], g[0, nh:]
+        c, n, m = state
+        flog = F.logsigmoid(f)
+        m_new = torch.maximum(flog + m, i)
+        fa, ia = torch.exp(flog + m - m_new), torch.exp(i - m_new)
+        qf = q.float().view(nh, dh) * dh ** -0.5
+        kf, vf = k.float().view(nh, dh), v.float().view(nh, dh)
+        c_new = fa[:, None, None] * c + ia[:, None, None] * (kf[:, :, None] * vf[:, None, :])
+        n_new = fa[:, None] * n + ia[:, None] * kf
+        num = torch.einsum("hd,hde->he", qf, c_new)
+        den = torch.maximum((qf * n_new).sum(-1).abs(), torch.exp(-m_new)) + L.mlstm_eps
+        hh = (num / den[:, None]).to(torch.bfloat16)
+        c.copy_(c_new)
+        n.copy_(n_new)
+        m.copy_(m_new)
+        hn = self.rms(hh, L.mh_norm).reshape(1, d)
+        h2 = h + F.linear(torch.sigmoid(o) * hn, L.w_out)
+        gu = F.linear(self.rms(h2, L.norm2), L.w_gu)
+        return h2 + F.linear(F.silu(gu[:, :L.ffn]) * gu[:, L.ffn:], L.w_down)
+
+    def glob_block(self, i, b, x):
+        F, nh, hd = self.F, self.nh, self.hd
+        y = F.linear(x, b.w_qkv)
+        q, k, v = y.split(self.d, dim=-1)
+        q, k = self.rms(q, b.q_norm).view(1, nh, 1, hd), self.rms(k, b.k_norm).view(1, nh, 1, hd)
+        cos, sin = self.cos.index_select(0, self.pos), self.sin.index_select(0, self.pos)
+        cos, sin = torch.cat([cos, cos], -1).to(torch.bfloat16), torch.cat([sin, sin], -1).to(torch.bfloat16)
+
+        def rot(t):
+            return torch.cat([-t[..., hd // 2:], t[..., :hd // 2]], dim=-1)
+
+        q, k = q * cos + rot(q) * sin, k * cos + rot(k) * sin
+        self.kc[i].index_copy_(2, self.pos, k)
+        self.vc[i].index_copy_(2, self.pos, v.view(1, nh, 1, hd))
+        mask = (self.slots <= self.pos).view(1, 1, 1, -1)
+        att = F.scaled_dot_product_attention(q, self.kc[i], self.vc[i], attn_mask=mask).reshape(1, self.d)
+        h = x + self.rms(F.linear(att, b.w_o), b.attn_norm)
+        gu = F.linear(h, b.w_gu)
+        return h + self.rms(F.linear(F.silu(gu[:, :b.ffn]) * gu[:, b.ffn:], b.w_down), b.mlp_norm)
+
+    def enc_step(self):
+        m = self.m
+        h = m.embed.index_select(0, self.byte)
+        e = self.rms(self.local(m.enc, self.states["enc"], h), m.enc_norm)
+        self.e.copy_(e)
+        self.patch.copy_(self.F.linear(e, m.w_patch))
+        self.bl.copy_(self.F.linear(e, m.w_boundary).float())
+
+    def glob_step(self):
+        x = self.patch
+        for i, b in enumerate(self.m.blocks):
+            x = self.glob_block(i, b, x)
+        self.value.copy_(self.rms(x, self.m.dec_in_norm))
+        self.pos.add_(1)
+
+    def dec_step(self):
+        m = self.m
+        h = self.F.linear(self.e, m.w_in) + self.value
+        logits = self.F.linear(self.rms(self.local(m.dec, self.states["dec"], h), m.final_norm), m.lm_head).float()
+        self.out[0:1].copy_(torch.argmax(logits, dim=-1))
+        self.out[1:2].copy_((torch.sigmoid(self.bl) >= 0.5).view(1).long())
+
+    def reset(self):
+        for st in self.states.values():
+            for t in st:
+                t.zero_()
+        for t in self.kc + self.vc:
+            t.zero_()
+        self.pos.zero_()
+        self.value.zero_()
+        self.patches = 0
+
+    def capture(self):
+        pieces = (("enc0", self.enc_step), ("glob", self.glob_step), ("dec0", self.dec_step))
+        s_ = torch.cuda.Stream()
+        s_.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s_):
+            for _, fn in pieces:
+                fn()
+        torch.cuda.current_stream().wait_stream(s_)
+        for name, fn in pieces:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                fn()
+            self.graphs[name] = g
+        torch.cuda.synchronize()
+        self.reset()
+
+    def feed(self, b, new_patch):
+        self._pin_byte[0] = b
+        self.byte.copy_(self._pin_byte, non_blocking=True)
+        self.graphs["enc0"].replay()
+        if new_patch:
+            self.graphs["glob"].replay()
+            self.patches += 1
+        self.graphs["dec0"].replay()
+        self._pin_out.copy_(self.out, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        return int(self._pin_out[0]), bool(self._pin_out[1])
+
+
+def _time_decode(m, seed: int, reps: int, replay: list | None = None) -> dict:
+    """Prompt of 256 random bytes fed byte by byte, then 511 greedy steps timed on the wall clock (each
+    step ends with its host synchronisation); then each graph replayed alone for its device time.
+    `replay` = another run's (byte, opens a patch) sequence to feed instead of this model's own greedy
+    choices, so that two implementations do exactly the same work."""
     prompt = torch.randint(0, 256, (DECODE_PROMPT,), generator=torch.Generator().manual_seed(seed)).tolist()
     m.reset()
-    tok, new_patch = 0, True
-    for b in prompt:
+    tok, new_patch, fed = 0, True, []
+    for i, b in enumerate(prompt):
+        if replay is not None:
+            b, new_patch = replay[i]
+        fed.append((b, new_patch))
         tok, new_patch = m.feed(b, new_patch)
     prompt_patches = m.patches
     torch.cuda.synchronize()
+    gen = [tok]
     t0 = time.perf_counter()
-    for _ in range(DECODE_NEW - 1):
+    for i in range(DECODE_NEW - 1):
+        if replay is not None:
+            tok, new_patch = replay[DECODE_PROMPT + i]
+        fed.append((tok, new_patch))
         tok, new_patch = m.feed(tok, new_patch)
+        gen.append(tok)
     wall = time.perf_counter() - t0
-    gen_patches = m.patches - prompt_patches
-    w = m.weights()
-    local_bytes = sum(t.numel() * t.element_size() for k, t in w.items()
-                      if not k.startswith("glob") and k != "embed") + 2 * m.d  # + the embedding row
-    glob_bytes = sum(t.numel() * t.element_size() for k, t in w.items() if k.startswith("glob"))
     per = {}
     for name in ("enc0", "dec0", "glob"):
         g = m.graphs[name]
         time_graph_replays(g, 2)
         per[name] = round(time_graph_replays(g, reps) * 1e3 / reps, 2)
+    return {"wall": wall, "gen_patches": m.patches - prompt_patches, "prompt_patches": prompt_patches,
+            "device_us": per, "tokens": gen, "fed": fed}
+
+
+def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 20) -> dict:
+    """greedy decoding of the random-init Bolmo-1B-shaped byte model, batch 1, on this
+    repository's kernels, and the same model and loop on stock PyTorch ops (TorchDecoder) beside it."""
+    from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+
+    m = BolmoDecoder(device=device, seed=seed)
+    m.capture()
+    ours = _time_decode(m, seed, reps)
+    w = m.weights()
+    local_bytes = sum(t.numel() * t.element_size() for k, t in w.items()
+                      if not k.startswith("glob") and k != "embed") + 2 * m.d  # + the embedding row
+    glob_bytes = sum(t.numel() * t.element_size() for k, t in w.items() if k.startswith("glob"))
     steps = DECODE_NEW - 1
-    streamed = local_bytes * steps + glob_bytes * gen_patches
+    streamed = local_bytes * steps + glob_bytes * ours["gen_patches"]
     out = {
-        "bytes_per_s": round(steps / wall, 1), "ms_per_byte": round(wall / steps * 1e3, 4),
-        "generated": DECODE_NEW, "timed_steps": steps, "patches_in_timed_steps": gen_patches,
-        "prompt_patches": prompt_patches, "device_us": per,
+        "bytes_per_s": round(steps / ours["wall"], 1), "ms_per_byte": round(ours["wall"] / steps * 1e3, 4),
+        "generated": DECODE_NEW, "timed_steps": steps, "patches_in_timed_steps": ours["gen_patches"],
+        "prompt_patches": ours["prompt_patches"], "device_us": ours["device_us"],
         "weight_bytes": {"local_per_byte": local_bytes, "global_per_patch": glob_bytes},
-        "weight_gbs": round(streamed / wall / 1e9, 1), "frac": round(streamed / wall / 1e9 / peak, 4),
+        "weight_gbs": round(streamed / ours["wall"] / 1e9, 1),
+        "frac": round(streamed / ours["wall"] / 1e9 / peak, 4),
         "graphs_per_byte": "enc + dec, + glob on a patch start; one host sync per byte",
     }
+    try:
+        t = TorchDecoder(m)
+        t.capture()
+        theirs = _time_decode(t, seed, reps, replay=ours["fed"])
+        # the torch arm's prediction at step i is for the byte fed at step i + 1 (teacher forced)
+        pred = theirs["tokens"]
+        agree = sum(a == b for a, b in zip(ours["tokens"], pred))
+        out["torch_path"] = {
+            "bytes_per_s": round(steps / theirs["wall"], 1), "ms_per_byte": round(theirs["wall"] / steps * 1e3, 4),
+            "patches_in_timed_steps": theirs["gen_patches"], "device_us": theirs["device_us"],
+            "greedy_agreement_with_ours": f"{agree}/{len(ours['tokens'])}",
+            "what": "same weights and loop on stock torch ops (cuBLAS F.linear, SDPA, torch RMSNorm, torch mLSTM "
+                    "step), CUDA graphs, one sync per byte; fed our bytes and patch decisions, so both do the "
+                    "same work"}
+        out["speedup_vs_torch_path"] = round(out["bytes_per_s"] / out["torch_path"]["bytes_per_s"], 3)
+        del t
+    except Exception as exc:  # noqa: BLE001 - the comparison arm must not hide our own number
+        out["torch_path"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     del m
     torch.cuda.empty_cache()
     return out
@@ -623,6 +810,26 @@ def run_case(args) -> int:
     return 0
 
 
+def run_decode_short(args) -> int:
+    """N bytes through the decode graphs, each opening a patch, with the device time of each piece."""
+    from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+
+    device = torch.device("cuda", 0)
+    m = BolmoDecoder(device=device, seed=0)
+    m.capture()
+    m.reset()
+    m.pos.fill_(args.decode_pos)
+    m.patches = args.decode_pos
+    for i in range(args.decode):
+        m.feed(65 + i % 26, True)
+    torch.cuda.synchronize()
+    per = {}
+    for name in ("enc0", "dec0", "glob"):
+        per[name] = round(time_graph_replays(m.graphs[name], 5) * 1e3 / 5, 2)
+    print(json.dumps({"decode_bytes": args.decode, "start_pos": args.decode_pos, "device_us": per}), flush=True)
+    return 0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -632,6 +839,10 @@ def main(argv=None) -> int:
     ap.add_argument("--quick", action="store_true", help="skip the per-cell, int8, scan and CPU passes")
     ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8|int4]: time one sweep cell alone (ncu captures)")
     ap.add_argument("--graph", action="store_true", help="with --case: time a CUDA graph of the weight ring")
+    ap.add_argument("--decode", type=int, default=0, metavar="N",
+                    help="only N bytes of the Bolmo-shaped decode, each opening a patch (short runs for ncu)")
+    ap.add_argument("--decode-pos", type=int, default=0, metavar="P",
+                    help="with --decode: start at patch position P (attention over P cached positions)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -639,6 +850,8 @@ def main(argv=None) -> int:
         return run_reference(args)
     if args.case:
         return run_case(args)
+    if args.decode:
+        return run_decode_short(args)
     return run_ours(args)
 
 

@@ -39,9 +39,8 @@ _SIGNATURES = {
     "bp_swiglu": (c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int, c_void_p]),
     "bp_gate_softcap": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_longlong, c_int, c_int, c_float,
                                 c_void_p]),
-    "bp_decode_attention_workspace_bytes": (c_size_t, [c_int, c_int]),
     "bp_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                    c_void_p, c_int, c_int, c_int, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+                                    c_void_p, c_int, c_int, c_int, c_float, c_float, c_void_p]),
     "bp_decode_finish": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "bp_mlstm_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                               c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -1,12 +1,13 @@
 // Glue kernels of the batch-1 byte decoder (a Bolmo-shaped model: mLSTM local layers around an
 // OLMo-2 global model), each replacing a chain of small framework ops by one launch:
 //   * bp_rmsnorm_ex   RMSNorm fused with the residual add that precedes it (pre-norm layers), the one
-//                     that follows it (OLMo-2's norm-after blocks) or the mLSTM output gate;
+//                     that follows it (OLMo-2's norm-after blocks) or the mLSTM output gate; bp_rmsnorm
+//                     is its plain mode;
 //   * bp_swiglu       silu(gate) * up of a SwiGLU MLP;
 //   * bp_gate_softcap cap * tanh((g + bias) / cap) of the mLSTM input / forget gate pre-activations;
 //   * bp_decode_attention  one query position against a static KV cache: RMSNorm of q and k over the
 //                     model width, rotary embedding, the cache write of k and v, and the attention
-//                     split over 64-position chunks with a deterministic last-arriver combine;
+//                     split over a cluster of 8 CTAs per head, merged through distributed shared memory;
 //   * bp_decode_finish the step's greedy argmax and boundary flag in one int64 pair.
 // Reference: the per-byte pieces of byteprof's minimal Bolmo loop (byteprof/optim/bolmo.py:32-136,
 // byteprof/optim/bolmo_loop.py:36-64), whose layers run these steps as separate framework ops.
@@ -31,8 +32,6 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<const uint32_t*>(&p);
 }
 
-__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + expf(-v)); }
-
 template <typename Kern, typename... Args>
 cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, cudaStream_t stream, Args... args) {
   cudaLaunchConfig_t cfg = {};
@@ -52,7 +51,14 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, cudaStream_t stream, Ar
 }
 
 // ---- RMSNorm with a fused add or gate ---------------------------------------------------------------
-constexpr int kNormWarps = 8;
+// One team of `team` threads (32 to 256) per row; a CTA holds 256 / team rows. Thread t of a team owns
+// the 8-value chunks t, t + team, ... of its row and keeps up to kNormCache of them in registers, so a
+// 2048-wide row is one 16-byte load per thread, all in flight at once. The sum of squares runs in a
+// fixed order (each thread's chunks in order, a butterfly over the warp, the team's warps in order),
+// so a row's result never depends on how many rows the launch holds. 1 / sqrt is two correctly
+// rounded operations, reproducible on any IEEE machine.
+constexpr int kNormThreads = 256;
+constexpr int kNormCache = 4;
 
 struct NormArgs {
   const __nv_bfloat16* x;
@@ -67,6 +73,7 @@ struct NormArgs {
   long long ldy;
   int rows, cols;
   float eps;
+  int team, iters;
 };
 
 // Row r = g * w_rows + j lives at g * ld + j * cols (w_rows = 1: the usual r * ld).
@@ -74,67 +81,103 @@ __device__ __forceinline__ long long row_off(int r, int w_rows, int cols, long l
   return static_cast<long long>(r / w_rows) * ld + static_cast<long long>(r % w_rows) * cols;
 }
 
-template <int MODE>
-__device__ __forceinline__ void norm_in8(const __nv_bfloat16* xr, const __nv_bfloat16* rr, int c, float (&f)[8]) {
-  const uint4 v = ldg16(xr + c);
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
   f[0] = bf16lo(v.x); f[1] = bf16hi(v.x); f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
   f[4] = bf16lo(v.z); f[5] = bf16hi(v.z); f[6] = bf16lo(v.w); f[7] = bf16hi(v.w);
+}
+
+template <int MODE>
+__device__ __forceinline__ void norm_in8(const __nv_bfloat16* xr, const __nv_bfloat16* rr, int c, float (&f)[8]) {
+  unpack8(ldg16(xr + c), f);
   if (MODE == BP_NORM_ADD_FIRST) {  // the normalised value is the bf16 sum
-    const uint4 u = ldg16(rr + c);
-    const float g[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
-                        bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
+    float g[8];
+    unpack8(ldg16(rr + c), g);
 #pragma unroll
     for (int j = 0; j < 8; ++j) f[j] = round_bf16(__fadd_rn(f[j], g[j]));
   }
 }
 
+// sigmoid evaluated in double precision and rounded once to fp32 (the correctly rounded value in all
+// but rare cases), so that every implementation that does the same gets the same bits.
+__device__ __forceinline__ float sigmoid_d(float v) { return static_cast<float>(1.0 / (1.0 + exp(-static_cast<double>(v)))); }
+
 template <int MODE>
-__global__ void __launch_bounds__(kNormWarps * 32) norm_ex_kernel(NormArgs a) {
+__device__ __forceinline__ void norm_out8(const float (&f)[8], float inv, const __nv_bfloat16* wr,
+                                          const __nv_bfloat16* rr, __nv_bfloat16* sr, __nv_bfloat16* yr, int c) {
+  float wv[8], o[8];
+  unpack8(ldg16(wr + c), wv);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], inv), wv[j]);  // bf16(x * inv * w) below
+  if (MODE == BP_NORM_ADD_AFTER || MODE == BP_NORM_GATE) {
+    float e[8];
+    unpack8(ldg16(rr + c), e);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float nb = round_bf16(o[j]);
+      o[j] = MODE == BP_NORM_ADD_AFTER ? __fadd_rn(e[j], nb) : __fmul_rn(round_bf16(sigmoid_d(e[j])), nb);
+    }
+  }
+  if (sr != nullptr)
+    *reinterpret_cast<uint4*>(sr + c) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                                   pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  *reinterpret_cast<uint4*>(yr + c) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
+                                                 pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+}
+
+template <int MODE, bool kCached>
+__global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs a) {
+  __shared__ float red[kNormThreads / 32];
   pdl_launch_dependents();
   pdl_wait_prior_grids();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int r = blockIdx.x * kNormWarps + warp;
-  if (r >= a.rows) return;
-  const __nv_bfloat16* wr = a.w + static_cast<long long>(r % a.w_rows) * a.cols;
-  const __nv_bfloat16* xr = a.x + row_off(r, a.w_rows, a.cols, a.ldx);
-  const __nv_bfloat16* rr = MODE == BP_NORM_PLAIN ? nullptr : a.res + row_off(r, a.w_rows, a.cols, a.ldres);
-  __nv_bfloat16* yr = a.y + row_off(r, a.w_rows, a.cols, a.ldy);
-  __nv_bfloat16* sr = (MODE == BP_NORM_ADD_FIRST && a.s_out != nullptr) ? a.s_out + row_off(r, a.w_rows, a.cols, a.lds)
-                                                                        : nullptr;
+  const int team = a.team, warps = team / 32;
+  const int t = threadIdx.x % team, slot = threadIdx.x / team;
+  const int r = blockIdx.x * (kNormThreads / team) + slot;
+  const bool live = r < a.rows;
+  const int rc = live ? r : a.rows - 1;  // rows past the end read the last row and store nothing
+  const __nv_bfloat16* wr = a.w + static_cast<long long>(rc % a.w_rows) * a.cols;
+  const __nv_bfloat16* xr = a.x + row_off(rc, a.w_rows, a.cols, a.ldx);
+  const __nv_bfloat16* rr = MODE == BP_NORM_PLAIN ? nullptr : a.res + row_off(rc, a.w_rows, a.cols, a.ldres);
+  float f[kCached ? kNormCache : 1][8];
   float ss = 0.0f;
-  for (int c = lane * 8; c < a.cols; c += 32 * 8) {  // the same per-lane order as bp_rmsnorm
-    float f[8];
-    norm_in8<MODE>(xr, rr, c, f);
+  if (kCached) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+    for (int i = 0; i < kNormCache; ++i) {
+      const int c = (t + i * team) * 8;
+      if (i < a.iters && c < a.cols) {
+        norm_in8<MODE>(xr, rr, c, f[i]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ss = fmaf(f[i][j], f[i][j], ss);
+      }
+    }
+  } else {
+    for (int c = t * 8; c < a.cols; c += team * 8) {
+      norm_in8<MODE>(xr, rr, c, f[0]);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss = fmaf(f[0][j], f[0][j], ss);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFull, ss, o);
-  const float inv = rsqrtf(ss / static_cast<float>(a.cols) + a.eps);
-  for (int c = lane * 8; c < a.cols; c += 32 * 8) {
-    float f[8];
-    norm_in8<MODE>(xr, rr, c, f);
-    const uint4 g = ldg16(wr + c);
-    const float wv[8] = {bf16lo(g.x), bf16hi(g.x), bf16lo(g.y), bf16hi(g.y),
-                         bf16lo(g.z), bf16hi(g.z), bf16lo(g.w), bf16hi(g.w)};
-    float o[8];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.0f;
+  for (int w = 0; w < warps; ++w) tot += red[slot * warps + w];
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(a.cols)), a.eps)));
+  if (!live) return;
+  __nv_bfloat16* yr = a.y + row_off(r, a.w_rows, a.cols, a.ldy);
+  __nv_bfloat16* sr = (MODE == BP_NORM_ADD_FIRST && a.s_out != nullptr) ? a.s_out + row_off(r, a.w_rows, a.cols, a.lds)
+                                                                        : nullptr;
+  if (kCached) {
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], inv), wv[j]);  // bf16(x * inv * w) below
-    if (MODE == BP_NORM_ADD_AFTER || MODE == BP_NORM_GATE) {
-      const uint4 u = ldg16(rr + c);
-      const float e[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
-                          bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float nb = round_bf16(o[j]);
-        o[j] = MODE == BP_NORM_ADD_AFTER ? __fadd_rn(e[j], nb) : __fmul_rn(round_bf16(sigmoid_f(e[j])), nb);
-      }
+    for (int i = 0; i < kNormCache; ++i) {
+      const int c = (t + i * team) * 8;
+      if (i < a.iters && c < a.cols) norm_out8<MODE>(f[i], inv, wr, rr, sr, yr, c);
     }
-    if (sr != nullptr)
-      *reinterpret_cast<uint4*>(sr + c) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                                     pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
-    *reinterpret_cast<uint4*>(yr + c) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                                   pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  } else {
+    for (int c = t * 8; c < a.cols; c += team * 8) {
+      norm_in8<MODE>(xr, rr, c, f[0]);
+      norm_out8<MODE>(f[0], inv, wr, rr, sr, yr, c);
+    }
   }
 }
 
@@ -153,7 +196,8 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __rest
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
     const float g0 = bf16lo(gv[q]), g1 = bf16hi(gv[q]);
-    const float s0 = round_bf16(g0 / (1.0f + expf(-g0))), s1 = round_bf16(g1 / (1.0f + expf(-g1)));
+    const float s0 = round_bf16(static_cast<float>(g0 / (1.0 + exp(-static_cast<double>(g0)))));
+    const float s1 = round_bf16(static_cast<float>(g1 / (1.0 + exp(-static_cast<double>(g1)))));
     o[q] = pack_bf16x2(__fmul_rn(s0, bf16lo(uv[q])), __fmul_rn(s1, bf16hi(uv[q])));
   }
   *reinterpret_cast<uint4*>(out + static_cast<long long>(r) * ldo + j) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -168,15 +212,22 @@ __global__ void __launch_bounds__(256) softcap_kernel(const float* g, long long 
   if (i >= rows * n) return;
   const int r = i / n, c = i % n;
   const float t = __fadd_rn(g[static_cast<long long>(r) * ldg + c], bias != nullptr ? bias[c] : 0.0f);
-  out[static_cast<long long>(r) * ldo + c] = __fmul_rn(cap, tanhf(__fdiv_rn(t, cap)));
+  out[static_cast<long long>(r) * ldo + c] = __fmul_rn(cap, static_cast<float>(tanh(static_cast<double>(__fdiv_rn(t, cap)))));
 }
 
 // ---- single-position attention over a static KV cache -------------------------------------------------
+// One thread-block cluster of 8 CTAs per head. CTA `rank` of head h takes positions rank * 128 .. +127 of
+// every 1024-position round (warp w: 16 of them; lane: 4 of the 128 dims), keeps a running softmax (max,
+// sum, unnormalised output) per warp, merges its 8 warps in shared memory and pushes the CTA's partial
+// into slot `rank` of the leader CTA's shared memory (distributed shared memory); after one cluster
+// barrier the leader merges the 8 slots in rank order (deterministic) and writes the head's output.
 constexpr int kHd = 128;        // head dim
-constexpr int kChunk = 64;      // positions per CTA
-constexpr int kPerWarp = 16;    // positions per warp
-constexpr int kAttnThreads = 128;
-static_assert(kChunk == kPerWarp * kAttnThreads / 32, "chunk = 4 warps x 16 positions");
+constexpr int kPerWarp = 16;    // positions per warp and round
+constexpr int kAttnWarps = 8;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kCtaSpan = kAttnWarps * kPerWarp;   // 128 positions per CTA and round
+constexpr int kAttnCluster = 8;                    // CTAs per head
+constexpr int kRound = kAttnCluster * kCtaSpan;    // 1024 positions per round
 
 struct AttnArgs {
   const __nv_bfloat16* qkv;  // [3 * nh * kHd]: q | k | v of the current position
@@ -188,120 +239,190 @@ struct AttnArgs {
   __nv_bfloat16* kc;         // [max_pos, nh, kHd]
   __nv_bfloat16* vc;
   __nv_bfloat16* out;        // [nh * kHd]
-  float* part;               // [nh][max_chunks][kHd + 2]: chunk max, sum, unnormalised output
-  unsigned* counters;        // [nh], zero between launches
-  int nh, max_pos, max_chunks;
+  int nh, max_pos;
   float eps, scale;
 };
 
-__device__ __forceinline__ float block_sum4(float v, float* red) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  return ((red[0] + red[1]) + red[2]) + red[3];
+
+__device__ __forceinline__ float inv_rms(float sum_sq, int n, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum_sq, static_cast<float>(n)), eps)));
 }
 
-__global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(AttnArgs a) {
+__device__ __forceinline__ void load_rows(const AttnArgs& a, long long base, long long p, int h, int lane,
+                                          uint2 (&kk)[kPerWarp], uint2 (&vv)[kPerWarp]) {
+#pragma unroll
+  for (int j = 0; j < kPerWarp; ++j) {
+    kk[j] = make_uint2(0u, 0u);
+    vv[j] = make_uint2(0u, 0u);
+    if (base + j < p) {  // rows below p were written by earlier launches; row p comes from this CTA
+      const long long off = ((base + j) * a.nh + h) * kHd + lane * 4;
+      kk[j] = __ldg(reinterpret_cast<const uint2*>(a.kc + off));
+      vv[j] = __ldg(reinterpret_cast<const uint2*>(a.vc + off));
+    }
+  }
+}
+
+__global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThreads)
+    decode_attention_kernel(AttnArgs a) {
+  constexpr int kHalf = kHd / 2;
   __shared__ __align__(16) float qs[kHd];
-  __shared__ float red[2][4];
-  __shared__ float wm[4], wl[4];
-  __shared__ __align__(16) float wo[4][kHd];
-  __shared__ int is_last;
+  __shared__ __align__(16) float ks[kHd];  // position p's rotated k (bf16 values) and v, owner CTA only
+  __shared__ __align__(16) float vs[kHd];
+  __shared__ float red[2][kAttnWarps];
+  __shared__ float wm[kAttnWarps], wl[kAttnWarps];
+  __shared__ __align__(16) float wo[kAttnWarps][kHd];
+  __shared__ float cm[kAttnCluster], cl[kAttnCluster];  // the leader's slots, one per CTA of the cluster
+  __shared__ __align__(16) float co[kAttnCluster][kHd];
   pdl_launch_dependents();
   pdl_wait_prior_grids();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int chunk = blockIdx.x, h = blockIdx.y;
+  const int rank = static_cast<int>(cluster_ctarank()), h = blockIdx.y;
   const long long p = *a.pos;
-  if (p < 0 || p >= a.max_pos) {  // host-side checks keep p in range; never index with a bad one
-    if (chunk == 0) a.out[h * kHd + tid] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
+  if (p < 0 || p >= a.max_pos) {  // the same p for the whole cluster: every CTA leaves here together
+    if (rank == 0 && tid < kHd) a.out[h * kHd + tid] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
     return;
   }
-  const int nchunks = static_cast<int>(p / kChunk) + 1;
-  if (chunk >= nchunks) return;
-  const bool own = chunk == nchunks - 1;  // this CTA's range holds position p
+  const int rounds = static_cast<int>(p / kRound) + 1;
+  const bool own = static_cast<int>((p % kRound) / kCtaSpan) == rank;  // this CTA's range holds p
   const int d = a.nh * kHd;
   const __nv_bfloat16* q = a.qkv;
   const __nv_bfloat16* k = a.qkv + d;
   const __nv_bfloat16* v = a.qkv + 2 * d;
 
+  // Everything that depends only on p is requested first: round 0's cached rows of this warp, the
+  // rotary factors, this head's q / k / v values and norm weights, the q and k vectors for the norms.
+  uint2 kk[kPerWarp], vv[kPerWarp];
+  load_rows(a, static_cast<long long>(rank) * kCtaSpan + warp * kPerWarp, p, h, lane, kk, vv);
+  const int hi = h * kHd + (tid % kHalf);
+  float cs = 0.0f, sn = 0.0f, qa = 0.0f, qb = 0.0f, qwa = 0.0f, qwb = 0.0f, ka = 0.0f, kb = 0.0f, kwa = 0.0f, kwb = 0.0f;
+  float va = 0.0f, vb = 0.0f;
+  if (tid < kHalf) {
+    cs = a.cos_t[p * kHalf + tid];
+    sn = a.sin_t[p * kHalf + tid];
+    qa = __bfloat162float(q[hi]);
+    qb = __bfloat162float(q[hi + kHalf]);
+    qwa = __bfloat162float(a.qw[hi]);
+    qwb = __bfloat162float(a.qw[hi + kHalf]);
+    if (own) {
+      ka = __bfloat162float(k[hi]);
+      kb = __bfloat162float(k[hi + kHalf]);
+      kwa = __bfloat162float(a.kw[hi]);
+      kwb = __bfloat162float(a.kw[hi + kHalf]);
+    }
+  } else if (own && tid < kHd) {
+    const int j = (tid - kHalf) * 2;
+    va = __bfloat162float(v[h * kHd + j]);
+    vb = __bfloat162float(v[h * kHd + j + 1]);
+  }
   float sq = 0.0f, sk = 0.0f;
   for (int c = tid * 8; c < d; c += kAttnThreads * 8) {
-    const uint4 qv = ldg16(q + c), kv = ldg16(k + c);
-    const uint32_t qa[4] = {qv.x, qv.y, qv.z, qv.w}, ka[4] = {kv.x, kv.y, kv.z, kv.w};
+    float fq[8], fk[8];
+    unpack8(ldg16(q + c), fq);
+    unpack8(ldg16(k + c), fk);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      sq = fmaf(bf16lo(qa[j]), bf16lo(qa[j]), sq);
-      sq = fmaf(bf16hi(qa[j]), bf16hi(qa[j]), sq);
-      sk = fmaf(bf16lo(ka[j]), bf16lo(ka[j]), sk);
-      sk = fmaf(bf16hi(ka[j]), bf16hi(ka[j]), sk);
+    for (int j = 0; j < 8; ++j) {
+      sq = fmaf(fq[j], fq[j], sq);
+      sk = fmaf(fk[j], fk[j], sk);
     }
   }
-  const float tq = block_sum4(sq, red[0]);
-  const float tk = block_sum4(sk, red[1]);
-  const float inv_q = rsqrtf(tq / static_cast<float>(d) + a.eps);
-  const float inv_k = rsqrtf(tk / static_cast<float>(d) + a.eps);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sq += __shfl_xor_sync(kFull, sq, o);
+    sk += __shfl_xor_sync(kFull, sk, o);
+  }
+  if (lane == 0) {
+    red[0][warp] = sq;
+    red[1][warp] = sk;
+  }
+  __syncthreads();
+  float tq = 0.0f, tk = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kAttnWarps; ++w) {
+    tq += red[0][w];
+    tk += red[1][w];
+  }
+  const float inv_q = inv_rms(tq, d, a.eps), inv_k = inv_rms(tk, d, a.eps);
   const long long slot = p * a.nh + h;  // cache row of (p, h)
-  if (tid < kHd / 2) {
-    const int i0 = h * kHd + tid, i1 = i0 + kHd / 2;
-    const float cs = a.cos_t[p * (kHd / 2) + tid], sn = a.sin_t[p * (kHd / 2) + tid];
-    const float q0 = round_bf16(__fmul_rn(__fmul_rn(__bfloat162float(q[i0]), inv_q), __bfloat162float(a.qw[i0])));
-    const float q1 = round_bf16(__fmul_rn(__fmul_rn(__bfloat162float(q[i1]), inv_q), __bfloat162float(a.qw[i1])));
+  if (tid < kHalf) {
+    const float q0 = round_bf16(__fmul_rn(__fmul_rn(qa, inv_q), qwa));
+    const float q1 = round_bf16(__fmul_rn(__fmul_rn(qb, inv_q), qwb));
     qs[tid] = __fsub_rn(__fmul_rn(q0, cs), __fmul_rn(q1, sn));
-    qs[tid + kHd / 2] = __fadd_rn(__fmul_rn(q1, cs), __fmul_rn(q0, sn));
+    qs[tid + kHalf] = __fadd_rn(__fmul_rn(q1, cs), __fmul_rn(q0, sn));
     if (own) {
-      const float k0 = round_bf16(__fmul_rn(__fmul_rn(__bfloat162float(k[i0]), inv_k), __bfloat162float(a.kw[i0])));
-      const float k1 = round_bf16(__fmul_rn(__fmul_rn(__bfloat162float(k[i1]), inv_k), __bfloat162float(a.kw[i1])));
-      a.kc[slot * kHd + tid] = __float2bfloat16_rn(__fsub_rn(__fmul_rn(k0, cs), __fmul_rn(k1, sn)));
-      a.kc[slot * kHd + tid + kHd / 2] = __float2bfloat16_rn(__fadd_rn(__fmul_rn(k1, cs), __fmul_rn(k0, sn)));
+      const float k0 = round_bf16(__fmul_rn(__fmul_rn(ka, inv_k), kwa));
+      const float k1 = round_bf16(__fmul_rn(__fmul_rn(kb, inv_k), kwb));
+      const __nv_bfloat16 r0 = __float2bfloat16_rn(__fsub_rn(__fmul_rn(k0, cs), __fmul_rn(k1, sn)));
+      const __nv_bfloat16 r1 = __float2bfloat16_rn(__fadd_rn(__fmul_rn(k1, cs), __fmul_rn(k0, sn)));
+      a.kc[slot * kHd + tid] = r0;
+      a.kc[slot * kHd + tid + kHalf] = r1;
+      ks[tid] = __bfloat162float(r0);
+      ks[tid + kHalf] = __bfloat162float(r1);
     }
-  } else if (own) {
-    const int j = (tid - kHd / 2) * 2;
-    a.vc[slot * kHd + j] = v[h * kHd + j];
-    a.vc[slot * kHd + j + 1] = v[h * kHd + j + 1];
+  } else if (own && tid < kHd) {
+    const int j = (tid - kHalf) * 2;
+    a.vc[slot * kHd + j] = __float2bfloat16_rn(va);
+    a.vc[slot * kHd + j + 1] = __float2bfloat16_rn(vb);
+    vs[j] = va;
+    vs[j + 1] = vb;
   }
-  __syncthreads();  // qs, and this CTA's cache writes, visible to the whole CTA
+  __syncthreads();  // qs (and ks, vs) visible to the whole CTA
 
-  // Scores: warp w takes positions base .. base + 15; lane holds dims 4 * lane .. 4 * lane + 3.
-  // Plain loads: the cache row of p was written by this CTA in this launch.
-  const long long base = static_cast<long long>(chunk) * kChunk + warp * kPerWarp;
   const float4 qv = *reinterpret_cast<const float4*>(&qs[lane * 4]);
-  float sc[kPerWarp];
+  float mw = -INFINITY, lw = 0.0f, o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int r = 0; r < rounds; ++r) {
+    const long long base = static_cast<long long>(r) * kRound + rank * kCtaSpan + warp * kPerWarp;
+    if (r > 0) load_rows(a, base, p, h, lane, kk, vv);
+    float sc[kPerWarp];
 #pragma unroll
-  for (int j = 0; j < kPerWarp; ++j) {
-    float dot = 0.0f;
-    if (base + j <= p) {
-      const uint2 kk = *reinterpret_cast<const uint2*>(a.kc + ((base + j) * a.nh + h) * kHd + lane * 4);
-      dot = __fmul_rn(qv.x, bf16lo(kk.x));
-      dot = fmaf(qv.y, bf16hi(kk.x), dot);
-      dot = fmaf(qv.z, bf16lo(kk.y), dot);
-      dot = fmaf(qv.w, bf16hi(kk.y), dot);
+    for (int j = 0; j < kPerWarp; ++j) {
+      float k4[4];
+      if (base + j == p) {
+        const float4 t = *reinterpret_cast<const float4*>(&ks[lane * 4]);
+        k4[0] = t.x; k4[1] = t.y; k4[2] = t.z; k4[3] = t.w;
+      } else {
+        k4[0] = bf16lo(kk[j].x); k4[1] = bf16hi(kk[j].x); k4[2] = bf16lo(kk[j].y); k4[3] = bf16hi(kk[j].y);
+      }
+      float dot = __fmul_rn(qv.x, k4[0]);
+      dot = fmaf(qv.y, k4[1], dot);
+      dot = fmaf(qv.z, k4[2], dot);
+      dot = fmaf(qv.w, k4[3], dot);
+      sc[j] = dot;
     }
-    sc[j] = dot;
-  }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
+    for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-    for (int j = 0; j < kPerWarp; ++j) sc[j] += __shfl_xor_sync(kFull, sc[j], o);
-  float mw = -INFINITY;
+      for (int j = 0; j < kPerWarp; ++j) sc[j] += __shfl_xor_sync(kFull, sc[j], o);
+    float mr = -INFINITY;
 #pragma unroll
-  for (int j = 0; j < kPerWarp; ++j) {
-    sc[j] = base + j <= p ? sc[j] * a.scale : -INFINITY;
-    mw = fmaxf(mw, sc[j]);
-  }
-  float lw = 0.0f, o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  if (mw != -INFINITY) {
+    for (int j = 0; j < kPerWarp; ++j) {
+      sc[j] = base + j <= p ? __fmul_rn(sc[j], a.scale) : -INFINITY;
+      mr = fmaxf(mr, sc[j]);
+    }
+    if (mr == -INFINITY) continue;  // no position of this round is at or below p (warp-uniform)
+    const float m_new = fmaxf(mw, mr);
+    if (mw != -INFINITY) {  // rescale what earlier rounds accumulated
+      const float f = expf(__fsub_rn(mw, m_new));
+      lw = __fmul_rn(lw, f);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o4[c] = __fmul_rn(o4[c], f);
+    }
+    mw = m_new;
+    float e[kPerWarp];
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) e[j] = base + j <= p ? expf(__fsub_rn(sc[j], mw)) : 0.0f;
 #pragma unroll
     for (int j = 0; j < kPerWarp; ++j) {
       if (base + j > p) continue;
-      const float e = expf(sc[j] - mw);
-      lw += e;
-      const uint2 vv = *reinterpret_cast<const uint2*>(a.vc + ((base + j) * a.nh + h) * kHd + lane * 4);
-      o4[0] = fmaf(e, bf16lo(vv.x), o4[0]);
-      o4[1] = fmaf(e, bf16hi(vv.x), o4[1]);
-      o4[2] = fmaf(e, bf16lo(vv.y), o4[2]);
-      o4[3] = fmaf(e, bf16hi(vv.y), o4[3]);
+      lw = __fadd_rn(lw, e[j]);
+      float v4[4];
+      if (base + j == p) {
+        const float4 t = *reinterpret_cast<const float4*>(&vs[lane * 4]);
+        v4[0] = t.x; v4[1] = t.y; v4[2] = t.z; v4[3] = t.w;
+      } else {
+        v4[0] = bf16lo(vv[j].x); v4[1] = bf16hi(vv[j].x); v4[2] = bf16lo(vv[j].y); v4[3] = bf16hi(vv[j].y);
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) o4[c] = fmaf(e[j], v4[c], o4[c]);
     }
   }
   if (lane == 0) {
@@ -310,40 +431,40 @@ __global__ void __launch_bounds__(kAttnThreads) decode_attention_kernel(AttnArgs
   }
   *reinterpret_cast<float4*>(&wo[warp][lane * 4]) = make_float4(o4[0], o4[1], o4[2], o4[3]);
   __syncthreads();
-  // Chunk partial (warp 0's first position is chunk * 64 <= p, so the chunk max is finite).
-  const float mc = fmaxf(fmaxf(wm[0], wm[1]), fmaxf(wm[2], wm[3]));
-  float lc = 0.0f, oc = 0.0f;
+  // This CTA's partial (max, sum, output), pushed into slot `rank` of the leader CTA.
+  if (tid < kHd) {
+    float mc = -INFINITY;
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const float f = wm[w] == -INFINITY ? 0.0f : expf(wm[w] - mc);
-    lc = fmaf(wl[w], f, lc);
-    oc = fmaf(wo[w][tid], f, oc);
+    for (int w = 0; w < kAttnWarps; ++w) mc = fmaxf(mc, wm[w]);
+    float lc = 0.0f, oc = 0.0f;
+    if (mc != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float f = wm[w] == -INFINITY ? 0.0f : expf(__fsub_rn(wm[w], mc));
+        lc = fmaf(wl[w], f, lc);
+        oc = fmaf(wo[w][tid], f, oc);
+      }
+    }
+    const uint32_t dst_o = mapa_shared(smem_addr(&co[rank][tid]), 0);
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(dst_o), "f"(oc) : "memory");
+    if (tid == 0) {
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(mapa_shared(smem_addr(&cm[rank]), 0)), "f"(mc) : "memory");
+      asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(mapa_shared(smem_addr(&cl[rank]), 0)), "f"(lc) : "memory");
+    }
   }
-  float* ph = a.part + static_cast<long long>(h) * a.max_chunks * (kHd + 2);
-  float* pc = ph + static_cast<long long>(chunk) * (kHd + 2);
-  pc[2 + tid] = oc;
-  if (tid == 0) {
-    pc[0] = mc;
-    pc[1] = lc;
-  }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(&a.counters[h], 1u) == static_cast<unsigned>(nchunks - 1);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  // The last CTA of head h combines all chunks in chunk order (deterministic).
-  float mg = -INFINITY;
-  for (int c = 0; c < nchunks; ++c) mg = fmaxf(mg, __ldcg(ph + static_cast<long long>(c) * (kHd + 2)));
+  cluster_sync_unaligned();  // every CTA's slot written (release) and visible to the leader (acquire)
+  if (rank != 0 || tid >= kHd) return;
+  float mg = -INFINITY;  // finite: rank 0's first position is 0 <= p
+#pragma unroll
+  for (int c = 0; c < kAttnCluster; ++c) mg = fmaxf(mg, cm[c]);
   float lg = 0.0f, og = 0.0f;
-  for (int c = 0; c < nchunks; ++c) {
-    const float* pp = ph + static_cast<long long>(c) * (kHd + 2);
-    const float f = expf(__ldcg(pp) - mg);
-    lg = fmaf(__ldcg(pp + 1), f, lg);
-    og = fmaf(__ldcg(pp + 2 + tid), f, og);
+#pragma unroll
+  for (int c = 0; c < kAttnCluster; ++c) {
+    const float f = cm[c] == -INFINITY ? 0.0f : expf(__fsub_rn(cm[c], mg));
+    lg = fmaf(cl[c], f, lg);
+    og = fmaf(co[c][tid], f, og);
   }
-  a.out[h * kHd + tid] = __float2bfloat16_rn(og / lg);
-  if (tid == 0) a.counters[h] = 0u;
+  a.out[h * kHd + tid] = __float2bfloat16_rn(__fdiv_rn(og, lg));
 }
 
 // ---- argmax + boundary flag --------------------------------------------------------------------------
@@ -394,7 +515,7 @@ __global__ void __launch_bounds__(kFinishThreads) decode_finish_kernel(const flo
         idx = bi[w];
       }
     out[0] = idx;
-    out[1] = boundary_logit != nullptr && sigmoid_f(*boundary_logit) >= 0.5f ? 1 : 0;
+    out[1] = boundary_logit != nullptr && sigmoid_d(*boundary_logit) >= 0.5f ? 1 : 0;
   }
 }
 
@@ -402,24 +523,38 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 }  // namespace
 
-size_t decode_attention_workspace_bytes(int nh, int max_pos) {
-  const size_t chunks = static_cast<size_t>((max_pos + kChunk - 1) / kChunk);
-  const size_t part = static_cast<size_t>(nh) * chunks * (kHd + 2) * sizeof(float);
-  return ((part + 255) / 256) * 256 + static_cast<size_t>(nh) * sizeof(unsigned);
-}
-
 }  // namespace bp
 
-extern "C" int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_rows, const void* res, long long ldres, void* s_out, long long lds, void* y,
-                             long long ldy, int rows, int cols, float eps, int mode, void* stream) {
+namespace bp {
+namespace {
+
+template <int MODE>
+cudaError_t launch_norm(NormArgs a, cudaStream_t s) {
+  int team = 32;  // threads per row: the power of two (32 to 256) covering cols / 8 chunks
+  while (team < kNormThreads && team * 8 < a.cols) team *= 2;
+  a.team = team;
+  a.iters = (a.cols + team * 8 - 1) / (team * 8);
+  const dim3 grid((a.rows + kNormThreads / team - 1) / (kNormThreads / team)), block(kNormThreads);
+  return a.iters <= kNormCache ? launch_pdl(norm_ex_kernel<MODE, true>, grid, block, s, a)
+                               : launch_pdl(norm_ex_kernel<MODE, false>, grid, block, s, a);
+}
+
+}  // namespace
+}  // namespace bp
+
+extern "C" int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_rows, const void* res, long long ldres,
+                             void* s_out, long long lds, void* y, long long ldy, int rows, int cols, float eps, int mode,
+                             void* stream) {
   using namespace bp;
   clear_error();
-  if (rows < 0 || cols < 0 || w_rows < 1) return fail(BP_ERR_INVALID_ARGUMENT, "bad size (rows=%d cols=%d w_rows=%d)", rows, cols, w_rows);
+  if (rows < 0 || cols < 0 || w_rows < 1)
+    return fail(BP_ERR_INVALID_ARGUMENT, "bad size (rows=%d cols=%d w_rows=%d)", rows, cols, w_rows);
   if (mode < BP_NORM_PLAIN || mode > BP_NORM_GATE) return fail(BP_ERR_INVALID_ARGUMENT, "unknown norm mode %d", mode);
   if (rows == 0 || cols == 0) return BP_OK;
   if (x == nullptr || w == nullptr || y == nullptr || (mode != BP_NORM_PLAIN && res == nullptr))
     return fail(BP_ERR_INVALID_ARGUMENT, "x, w, y (or res for this mode) is NULL");
-  if (s_out != nullptr && mode != BP_NORM_ADD_FIRST) return fail(BP_ERR_INVALID_ARGUMENT, "s_out is written by mode ADD_FIRST only");
+  if (s_out != nullptr && mode != BP_NORM_ADD_FIRST)
+    return fail(BP_ERR_INVALID_ARGUMENT, "s_out is written by mode ADD_FIRST only");
   const long long span = static_cast<long long>(w_rows) * cols;  // a group of rows must fit its stride
   if (ldx < span || ldy < span || (mode != BP_NORM_PLAIN && ldres != 0 && ldres < span) ||
       (s_out != nullptr && lds < span))
@@ -429,19 +564,24 @@ extern "C" int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_
     return fail(BP_ERR_MISALIGNED, "rmsnorm_ex needs 16-byte aligned rows, cols and strides multiples of 8");
   int st = require_sm100();
   if (st != BP_OK) return st;
-  NormArgs a{static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w), w_rows, static_cast<const __nv_bfloat16*>(res), ldres,
-             static_cast<__nv_bfloat16*>(s_out), lds, static_cast<__nv_bfloat16*>(y), ldy, rows, cols, eps};
-  const dim3 grid((rows + kNormWarps - 1) / kNormWarps), block(kNormWarps * 32);
+  NormArgs a{static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w), w_rows,
+             static_cast<const __nv_bfloat16*>(res), ldres, static_cast<__nv_bfloat16*>(s_out), lds,
+             static_cast<__nv_bfloat16*>(y), ldy, rows, cols, eps, 0, 0};
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e;
   switch (mode) {
-    case BP_NORM_PLAIN: e = launch_pdl(norm_ex_kernel<BP_NORM_PLAIN>, grid, block, s, a); break;
-    case BP_NORM_ADD_FIRST: e = launch_pdl(norm_ex_kernel<BP_NORM_ADD_FIRST>, grid, block, s, a); break;
-    case BP_NORM_ADD_AFTER: e = launch_pdl(norm_ex_kernel<BP_NORM_ADD_AFTER>, grid, block, s, a); break;
-    default: e = launch_pdl(norm_ex_kernel<BP_NORM_GATE>, grid, block, s, a); break;
+    case BP_NORM_PLAIN: e = launch_norm<BP_NORM_PLAIN>(a, s); break;
+    case BP_NORM_ADD_FIRST: e = launch_norm<BP_NORM_ADD_FIRST>(a, s); break;
+    case BP_NORM_ADD_AFTER: e = launch_norm<BP_NORM_ADD_AFTER>(a, s); break;
+    default: e = launch_norm<BP_NORM_GATE>(a, s); break;
   }
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "rmsnorm_ex launch: %s", cudaGetErrorString(e));
   return check_launch("rmsnorm_ex");
+}
+
+extern "C" int bp_rmsnorm(const void* x, long long ldx, const void* w, void* y, long long ldy, int rows, int cols,
+                          float eps, void* stream) {
+  return bp_rmsnorm_ex(x, ldx, w, 1, nullptr, 0, nullptr, 0, y, ldy, rows, cols, eps, BP_NORM_PLAIN, stream);
 }
 
 extern "C" int bp_swiglu(const void* gu, long long ldgu, void* out, long long ldo, int rows, int ffn, void* stream) {
@@ -482,38 +622,25 @@ extern "C" int bp_gate_softcap(const float* g, long long ldg, const float* bias,
   return check_launch("gate_softcap");
 }
 
-extern "C" size_t bp_decode_attention_workspace_bytes(int nh, int max_pos) {
-  if (nh < 1 || max_pos < 1) return 0;
-  return bp::decode_attention_workspace_bytes(nh, max_pos);
-}
-
 extern "C" int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos_t,
                                    const float* sin_t, const int64_t* pos, void* k_cache, void* v_cache, void* out,
-                                   int nh, int head_dim, int max_pos, float eps, float scale, void* workspace,
-                                   size_t workspace_bytes, void* stream) {
+                                   int nh, int head_dim, int max_pos, float eps, float scale, void* stream) {
   using namespace bp;
   clear_error();
   if (head_dim != kHd) return fail(BP_ERR_UNSUPPORTED, "decode attention supports head_dim 128 (got %d)", head_dim);
   if (nh < 1 || nh > 65535 || max_pos < 1) return fail(BP_ERR_INVALID_ARGUMENT, "bad nh=%d or max_pos=%d", nh, max_pos);
   if (qkv == nullptr || q_norm_w == nullptr || k_norm_w == nullptr || cos_t == nullptr || sin_t == nullptr ||
-      pos == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr || workspace == nullptr)
+      pos == nullptr || k_cache == nullptr || v_cache == nullptr || out == nullptr)
     return fail(BP_ERR_INVALID_ARGUMENT, "a pointer argument is NULL");
-  if (workspace_bytes < decode_attention_workspace_bytes(nh, max_pos))
-    return fail(BP_ERR_INVALID_ARGUMENT, "workspace too small (%zu < %zu bytes)", workspace_bytes,
-                decode_attention_workspace_bytes(nh, max_pos));
-  if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache) || !aligned16(workspace))
-    return fail(BP_ERR_MISALIGNED, "qkv, the caches and the workspace must be 16-byte aligned");
+  if (!aligned16(qkv) || !aligned16(k_cache) || !aligned16(v_cache))
+    return fail(BP_ERR_MISALIGNED, "qkv and the caches must be 16-byte aligned");
   int st = require_sm100();
   if (st != BP_OK) return st;
-  const int max_chunks = (max_pos + kChunk - 1) / kChunk;
-  const size_t part_bytes = static_cast<size_t>(nh) * max_chunks * (kHd + 2) * sizeof(float);
   AttnArgs a{static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(q_norm_w),
              static_cast<const __nv_bfloat16*>(k_norm_w), cos_t, sin_t, reinterpret_cast<const long long*>(pos),
              static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
-             static_cast<__nv_bfloat16*>(out), static_cast<float*>(workspace),
-             reinterpret_cast<unsigned*>(static_cast<char*>(workspace) + ((part_bytes + 255) / 256) * 256), nh, max_pos,
-             max_chunks, eps, scale};
-  const cudaError_t e = launch_pdl(decode_attention_kernel, dim3(max_chunks, nh), dim3(kAttnThreads),
+             static_cast<__nv_bfloat16*>(out), nh, max_pos, eps, scale};
+  const cudaError_t e = launch_pdl(decode_attention_kernel, dim3(kAttnCluster, nh), dim3(kAttnThreads),
                                    static_cast<cudaStream_t>(stream), a);
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "decode_attention launch: %s", cudaGetErrorString(e));
   return check_launch("decode_attention");

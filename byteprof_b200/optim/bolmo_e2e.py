@@ -39,8 +39,7 @@ def _norm_w(gen, device, *shape):
 class GlobalBlock:
     """One OLMo-2 block for single-position decoding with a static KV cache."""
 
-    def __init__(self, d: int, nh: int, ffn: int, max_pos: int, gen: torch.Generator, device: torch.device,
-                 workspace: torch.Tensor):
+    def __init__(self, d: int, nh: int, ffn: int, max_pos: int, gen: torch.Generator, device: torch.device):
         self.d, self.nh, self.ffn = d, nh, ffn
         self.w_qkv = _rnd(gen, device, 3 * d, d)
         self.q_norm = _norm_w(gen, device, d)
@@ -50,7 +49,7 @@ class GlobalBlock:
         self.w_gu = _rnd(gen, device, 2 * ffn, d)
         self.w_down = _rnd(gen, device, d, ffn)
         self.mlp_norm = _norm_w(gen, device, d)
-        self.attn = DecodeAttention(nh, d // nh, max_pos, device, workspace)
+        self.attn = DecodeAttention(nh, d // nh, max_pos, device)
 
     def step(self, x: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
         """x [1, d] bf16 at patch position `pos` (device int64) -> the block's output [1, d]."""
@@ -75,8 +74,7 @@ class BolmoDecoder:
         self.enc_norm = _norm_w(gen, device, d)
         self.w_boundary = _rnd(gen, device, 1, d)
         self.w_patch = _rnd(gen, device, d, d)
-        ws = DecodeAttention.workspace_for(global_heads, max_patches, device)
-        self.blocks = [GlobalBlock(d, global_heads, global_ffn, max_patches, gen, device, ws)
+        self.blocks = [GlobalBlock(d, global_heads, global_ffn, max_patches, gen, device)
                        for _ in range(global_layers)]
         self.dec_in_norm = _norm_w(gen, device, d)
         self.w_in = _rnd(gen, device, d, d)

@@ -132,22 +132,12 @@ def rope_tables(max_pos: int, head_dim: int, theta: float, device: torch.device)
 
 
 class DecodeAttention:
-    """Static KV caches of one layer plus the shared split-attention workspace."""
+    """Static KV caches of one layer and its single-position attention."""
 
-    def __init__(self, nh: int, head_dim: int, max_pos: int, device: torch.device,
-                 workspace: torch.Tensor | None = None):
+    def __init__(self, nh: int, head_dim: int, max_pos: int, device: torch.device):
         self.nh, self.hd, self.max_pos = nh, head_dim, max_pos
         self.k_cache = torch.zeros(max_pos, nh, head_dim, dtype=torch.bfloat16, device=device)
         self.v_cache = torch.zeros(max_pos, nh, head_dim, dtype=torch.bfloat16, device=device)
-        need = int(_lib.lib().bp_decode_attention_workspace_bytes(nh, max_pos))
-        if workspace is None or workspace.numel() < need:
-            workspace = torch.zeros(need, dtype=torch.uint8, device=device)
-        self.workspace = workspace
-
-    @staticmethod
-    def workspace_for(nh: int, max_pos: int, device: torch.device) -> torch.Tensor:
-        need = int(_lib.lib().bp_decode_attention_workspace_bytes(nh, max_pos))
-        return torch.zeros(need, dtype=torch.uint8, device=device)
 
     def reset(self) -> None:
         self.k_cache.zero_()
@@ -166,6 +156,5 @@ class DecodeAttention:
         with torch.cuda.device(qkv.device):
             _lib.call("bp_decode_attention", qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(),
                       sin.data_ptr(), pos.data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(), y.data_ptr(),
-                      self.nh, self.hd, self.max_pos, eps, self.hd ** -0.5, self.workspace.data_ptr(),
-                      self.workspace.numel(), _lib.stream_of(qkv))
+                      self.nh, self.hd, self.max_pos, eps, self.hd ** -0.5, _lib.stream_of(qkv))
         return y

@@ -176,16 +176,14 @@ int bp_gate_softcap(const float* g, long long ldg, const float* bias, float* out
  *   whole width (weights q_norm_w, k_norm_w, eps), rotated (rotary halves; cos_t / sin_t fp32
  *   [max_pos, head_dim / 2]), k and v written to k_cache / v_cache [max_pos, nh, head_dim] bf16 at p;
  *   out [nh * head_dim] bf16 = softmax(q . k_j * scale) over j <= p, times v_j.
- * Work is split over 64-position chunks per head; the last chunk to finish combines them in chunk
- * order (deterministic). workspace: the bytes bp_decode_attention_workspace_bytes returns for nh and
- * max_pos, zero-filled before first use and left zero-filled. head_dim 128. A position outside [0, max_pos) writes NaN.
+ * Work per head is one thread-block cluster of 8 CTAs (128 positions each per 1024-position round),
+ * merged in the leader CTA in a fixed order (deterministic). head_dim 128. A position outside
+ * [0, max_pos) writes NaN and touches no cache row.
  * Replaces GlobalStep.step's attention over the StaticCache (byteprof/optim/bolmo.py:100-136).
  */
-size_t bp_decode_attention_workspace_bytes(int nh, int max_pos);
 int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos_t,
                         const float* sin_t, const int64_t* pos, void* k_cache, void* v_cache, void* out, int nh,
-                        int head_dim, int max_pos, float eps, float scale, void* workspace, size_t workspace_bytes,
-                        void* stream);
+                        int head_dim, int max_pos, float eps, float scale, void* stream);
 
 /*
  * End of a decode step: out[0] = argmax(logits[0:n]) (torch.argmax order: NaN largest, lowest index on

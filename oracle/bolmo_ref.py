@@ -36,11 +36,13 @@ def _f32(a) -> np.ndarray:
 
 
 def rmsnorm(x, w, eps: float) -> np.ndarray:
-    """bf16(x * rsqrt(mean(x^2) + eps) * w) row-wise, x [rows, cols]."""
+    """bf16(x * (1 / sqrt(mean(x^2) + eps)) * w) row-wise, x [rows, cols]; the mean, the sum, the square
+    root and the reciprocal each rounded to float32 as the kernels do (the sum of squares is exact here,
+    the kernels' is an fp32 sum)."""
     x = _f32(x)
     ss = (x.astype(F64) ** 2).sum(axis=-1, keepdims=True).astype(F32)
-    t = (ss / F32(x.shape[-1])).astype(F32) + F32(eps)
-    inv = (1.0 / np.sqrt(t.astype(F64))).astype(F32)
+    t = ((ss / F32(x.shape[-1])).astype(F32) + F32(eps)).astype(F32)
+    inv = (F32(1.0) / np.sqrt(t)).astype(F32)
     return round_bf16((x * inv).astype(F32) * _f32(w))
 
 

@@ -141,18 +141,20 @@ def test_attention_over_a_growing_cache_against_the_oracle():
         out, ref = a.step(p)
         ok, err, exact = _attn_close(out, ref)
         assert ok, (p, err, exact)
-    assert int(a.k.workspace[-4 * a.nh:].view(torch.int32).abs().sum()) == 0  # counters left at zero
 
 
-def test_attention_many_chunks_and_the_last_position():
-    a = _Attn(seed=3)
+@pytest.mark.parametrize("max_pos,positions", [(1024, (700, 1023)), (2500, (1024, 1100, 2047, 2048, 2499))])
+def test_attention_many_chunks_rounds_and_the_last_position(max_pos, positions):
+    """Every CTA of the cluster busy, and caches longer than one 1024-position round (the running
+    softmax rescaled between rounds)."""
+    a = _Attn(seed=3, max_pos=max_pos)
     g = torch.Generator(device="cuda").manual_seed(9)
-    fill = (torch.randn(1024, a.nh, a.hd, generator=g, device="cuda")).to(torch.bfloat16)
+    fill = (torch.randn(max_pos, a.nh, a.hd, generator=g, device="cuda")).to(torch.bfloat16)
     a.k.k_cache.copy_(fill)
     a.k.v_cache.copy_(fill.flip(0))
     a.ref.k[:] = to_np(fill)
     a.ref.v[:] = to_np(fill.flip(0))
-    for p in (700, 1023):
+    for p in positions:
         out, ref = a.step(p)
         ok, err, exact = _attn_close(out, ref)
         assert ok, (p, err, exact)
