@@ -1,0 +1,804 @@
+// One global-model step of the batch-1 byte decoder in a single persistent kernel: the OLMo-2 blocks of a
+// Bolmo-1B-shaped model (d 2048, 16 heads x 128, SwiGLU 8192) at one patch position.
+//
+// Reference: GlobalStep.step of byteprof's minimal Bolmo loop (byteprof/optim/bolmo.py:100-136), which
+// runs every block as a chain of framework kernels. The same computation exists here kernel by kernel
+// (skinny GEMMs and the decode.cu glue); this kernel gives the same result except for the summation order
+// inside the matrix-vector products, and removes the ~8 kernel boundaries per block.
+//
+// Work layout. Each CTA (one per SM, cooperative launch) owns a contiguous slice of the rows of every
+// weight matrix: qkv [3d, d], o [d, d], the gate and up halves of gu [2 ffn, d] (the same row indices in
+// both), down [d, ffn]. Its producer warp streams these slices, block after block, in 16 KB 1-D bulk
+// copies into a 12-slot shared-memory ring. Weights never depend on activations, so the stream runs ahead
+// of the computation and through the grid barriers, and HBM stays busy while CTAs wait for each other.
+// The 8 consumer warps run five phases per block, each ended by a grid barrier:
+//   1 qkv   x = the block input (the patch vector, or h + rmsnorm(dn) * mlp_norm of the block before,
+//           recomputed by every CTA from global memory); y = W_qkv x
+//   2 attn  16 heads x 8 position chunks: q, k RMSNorm over d, rotary embedding, the cache write of
+//           position p (the chunk that holds p), scores and a softmax partial (max, sum, output)
+//   3 o     att = the 8 partials of each head merged in chunk order (every CTA); o = W_o att
+//   4 gu    h = x + rmsnorm(o) * attn_norm; a = silu(W_gate h) * (W_up h)
+//   5 down  dn = W_down a
+// After the last block CTA 0 writes value = rmsnorm(h + rmsnorm(dn) * mlp_norm) * out_norm and advances
+// the patch position. Norms, rotary embedding, softmax and SwiGLU round exactly as the decode.cu kernels.
+//
+// Grid barriers: one arrival counter in global memory (release add, acquire polling). A CTA that waits
+// longer than kWaitLimitNs, or finds the shared abort word set, sets it (and the device error flag);
+// every CTA then leaves after the bulk copies it has in flight have landed.
+#include "bp_common.cuh"
+#include "skinny_internal.h"
+#include "sm100.cuh"
+
+namespace bp {
+namespace {
+
+constexpr int kD = 2048, kNH = 16, kHd = 128, kFfn = 8192;
+constexpr int kQkvRows = 3 * kD;
+constexpr int kChunks = 8;                        // attention position chunks per head
+constexpr int kPerWarp = 16;                      // positions per warp and round
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;   // 256
+constexpr int kThreads = kConsumers + 32;         // + the producer warp
+constexpr int kSpan = kConsumerWarps * kPerWarp;  // 128 positions per chunk and round
+constexpr int kRound = kChunks * kSpan;           // 1024
+constexpr int kPartO = 4;                         // partial: max, sum, 2 unused, output[128] (16-byte aligned)
+constexpr int kPart = kPartO + kHd;
+constexpr int kSlots = 12;
+constexpr int kSlotBytes = 16384;
+constexpr int kRows2048 = kSlotBytes / (kD * 2);  // 4 rows of K = 2048 per slot
+constexpr int kMaxLayers = 32;
+constexpr int kMaxGuRows = 128;                   // gate rows per CTA (needs >= 64 CTAs)
+constexpr unsigned kFull = 0xffffffffu;
+
+struct Layer {
+  const __nv_bfloat16 *w_qkv, *q_norm, *k_norm, *w_o, *attn_norm, *w_gu, *w_down, *mlp_norm;
+  __nv_bfloat16 *kc, *vc;
+};
+
+struct Args {
+  Layer L[kMaxLayers];
+  int n_layers, max_pos;
+  const __nv_bfloat16* x_in;
+  const __nv_bfloat16* out_norm;
+  __nv_bfloat16* value_out;
+  long long* pos;
+  const float* cos_t;
+  const float* sin_t;
+  float eps, scale;
+  __nv_bfloat16* y;     // [3d]
+  float* part;          // [nh][kChunks][kPart]
+  __nv_bfloat16* o;     // [d]
+  __nv_bfloat16* a;     // [ffn]
+  __nv_bfloat16* dn;    // [d]
+  __nv_bfloat16* xres;  // [2][d]: block input x, by block parity
+  __nv_bfloat16* hres;  // [2][d]: h, by block parity
+  unsigned* sync;       // [0] barrier arrivals (grows during a launch), [2] abort
+};
+
+struct Smem {
+  alignas(128) uint8_t ring[kSlots][kSlotBytes];
+  alignas(16) __nv_bfloat16 vec[kFfn];  // the phase's input vector
+  alignas(16) float wo[kConsumerWarps][kHd];
+  alignas(16) float qs[kHd];
+  alignas(16) float ks[kHd];
+  alignas(16) float vs[kHd];
+  float red[2][kConsumerWarps];
+  float wm[kConsumerWarps], wl[kConsumerWarps];
+  float gbuf[kMaxGuRows], ubuf[kMaxGuRows];  // gate and up values of this CTA's rows
+  int readers[kSlots];                       // warps done with each ring slot
+  uint64_t full[kSlots], empty[kSlots];
+  int abort;  // this CTA stops (read by the producer's waits)
+  int bad;    // consumer-wide result of the last grid barrier
+};
+
+__device__ __forceinline__ void split(int n, int g, int c, int& r0, int& r1) {
+  r0 = static_cast<int>(static_cast<long long>(c) * n / g);
+  r1 = static_cast<int>(static_cast<long long>(c + 1) * n / g);
+}
+
+__device__ __forceinline__ void consumer_sync() { named_barrier_sync(1, kConsumers); }
+// Consumer barrier that also tells every consumer whether this CTA has stopped; a CTA that stops sets the
+// grid's abort word, so that the other CTAs leave their next barrier at once.
+__device__ __forceinline__ bool consumers_stop(Smem& s, unsigned* sync) {
+  const bool stop = named_barrier_or(1, kConsumers, s.abort != 0);
+  if (stop && threadIdx.x == 0) atomicExch(sync + 2, 1u);
+  return stop;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+  f[0] = bf16lo(v.x); f[1] = bf16hi(v.x); f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
+  f[4] = bf16lo(v.z); f[5] = bf16hi(v.z); f[6] = bf16lo(v.w); f[7] = bf16hi(v.w);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+__device__ __forceinline__ uint4 ldcg16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+__device__ __forceinline__ float inv_rms(float sum_sq, int n, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum_sq, static_cast<float>(n)), eps)));
+}
+
+// Sum over the 256 consumer threads in a fixed order (warp butterfly, then the warps in order).
+__device__ __forceinline__ float consumer_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  consumer_sync();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) t += red[w];
+  return t;
+}
+
+// out[e] = bf16(res[e] + bf16(src[e] * inv * w[e])) for this thread's 8 elements e = 8 t .. 8 t + 7 of a
+// d-vector, inv from the sum of squares of src (decode.cu's BP_NORM_ADD_AFTER with a 256-thread team).
+// src and res are read through L2 (written by other CTAs); the result goes to shared memory.
+__device__ void add_norm_vec(const __nv_bfloat16* src, const __nv_bfloat16* res, const __nv_bfloat16* w, float eps,
+                             Smem& s, float* red, bool res_global) {
+  const int e = threadIdx.x * 8;
+  float f[8], r[8], wv[8];
+  unpack8(ldcg16(src + e), f);
+  float ss = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
+  const float inv = inv_rms(consumer_sum(ss, red), kD, eps);
+  unpack8(res_global ? ldcg16(res + e) : *reinterpret_cast<const uint4*>(res + e), r);
+  unpack8(ldg16(w + e), wv);
+  float o[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(r[j], round_bf16(__fmul_rn(__fmul_rn(f[j], inv), wv[j])));
+  *reinterpret_cast<uint4*>(&s.vec[e]) =
+      make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+}
+
+// This lane's share of a 2048-vector in shared memory: x[lane * 8 + 256 i + j] -> xr[8 i + j].
+__device__ __forceinline__ void load_lane_x(const Smem& s, float (&xr)[64]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float f[8];
+    unpack8(*reinterpret_cast<const uint4*>(&s.vec[lane * 8 + 256 * i]), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr[8 * i + j] = f[j];
+  }
+}
+
+// The 4 rows of a K = 2048 chunk . x at once (their loads and FMAs interleave), fp32, fixed order.
+__device__ __forceinline__ void dot4x2048(const uint8_t* chunk, const float (&xr)[64], float (&out)[kRows2048]) {
+  const int lane = threadIdx.x & 31;
+  float acc[kRows2048][2];
+#pragma unroll
+  for (int r = 0; r < kRows2048; ++r) acc[r][0] = acc[r][1] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int r = 0; r < kRows2048; ++r) {
+      float w[8];
+      unpack8(*reinterpret_cast<const uint4*>(chunk + r * kD * 2 + (lane * 8 + 256 * i) * 2), w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[r][j & 1] = fmaf(w[j], xr[8 * i + j], acc[r][j & 1]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kRows2048; ++r) out[r] = acc[r][0] + acc[r][1];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < kRows2048; ++r) out[r] += __shfl_xor_sync(kFull, out[r], o);
+}
+
+// Row . vec for a bf16 row of 8192 in shared memory against the 8192-vector in s.vec.
+__device__ __forceinline__ float dot8192(const uint8_t* row, const Smem& s) {
+  const int lane = threadIdx.x & 31;
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+  for (int i = 0; i < kFfn / 256; ++i) {
+    float w[8], x[8];
+    unpack8(*reinterpret_cast<const uint4*>(row + (lane * 8 + 256 * i) * 2), w);
+    unpack8(*reinterpret_cast<const uint4*>(&s.vec[lane * 8 + 256 * i]), x);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j & 3] = fmaf(w[j], x[j], acc[j & 3]);
+  }
+  float v = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  return v;
+}
+
+// Waits until ring chunk j has landed; false when the CTA has stopped.
+__device__ __forceinline__ const uint8_t* acquire(Smem& s, uint32_t j) {
+  if (!mbar_wait(&s.full[j % kSlots], (j / kSlots) & 1u, &s.abort)) return nullptr;
+  return s.ring[j % kSlots];
+}
+
+// Grid barrier number `epoch` + 1: every CTA adds one to the arrival counter (release: the CTA's global
+// writes, ordered before it by the CTA barrier, become visible first) and waits (acquire) until the
+// counter reaches (epoch + 1) * gridDim.x. The counter only grows during a launch (the host zeroes it
+// before each launch), so there is no reset and no second word to publish.
+// The last of the `readers` warps done with ring chunk j gives its slot back to the producer.
+__device__ __forceinline__ void release(Smem& s, uint32_t j, int readers) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    const uint32_t slot = j % kSlots;
+    if (atomicAdd(&s.readers[slot], 1) == readers - 1) {
+      s.readers[slot] = 0;
+      mbar_arrive(&s.empty[slot]);
+    }
+  }
+}
+
+// Rows [r0, r1) of a K = 2048 weight, in 4-row ring chunks from chunk j0: warp w takes the chunks w,
+// w + 8, ... whole (one reader per chunk); out[row] = bf16(row . x). The warps run independently; a warp
+// whose wait fails (the CTA stops) leaves, and the end of the phase tells the others.
+__device__ uint32_t gemv2048(Smem& s, uint32_t j0, int r0, int r1, const float (&xr)[64], __nv_bfloat16* out) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nch = (r1 - r0 + kRows2048 - 1) / kRows2048;
+  for (int ch = warp; ch < nch; ch += kConsumerWarps) {
+    const uint8_t* slot = acquire(s, j0 + ch);
+    if (slot == nullptr) break;
+    float v[kRows2048];
+    dot4x2048(slot, xr, v);
+    release(s, j0 + ch, 1);
+    if (lane < kRows2048 && r0 + ch * kRows2048 + lane < r1) {
+      float mine = v[0];
+#pragma unroll
+      for (int r = 1; r < kRows2048; ++r) mine = lane == r ? v[r] : mine;
+      out[r0 + ch * kRows2048 + lane] = __float2bfloat16_rn(mine);
+    }
+  }
+  return j0 + nch;
+}
+
+__device__ bool grid_sync(const Args& a, Smem& s, unsigned& epoch) {
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    const unsigned target = (epoch + 1) * gridDim.x;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync) : "memory");
+      if (v >= target) break;
+      if ((it & 63u) == 63u) {
+        if (*reinterpret_cast<volatile unsigned*>(a.sync + 2) != 0u) {
+          ok = false;
+          break;
+        }
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          atomicExch(a.sync + 2, 1u);
+          atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    epoch += 1;
+    s.bad = ok ? 0 : 1;
+    if (!ok) s.abort = 1;
+  }
+  consumer_sync();
+  return s.bad == 0;
+}
+
+// ---- the producer: this CTA's weight slices, in the consumers' order --------------------------------
+// Chunk k of this CTA's stream (the same sequence for every block): the qkv rows in 4-row chunks, the o
+// rows in 4-row chunks, then for each 4 gate rows the chunk of gate rows and the chunk of the same up
+// rows, then the down rows one per chunk.
+struct Stream {
+  int q0, q1, o0, o1, g0, g1, d0, d1;  // this CTA's row ranges
+  int nq, no, ng, nd, per_layer;       // chunks per segment and per block
+  __device__ Stream(int c, int G) {
+    split(kQkvRows, G, c, q0, q1);
+    split(kD, G, c, o0, o1);
+    split(kFfn, G, c, g0, g1);
+    split(kD, G, c, d0, d1);
+    nq = (q1 - q0 + kRows2048 - 1) / kRows2048;
+    no = (o1 - o0 + kRows2048 - 1) / kRows2048;
+    ng = 2 * ((g1 - g0 + kRows2048 - 1) / kRows2048);
+    nd = d1 - d0;
+    per_layer = nq + no + ng + nd;
+  }
+  __device__ const void* chunk(const Args& a, int k, uint32_t& bytes) const {
+    const Layer& L = a.L[k / per_layer];
+    int i = k % per_layer;
+    if (i < nq) {
+      const int r = q0 + i * kRows2048;
+      bytes = min(kRows2048, q1 - r) * kD * 2;
+      return L.w_qkv + static_cast<size_t>(r) * kD;
+    }
+    i -= nq;
+    if (i < no) {
+      const int r = o0 + i * kRows2048;
+      bytes = min(kRows2048, o1 - r) * kD * 2;
+      return L.w_o + static_cast<size_t>(r) * kD;
+    }
+    i -= no;
+    if (i < ng) {
+      const int r = g0 + (i / 2) * kRows2048;
+      bytes = min(kRows2048, g1 - r) * kD * 2;
+      return L.w_gu + static_cast<size_t>((i & 1) * kFfn + r) * kD;
+    }
+    i -= ng;
+    bytes = kFfn * 2;
+    return L.w_down + static_cast<size_t>(d0 + i) * kFfn;
+  }
+};
+
+constexpr int kPrefetchAhead = 12;  // chunks requested into L2 ahead of the copies (192 KB per SM)
+
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+// Copies chunk after chunk into the ring and requests each chunk into L2 kPrefetchAhead chunks before its
+// copy, so that the copies hit L2 (a copy's latency bounds the ring's throughput). Farther requests would
+// not fit the L2 next to the other CTAs' streams.
+__device__ void producer(const Args& a, Smem& s, int c, int G, bool run) {
+  const uint64_t pol = l2_evict_first_policy();
+  const Stream st(c, G);
+  const int total = run ? st.per_layer * a.n_layers : 0;
+  int pf = 0;
+  uint32_t i = 0;
+  for (int k = 0; k < total; ++k) {
+    for (; pf < total && pf < k + kPrefetchAhead; ++pf) {
+      uint32_t nb;
+      const void* src = st.chunk(a, pf, nb);
+      prefetch_l2(src, nb);
+    }
+    const uint32_t slot = i % kSlots, use = i / kSlots;
+    if (use > 0 && !mbar_wait(&s.empty[slot], (use - 1) & 1u, &s.abort)) break;
+    uint32_t bytes;
+    const void* src = st.chunk(a, k, bytes);
+    mbar_arrive_expect_tx(&s.full[slot], bytes);
+    bulk_load(s.ring[slot], src, bytes, &s.full[slot], pol);
+    ++i;
+  }
+  // Every copy issued must land before the CTA may exit (the consumers may have stopped early).
+  int never = 0;
+  for (uint32_t j = i > static_cast<uint32_t>(kSlots) ? i - kSlots : 0u; j < i; ++j)
+    mbar_wait(&s.full[j % kSlots], (j / kSlots) & 1u, &never);
+}
+
+// ---- phase 2: one (head, chunk) unit of the attention ---------------------------------------------------
+__device__ void attention_unit(const Args& a, Smem& s, const Layer& L, int h, int chunk, long long p) {
+  constexpr int kHalf = kHd / 2;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int rounds = static_cast<int>(p / kRound) + 1;
+  const bool own = static_cast<int>((p % kRound) / kSpan) == chunk;
+  const __nv_bfloat16* q = a.y;
+  const __nv_bfloat16* k = a.y + kD;
+  const __nv_bfloat16* v = a.y + 2 * kD;
+  auto load_rows = [&](long long base, uint2 (&kk)[kPerWarp], uint2 (&vv)[kPerWarp]) {
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) {
+      kk[j] = make_uint2(0u, 0u);
+      vv[j] = make_uint2(0u, 0u);
+      if (base + j < p) {  // rows below p were written by earlier steps; row p comes from this unit
+        const long long off = ((base + j) * kNH + h) * kHd + lane * 4;
+        kk[j] = __ldg(reinterpret_cast<const uint2*>(L.kc + off));
+        vv[j] = __ldg(reinterpret_cast<const uint2*>(L.vc + off));
+      }
+    }
+  };
+  uint2 kk[kPerWarp], vv[kPerWarp];
+  load_rows(static_cast<long long>(chunk) * kSpan + warp * kPerWarp, kk, vv);
+  const int hi = h * kHd + (tid % kHalf);
+  float cs = 0.0f, sn = 0.0f, qa = 0.0f, qb = 0.0f, qwa = 0.0f, qwb = 0.0f, ka = 0.0f, kb = 0.0f, kwa = 0.0f, kwb = 0.0f;
+  float va = 0.0f, vb = 0.0f;
+  if (tid < kHalf) {
+    cs = a.cos_t[p * kHalf + tid];
+    sn = a.sin_t[p * kHalf + tid];
+    qa = __bfloat162float(__ldcg(q + hi));
+    qb = __bfloat162float(__ldcg(q + hi + kHalf));
+    qwa = __bfloat162float(L.q_norm[hi]);
+    qwb = __bfloat162float(L.q_norm[hi + kHalf]);
+    if (own) {
+      ka = __bfloat162float(__ldcg(k + hi));
+      kb = __bfloat162float(__ldcg(k + hi + kHalf));
+      kwa = __bfloat162float(L.k_norm[hi]);
+      kwb = __bfloat162float(L.k_norm[hi + kHalf]);
+    }
+  } else if (own && tid < kHd) {
+    const int j = (tid - kHalf) * 2;
+    va = __bfloat162float(__ldcg(v + h * kHd + j));
+    vb = __bfloat162float(__ldcg(v + h * kHd + j + 1));
+  }
+  float fq[8], fk[8];
+  unpack8(ldcg16(q + tid * 8), fq);
+  unpack8(ldcg16(k + tid * 8), fk);
+  float sq = 0.0f, sk = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    sq = fmaf(fq[j], fq[j], sq);
+    sk = fmaf(fk[j], fk[j], sk);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    sq += __shfl_xor_sync(kFull, sq, o);
+    sk += __shfl_xor_sync(kFull, sk, o);
+  }
+  if (lane == 0) {
+    s.red[0][warp] = sq;
+    s.red[1][warp] = sk;
+  }
+  consumer_sync();
+  float tq = 0.0f, tk = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    tq += s.red[0][w];
+    tk += s.red[1][w];
+  }
+  const float inv_q = inv_rms(tq, kD, a.eps), inv_k = inv_rms(tk, kD, a.eps);
+  const long long slot = p * kNH + h;
+  if (tid < kHalf) {
+    const float q0 = round_bf16(__fmul_rn(__fmul_rn(qa, inv_q), qwa));
+    const float q1 = round_bf16(__fmul_rn(__fmul_rn(qb, inv_q), qwb));
+    s.qs[tid] = __fsub_rn(__fmul_rn(q0, cs), __fmul_rn(q1, sn));
+    s.qs[tid + kHalf] = __fadd_rn(__fmul_rn(q1, cs), __fmul_rn(q0, sn));
+    if (own) {
+      const float k0 = round_bf16(__fmul_rn(__fmul_rn(ka, inv_k), kwa));
+      const float k1 = round_bf16(__fmul_rn(__fmul_rn(kb, inv_k), kwb));
+      const __nv_bfloat16 r0 = __float2bfloat16_rn(__fsub_rn(__fmul_rn(k0, cs), __fmul_rn(k1, sn)));
+      const __nv_bfloat16 r1 = __float2bfloat16_rn(__fadd_rn(__fmul_rn(k1, cs), __fmul_rn(k0, sn)));
+      L.kc[slot * kHd + tid] = r0;
+      L.kc[slot * kHd + tid + kHalf] = r1;
+      s.ks[tid] = __bfloat162float(r0);
+      s.ks[tid + kHalf] = __bfloat162float(r1);
+    }
+  } else if (own && tid < kHd) {
+    const int j = (tid - kHalf) * 2;
+    L.vc[slot * kHd + j] = __float2bfloat16_rn(va);
+    L.vc[slot * kHd + j + 1] = __float2bfloat16_rn(vb);
+    s.vs[j] = va;
+    s.vs[j + 1] = vb;
+  }
+  consumer_sync();
+
+  const float4 qv = *reinterpret_cast<const float4*>(&s.qs[lane * 4]);
+  float mw = -INFINITY, lw = 0.0f, o4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  for (int r = 0; r < rounds; ++r) {
+    const long long base = static_cast<long long>(r) * kRound + chunk * kSpan + warp * kPerWarp;
+    if (r > 0) load_rows(base, kk, vv);
+    float sc[kPerWarp];
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) {
+      float k4[4];
+      if (base + j == p) {
+        const float4 t = *reinterpret_cast<const float4*>(&s.ks[lane * 4]);
+        k4[0] = t.x; k4[1] = t.y; k4[2] = t.z; k4[3] = t.w;
+      } else {
+        k4[0] = bf16lo(kk[j].x); k4[1] = bf16hi(kk[j].x); k4[2] = bf16lo(kk[j].y); k4[3] = bf16hi(kk[j].y);
+      }
+      float dot = __fmul_rn(qv.x, k4[0]);
+      dot = fmaf(qv.y, k4[1], dot);
+      dot = fmaf(qv.z, k4[2], dot);
+      dot = fmaf(qv.w, k4[3], dot);
+      sc[j] = dot;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int j = 0; j < kPerWarp; ++j) sc[j] += __shfl_xor_sync(kFull, sc[j], o);
+    float mr = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) {
+      sc[j] = base + j <= p ? __fmul_rn(sc[j], a.scale) : -INFINITY;
+      mr = fmaxf(mr, sc[j]);
+    }
+    if (mr == -INFINITY) continue;
+    const float m_new = fmaxf(mw, mr);
+    if (mw != -INFINITY) {
+      const float f = expf(__fsub_rn(mw, m_new));
+      lw = __fmul_rn(lw, f);
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) o4[cc] = __fmul_rn(o4[cc], f);
+    }
+    mw = m_new;
+    float e[kPerWarp];
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) e[j] = base + j <= p ? expf(__fsub_rn(sc[j], mw)) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < kPerWarp; ++j) {
+      if (base + j > p) continue;
+      lw = __fadd_rn(lw, e[j]);
+      float v4[4];
+      if (base + j == p) {
+        const float4 t = *reinterpret_cast<const float4*>(&s.vs[lane * 4]);
+        v4[0] = t.x; v4[1] = t.y; v4[2] = t.z; v4[3] = t.w;
+      } else {
+        v4[0] = bf16lo(vv[j].x); v4[1] = bf16hi(vv[j].x); v4[2] = bf16lo(vv[j].y); v4[3] = bf16hi(vv[j].y);
+      }
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) o4[cc] = fmaf(e[j], v4[cc], o4[cc]);
+    }
+  }
+  if (lane == 0) {
+    s.wm[warp] = mw;
+    s.wl[warp] = lw;
+  }
+  *reinterpret_cast<float4*>(&s.wo[warp][lane * 4]) = make_float4(o4[0], o4[1], o4[2], o4[3]);
+  consumer_sync();
+  if (tid < kHd) {
+    float mc = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kConsumerWarps; ++w) mc = fmaxf(mc, s.wm[w]);
+    float lc = 0.0f, oc = 0.0f;
+    if (mc != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kConsumerWarps; ++w) {
+        const float f = s.wm[w] == -INFINITY ? 0.0f : expf(__fsub_rn(s.wm[w], mc));
+        lc = fmaf(s.wl[w], f, lc);
+        oc = fmaf(s.wo[w][tid], f, oc);
+      }
+    }
+    float* pc = a.part + (static_cast<long long>(h) * kChunks + chunk) * kPart;
+    pc[kPartO + tid] = oc;
+    if (tid == 0) {
+      pc[0] = mc;
+      pc[1] = lc;
+    }
+  }
+  consumer_sync();  // shared scratch is reused by the next unit
+}
+
+// ---- the consumers --------------------------------------------------------------------------------------
+__device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  unsigned epoch = 0;  // grid barriers passed (thread 0)
+  uint32_t j = 0;  // ring chunk counter, in the producer's order
+  float xr[64];
+  for (int l = 0; l < a.n_layers; ++l) {
+    const Layer& L = a.L[l];
+    __nv_bfloat16* xres = a.xres + (l & 1) * kD;
+    // ---- 1: x and y = W_qkv x
+    if (l == 0) {
+      *reinterpret_cast<uint4*>(&s.vec[tid * 8]) = ldg16(a.x_in + tid * 8);
+    } else {
+      add_norm_vec(a.dn, a.hres + ((l - 1) & 1) * kD, a.L[l - 1].mlp_norm, a.eps, s, s.red[0], true);
+    }
+    consumer_sync();
+    if (c == 0) *reinterpret_cast<uint4*>(xres + tid * 8) = *reinterpret_cast<const uint4*>(&s.vec[tid * 8]);
+    load_lane_x(s, xr);
+    int r0, r1;
+    split(kQkvRows, G, c, r0, r1);
+    j = gemv2048(s, j, r0, r1, xr, a.y);
+    if (consumers_stop(s, a.sync) || !grid_sync(a, s, epoch)) return;
+    // ---- 2: attention
+    for (int u = c; u < kNH * kChunks; u += G) attention_unit(a, s, L, u / kChunks, u % kChunks, p);
+    if (!grid_sync(a, s, epoch)) return;
+    // ---- 3: att (merge of the partials) and o = W_o att
+    {
+      const int e = tid * 8, h = e / kHd, dd = e % kHd;
+      const float* ph = a.part + static_cast<long long>(h) * kChunks * kPart;
+      float mc[kChunks], mg = -INFINITY;
+#pragma unroll
+      for (int ch = 0; ch < kChunks; ++ch) {
+        mc[ch] = __ldcg(ph + ch * kPart);
+        mg = fmaxf(mg, mc[ch]);
+      }
+      float lg = 0.0f, og[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+      for (int ch = 0; ch < kChunks; ++ch) {
+        const float f = mc[ch] == -INFINITY ? 0.0f : expf(__fsub_rn(mc[ch], mg));
+        lg = fmaf(__ldcg(ph + ch * kPart + 1), f, lg);
+        const float4 o0 = __ldcg(reinterpret_cast<const float4*>(ph + ch * kPart + kPartO + dd));
+        const float4 o1 = __ldcg(reinterpret_cast<const float4*>(ph + ch * kPart + kPartO + dd + 4));
+        const float ov[8] = {o0.x, o0.y, o0.z, o0.w, o1.x, o1.y, o1.z, o1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) og[i] = fmaf(ov[i], f, og[i]);
+      }
+      float at[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) at[i] = __fdiv_rn(og[i], lg);
+      *reinterpret_cast<uint4*>(&s.vec[e]) = make_uint4(pack_bf16x2(at[0], at[1]), pack_bf16x2(at[2], at[3]),
+                                                        pack_bf16x2(at[4], at[5]), pack_bf16x2(at[6], at[7]));
+    }
+    consumer_sync();
+    load_lane_x(s, xr);
+    split(kD, G, c, r0, r1);
+    j = gemv2048(s, j, r0, r1, xr, a.o);
+    if (consumers_stop(s, a.sync) || !grid_sync(a, s, epoch)) return;
+    // ---- 4: h = x + rmsnorm(o) * attn_norm; a = silu(W_gate h) * (W_up h)
+    add_norm_vec(a.o, xres, L.attn_norm, a.eps, s, s.red[0], true);
+    consumer_sync();
+    if (c == 0) *reinterpret_cast<uint4*>(a.hres + (l & 1) * kD + tid * 8) = *reinterpret_cast<const uint4*>(&s.vec[tid * 8]);
+    load_lane_x(s, xr);
+    split(kFfn, G, c, r0, r1);
+    {
+      // chunk 2m: gate rows r0 + 4m .., chunk 2m + 1: the same up rows; warp w takes the chunks w,
+      // w + 8, ... whole
+      const int npairs = (r1 - r0 + kRows2048 - 1) / kRows2048;
+      for (int ch = warp; ch < 2 * npairs; ch += kConsumerWarps) {
+        const uint8_t* slot = acquire(s, j + ch);
+        if (slot == nullptr) break;
+        float v[kRows2048];
+        dot4x2048(slot, xr, v);
+        release(s, j + ch, 1);
+        const int rl = (ch / 2) * kRows2048 + lane;
+        if (lane < kRows2048 && r0 + rl < r1) {
+          float mine = v[0];
+#pragma unroll
+          for (int r = 1; r < kRows2048; ++r) mine = lane == r ? v[r] : mine;
+          ((ch & 1) ? s.ubuf : s.gbuf)[rl] = mine;
+        }
+      }
+      j += 2 * npairs;
+    }
+    if (consumers_stop(s, a.sync)) return;
+    for (int rl = tid; rl < r1 - r0; rl += kConsumers) {
+      const float g = round_bf16(s.gbuf[rl]), up = round_bf16(s.ubuf[rl]);
+      const float sl = round_bf16(static_cast<float>(g / (1.0 + exp(-static_cast<double>(g)))));
+      a.a[r0 + rl] = __float2bfloat16_rn(__fmul_rn(sl, up));
+    }
+    if (!grid_sync(a, s, epoch)) return;
+    // ---- 5: dn = W_down a
+#pragma unroll
+    for (int i = 0; i < kFfn / (kConsumers * 8); ++i)
+      *reinterpret_cast<uint4*>(&s.vec[(i * kConsumers + tid) * 8]) = ldcg16(a.a + (i * kConsumers + tid) * 8);
+    consumer_sync();
+    split(kD, G, c, r0, r1);
+    for (int q = warp; q < r1 - r0; q += kConsumerWarps) {  // one row per chunk, one reader warp
+      const uint8_t* slot = acquire(s, j + q);
+      if (slot == nullptr) break;
+      const float v = dot8192(slot, s);
+      if (lane == 0) a.dn[r0 + q] = __float2bfloat16_rn(v);
+      release(s, j + q, 1);
+    }
+    j += r1 - r0;
+    if (consumers_stop(s, a.sync) || !grid_sync(a, s, epoch)) return;
+  }
+  // ---- value = rmsnorm(x_L) * out_norm, x_L = h + rmsnorm(dn) * mlp_norm of the last block
+  if (c != 0) return;
+  const int last = a.n_layers - 1;
+  add_norm_vec(a.dn, a.hres + (last & 1) * kD, a.L[last].mlp_norm, a.eps, s, s.red[0], true);
+  consumer_sync();
+  const int e = tid * 8;
+  float f[8], wv[8];
+  unpack8(*reinterpret_cast<const uint4*>(&s.vec[e]), f);
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+  const float inv = inv_rms(consumer_sum(ss, s.red[1]), kD, a.eps);
+  unpack8(ldg16(a.out_norm + e), wv);
+  float o[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(f[i], inv), wv[i]);
+  *reinterpret_cast<uint4*>(a.value_out + e) =
+      make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  if (tid == 0) *a.pos = p + 1;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) glob_step_kernel(Args a) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  Smem& s = *reinterpret_cast<Smem*>(smem_raw);
+  const int c = blockIdx.x, G = gridDim.x;
+  const long long p = *a.pos;
+  const bool valid = p >= 0 && p < a.max_pos;  // the same answer in every CTA
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kSlots; ++i) {
+      mbar_init(&s.full[i], 1);
+      mbar_init(&s.empty[i], 1);
+      s.readers[i] = 0;
+    }
+    s.abort = 0;
+    s.bad = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x >= kConsumers) {
+    if (threadIdx.x == kConsumers) producer(a, s, c, G, valid);
+    return;
+  }
+  if (!valid) {  // host checks keep p in range; never index with a bad one
+    if (c == 0) {
+      const uint4 nan4 = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+      *reinterpret_cast<uint4*>(a.value_out + threadIdx.x * 8) = nan4;
+    }
+    return;
+  }
+  consumers(a, s, c, G, p);
+}
+
+constexpr size_t kWsY = 0;
+constexpr size_t kWsPart = kWsY + 3 * kD * 2;
+constexpr size_t kWsO = kWsPart + static_cast<size_t>(kNH) * kChunks * kPart * 4;
+constexpr size_t kWsA = kWsO + kD * 2;
+constexpr size_t kWsDn = kWsA + kFfn * 2;
+constexpr size_t kWsX = kWsDn + kD * 2;
+constexpr size_t kWsH = kWsX + 2 * kD * 2;
+constexpr size_t kWsSync = kWsH + 2 * kD * 2;
+constexpr size_t kWsBytes = kWsSync + 256;
+
+}  // namespace
+
+BP_DEFINE_DEVICE_ERROR_READER(read_device_errors_glob)
+
+}  // namespace bp
+
+extern "C" size_t bp_glob_step_workspace_bytes(void) { return bp::kWsBytes; }
+
+extern "C" int bp_glob_step(const bp_glob_layer* layers, int n_layers, const void* x_in, const void* out_norm,
+                            void* value_out, int64_t* pos, const float* cos_t, const float* sin_t, int max_pos,
+                            float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (layers == nullptr || n_layers < 1 || n_layers > kMaxLayers)
+    return fail(BP_ERR_INVALID_ARGUMENT, "need 1..%d layers (got %d)", kMaxLayers, n_layers);
+  if (x_in == nullptr || out_norm == nullptr || value_out == nullptr || pos == nullptr || cos_t == nullptr ||
+      sin_t == nullptr || workspace == nullptr || max_pos < 1)
+    return fail(BP_ERR_INVALID_ARGUMENT, "a pointer argument is NULL or max_pos < 1");
+  if (workspace_bytes < kWsBytes)
+    return fail(BP_ERR_INVALID_ARGUMENT, "workspace too small (%zu < %zu bytes)", workspace_bytes, kWsBytes);
+  auto a16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+  if (!a16(x_in) || !a16(out_norm) || !a16(value_out) || !a16(workspace))
+    return fail(BP_ERR_MISALIGNED, "vectors and the workspace must be 16-byte aligned");
+  Args a{};
+  for (int l = 0; l < n_layers; ++l) {
+    const bp_glob_layer& g = layers[l];
+    const void* ptrs[] = {g.w_qkv, g.q_norm, g.k_norm, g.w_o, g.attn_norm, g.w_gu, g.w_down, g.mlp_norm, g.k_cache,
+                          g.v_cache};
+    for (const void* q : ptrs)
+      if (q == nullptr || !a16(q)) return fail(BP_ERR_MISALIGNED, "layer %d: a NULL or unaligned pointer", l);
+    a.L[l] = Layer{static_cast<const __nv_bfloat16*>(g.w_qkv), static_cast<const __nv_bfloat16*>(g.q_norm),
+                   static_cast<const __nv_bfloat16*>(g.k_norm), static_cast<const __nv_bfloat16*>(g.w_o),
+                   static_cast<const __nv_bfloat16*>(g.attn_norm), static_cast<const __nv_bfloat16*>(g.w_gu),
+                   static_cast<const __nv_bfloat16*>(g.w_down), static_cast<const __nv_bfloat16*>(g.mlp_norm),
+                   static_cast<__nv_bfloat16*>(g.k_cache), static_cast<__nv_bfloat16*>(g.v_cache)};
+  }
+  a.n_layers = n_layers;
+  a.max_pos = max_pos;
+  a.x_in = static_cast<const __nv_bfloat16*>(x_in);
+  a.out_norm = static_cast<const __nv_bfloat16*>(out_norm);
+  a.value_out = static_cast<__nv_bfloat16*>(value_out);
+  a.pos = reinterpret_cast<long long*>(pos);
+  a.cos_t = cos_t;
+  a.sin_t = sin_t;
+  a.eps = eps;
+  a.scale = 1.0f / sqrtf(static_cast<float>(kHd));
+  char* ws = static_cast<char*>(workspace);
+  a.y = reinterpret_cast<__nv_bfloat16*>(ws + kWsY);
+  a.part = reinterpret_cast<float*>(ws + kWsPart);
+  a.o = reinterpret_cast<__nv_bfloat16*>(ws + kWsO);
+  a.a = reinterpret_cast<__nv_bfloat16*>(ws + kWsA);
+  a.dn = reinterpret_cast<__nv_bfloat16*>(ws + kWsDn);
+  a.xres = reinterpret_cast<__nv_bfloat16*>(ws + kWsX);
+  a.hres = reinterpret_cast<__nv_bfloat16*>(ws + kWsH);
+  a.sync = reinterpret_cast<unsigned*>(ws + kWsSync);
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  const size_t smem = sizeof(Smem);
+  cudaError_t e = cudaFuncSetAttribute(glob_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "glob_step smem attribute: %s", cudaGetErrorString(e));
+  const int sms = tc_sm_count();
+  if ((kFfn + sms - 1) / sms > kMaxGuRows) return fail(BP_ERR_UNSUPPORTED, "glob_step needs at least 64 SMs");
+  int per_sm = 0;
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, glob_step_kernel, kThreads, smem);
+  if (e != cudaSuccess || per_sm < 1) return fail(BP_ERR_CUDA, "glob_step does not fit on an SM");
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  e = cudaMemsetAsync(a.sync, 0, 16, s);  // arrival counter, abort word
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "glob_step sync reset: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(sms);  // one CTA per SM, all resident (cooperative launch)
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, glob_step_kernel, a);
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "glob_step launch: %s", cudaGetErrorString(e));
+  return check_launch("glob_step");
+}

@@ -722,4 +722,6 @@ int launch_skinny_i8(const void* x, long long ldx, const void* w, const void* w_
   return BP_OK;
 }
 
+BP_DEFINE_DEVICE_ERROR_READER(read_device_errors_i8)
+
 }  // namespace bp

@@ -39,7 +39,11 @@ int tc_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
 int tc_sm_count();
 bool tc_pdl_enabled();
 
-// Reads and clears the device error word (synchronising copy).
+// Reads and clears the device error words of all units (synchronising copies); each unit whose kernels
+// can time out has its own word and reader.
 unsigned int read_and_clear_device_errors();
+unsigned int read_device_errors_tc();
+unsigned int read_device_errors_i8();
+unsigned int read_device_errors_glob();
 
 }  // namespace bp

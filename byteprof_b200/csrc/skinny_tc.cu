@@ -613,11 +613,10 @@ extern "C" int bp_skinny_mm_static_scratch(const void* x, long long ldx, const v
 
 namespace bp {
 
+BP_DEFINE_DEVICE_ERROR_READER(read_device_errors_tc)
+
 unsigned int read_and_clear_device_errors() {
-  unsigned int v = 0, zero = 0;
-  cudaMemcpyFromSymbol(&v, g_bp_device_errors, sizeof(v));
-  cudaMemcpyToSymbol(g_bp_device_errors, &zero, sizeof(zero));
-  return v;
+  return read_device_errors_tc() | read_device_errors_i8() | read_device_errors_glob();
 }
 
 }  // namespace bp

@@ -10,9 +10,18 @@
 namespace bp {
 
 // Device error word (bit flags) of the translation unit that includes this header (internal
-// linkage: each unit has its own); skinny_tc.cu reads and clears its word in bp_device_errors().
+// linkage: each unit has its own). A unit whose kernels set it defines its reader with
+// BP_DEFINE_DEVICE_ERROR_READER; bp_device_errors() ORs the words of all units.
 enum : unsigned int { BP_DEVERR_TIMEOUT = 1u };
 static __device__ unsigned int g_bp_device_errors = 0;
+
+#define BP_DEFINE_DEVICE_ERROR_READER(fn)                                    \
+  unsigned int fn() {                                                        \
+    unsigned int v = 0, zero = 0;                                            \
+    cudaMemcpyFromSymbol(&v, g_bp_device_errors, sizeof(v));                 \
+    cudaMemcpyToSymbol(g_bp_device_errors, &zero, sizeof(zero));             \
+    return v;                                                                \
+  }
 
 // A wait that has not completed after this long sets BP_DEVERR_TIMEOUT and gives up.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s

@@ -14,7 +14,9 @@ The loop is byteprof's minimal loop (byteprof/optim/bolmo_loop.py:1-20, 182-207;
 byte the encoder graph, the global graph only when the previous step flagged a boundary (the first
 byte opens a patch), the decoder graph, then one device-to-host read of (token, boundary flag): the
 only synchronisation. Every projection is a skinny GEMM of this library (M = 1), the mLSTM steps are
-the fused scan, and the glue between them is the fused kernels of `decode_ops`.
+the fused scan, and the glue between them is the fused kernels of `decode_ops`. By default the global
+step is one persistent kernel (decode_ops.GlobStep, csrc/glob_step.cu); fused_glob=False runs it kernel
+by kernel (GlobalBlock.step).
 """
 
 from __future__ import annotations
@@ -22,7 +24,7 @@ from __future__ import annotations
 import torch
 
 from .bolmo_local import LocalLayer, rmsnorm
-from .decode_ops import DecodeAttention, add_norm, decode_finish, norm_add, rope_tables, swiglu
+from .decode_ops import DecodeAttention, GlobStep, add_norm, decode_finish, norm_add, rope_tables, swiglu
 from .skinny import skinny_mm
 
 EPS = 1e-6
@@ -65,7 +67,7 @@ class BolmoDecoder:
     def __init__(self, device: torch.device | str = "cuda", seed: int = 0, d: int = 2048, vocab: int = 512,
                  local_heads: int = 4, local_dh: int = 512, local_ffn: int = 2816, global_layers: int = 16,
                  global_heads: int = 16, global_ffn: int = 8192, max_patches: int = 1024,
-                 rope_theta: float = 500000.0):
+                 rope_theta: float = 500000.0, fused_glob: bool = True):
         device = torch.device(device)
         gen = torch.Generator(device=device).manual_seed(seed)
         self.device, self.d, self.vocab, self.max_patches = device, d, vocab, max_patches
@@ -96,6 +98,10 @@ class BolmoDecoder:
         self.patches = 0  # patch positions used (host count)
         self._pin_byte = torch.zeros(1, dtype=torch.long).pin_memory()
         self._pin_out = torch.zeros(2, dtype=torch.long).pin_memory()
+        # the global step as one persistent kernel, or kernel by kernel (GlobalBlock.step)
+        self.fused_glob = fused_glob
+        self.glob_kernel = GlobStep(self.blocks, self.dec_in_norm, self.cos, self.sin, max_patches, EPS) \
+            if fused_glob else None
 
     def weights(self) -> dict[str, torch.Tensor]:
         """Every parameter by name (the CPU oracle rebuilds the model from these)."""
@@ -119,6 +125,9 @@ class BolmoDecoder:
         skinny_mm(e, self.w_boundary, out=self.boundary_logit)
 
     def glob_step(self) -> None:
+        if self.glob_kernel is not None:
+            self.glob_kernel(self.patch, self.value, self.pos)  # writes value, advances pos
+            return
         x = self.patch
         for blk in self.blocks:
             x = blk.step(x, self.pos, self.cos, self.sin)

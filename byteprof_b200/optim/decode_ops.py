@@ -10,11 +10,14 @@ GEMMs (byteprof/optim/bolmo.py:32-136, bolmo_loop.py:36-64):
   * DecodeAttention          one query position over a static KV cache (q/k RMSNorm, rotary
                              embedding, cache write, split attention)
   * decode_finish(logits, b, out)  out = [argmax(logits), sigmoid(b) >= 0.5]
+  * GlobStep                 the whole global-model step (all OLMo-2 blocks) as one persistent kernel
 Every bf16 intermediate is rounded where a bf16 torch tensor would hold it. CUDA tensors only; a
 missing library raises.
 """
 
 from __future__ import annotations
+
+import ctypes
 
 import torch
 
@@ -158,3 +161,42 @@ class DecodeAttention:
                       sin.data_ptr(), pos.data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(), y.data_ptr(),
                       self.nh, self.hd, self.max_pos, eps, self.hd ** -0.5, _lib.stream_of(qkv))
         return y
+
+
+class _GlobLayer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("w_qkv", "q_norm", "k_norm", "w_o", "attn_norm", "w_gu", "w_down",
+                                               "mlp_norm", "k_cache", "v_cache")]
+
+
+class GlobStep:
+    """The global-model step of a Bolmo-1B-shaped decoder (OLMo-2 blocks of d 2048, 16 heads x 128, SwiGLU
+    8192) in one persistent kernel (bp_glob_step): value = rmsnorm(blocks(x)) * out_norm at patch position
+    *pos, which it advances by one. `blocks` are objects with the attributes w_qkv, q_norm, k_norm, w_o,
+    attn_norm, w_gu, w_down, mlp_norm and attn (a DecodeAttention holding the caches)."""
+
+    def __init__(self, blocks, out_norm: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, max_pos: int,
+                 eps: float):
+        self.keep = list(blocks)  # the tensors must outlive every launch (and graph) that uses them
+        self.layers = (_GlobLayer * len(blocks))()
+        for i, b in enumerate(blocks):
+            ts = (b.w_qkv, b.q_norm, b.k_norm, b.w_o, b.attn_norm, b.w_gu, b.w_down, b.mlp_norm, b.attn.k_cache,
+                  b.attn.v_cache)
+            for t in ts:
+                if t.dtype != torch.bfloat16 or not t.is_contiguous() or not t.is_cuda:
+                    raise ValueError("global-step weights and caches must be contiguous bf16 CUDA tensors")
+            self.layers[i] = _GlobLayer(*(t.data_ptr() for t in ts))
+        self.out_norm, self.cos, self.sin, self.max_pos, self.eps = out_norm, cos, sin, max_pos, eps
+        dev = out_norm.device
+        self.workspace = torch.empty(int(_lib.lib().bp_glob_step_workspace_bytes()), dtype=torch.uint8, device=dev)
+
+    def __call__(self, x: torch.Tensor, value_out: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        _bf16(x, value_out)
+        if pos.dtype != torch.int64:
+            raise ValueError("pos must be a device int64")
+        _lib.require_cuda(x, value_out, pos)
+        with torch.cuda.device(x.device):
+            _lib.call("bp_glob_step", ctypes.addressof(self.layers), len(self.keep), x.data_ptr(),
+                      self.out_norm.data_ptr(), value_out.data_ptr(), pos.data_ptr(), self.cos.data_ptr(),
+                      self.sin.data_ptr(), self.max_pos, self.eps, self.workspace.data_ptr(), self.workspace.numel(),
+                      _lib.stream_of(x))
+        return value_out

@@ -17,7 +17,7 @@
  *                       byteprof/optim/mlstm_multistep.py:89-133 lazy_commit_kernel
  *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
  *   bp_mlstm_accept     byteprof/optim/mlstm_multistep.py:136-146 accept_kernel
- *   bp_rmsnorm_ex, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish
+ *   bp_rmsnorm_ex, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish, bp_glob_step
  *                       the per-byte pieces of the minimal Bolmo loop: byteprof/optim/bolmo.py:32-136
  *                       (_layer_step, LocalLoop.enc_step / dec_step, GlobalStep.step) and
  *                       byteprof/optim/bolmo_loop.py:36-64 (MinimalPieces: norm, lm_head, argmax)
@@ -184,6 +184,36 @@ int bp_gate_softcap(const float* g, long long ldg, const float* bias, float* out
 int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos_t,
                         const float* sin_t, const int64_t* pos, void* k_cache, void* v_cache, void* out, int nh,
                         int head_dim, int max_pos, float eps, float scale, void* stream);
+
+/*
+ * One global-model step of a Bolmo-1B-shaped byte decoder in a single persistent (cooperative) kernel:
+ * n_layers OLMo-2 blocks (d 2048, 16 heads x 128, SwiGLU 8192; RMSNorm of q and k over d, rotary
+ * embedding, attention over the static KV caches, RMSNorm of the attention and MLP outputs before each
+ * residual add) at patch position p = *pos, then value_out = rmsnorm(x_L) * out_norm and *pos = p + 1.
+ * Per layer: w_qkv [3d, d], q_norm [d], k_norm [d], w_o [d, d], attn_norm [d], w_gu [2 ffn, d] (gate rows,
+ * then up rows), w_down [d, ffn], mlp_norm [d], k_cache / v_cache [max_pos, 16, 128]; all bf16, 16-byte
+ * aligned. cos_t / sin_t fp32 [max_pos, 64]. workspace: bp_glob_step_workspace_bytes() bytes, 16-byte
+ * aligned, no initial content. Results equal the kernel-by-kernel path (bp_skinny_mm, bp_decode_attention,
+ * bp_rmsnorm_ex, bp_swiglu) up to the summation order of the matrix-vector products. Not capturable
+ * together with other work that needs the SMs meanwhile (one CTA per SM, all resident). Replaces
+ * GlobalStep.step (byteprof/optim/bolmo.py:100-136).
+ */
+typedef struct bp_glob_layer {
+  const void* w_qkv;
+  const void* q_norm;
+  const void* k_norm;
+  const void* w_o;
+  const void* attn_norm;
+  const void* w_gu;
+  const void* w_down;
+  const void* mlp_norm;
+  void* k_cache;
+  void* v_cache;
+} bp_glob_layer;
+size_t bp_glob_step_workspace_bytes(void);
+int bp_glob_step(const bp_glob_layer* layers, int n_layers, const void* x_in, const void* out_norm, void* value_out,
+                 int64_t* pos, const float* cos_t, const float* sin_t, int max_pos, float eps, void* workspace,
+                 size_t workspace_bytes, void* stream);
 
 /*
  * End of a decode step: out[0] = argmax(logits[0:n]) (torch.argmax order: NaN largest, lowest index on
