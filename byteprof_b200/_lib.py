@@ -43,6 +43,11 @@ _SIGNATURES = {
                                     c_void_p, c_int, c_int, c_int, c_float, c_float, c_void_p]),
     "bp_decode_finish": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "bp_glob_step_workspace_bytes": (c_size_t, []),
+    "bp_loc_step_workspace_bytes": (c_size_t, []),
+    "bp_loc_enc_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_float, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+    "bp_loc_dec_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_float, c_float, c_float, c_void_p, c_size_t, c_void_p]),
     "bp_glob_step": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float,
                              c_void_p, c_size_t, c_void_p]),
     "bp_mlstm_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

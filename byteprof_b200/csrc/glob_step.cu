@@ -26,29 +26,26 @@
 // longer than kWaitLimitNs, or finds the shared abort word set, sets it (and the device error flag);
 // every CTA then leaves after the bulk copies it has in flight have landed.
 #include "bp_common.cuh"
+#include "persist.cuh"
 #include "skinny_internal.h"
 #include "sm100.cuh"
 
 namespace bp {
 namespace {
 
+using namespace persist;
+
 constexpr int kD = 2048, kNH = 16, kHd = 128, kFfn = 8192;
 constexpr int kQkvRows = 3 * kD;
 constexpr int kChunks = 8;                        // attention position chunks per head
 constexpr int kPerWarp = 16;                      // positions per warp and round
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;   // 256
-constexpr int kThreads = kConsumers + 32;         // + the producer warp
 constexpr int kSpan = kConsumerWarps * kPerWarp;  // 128 positions per chunk and round
 constexpr int kRound = kChunks * kSpan;           // 1024
 constexpr int kPartO = 4;                         // partial: max, sum, 2 unused, output[128] (16-byte aligned)
 constexpr int kPart = kPartO + kHd;
-constexpr int kSlots = 12;
-constexpr int kSlotBytes = 16384;
 constexpr int kRows2048 = kSlotBytes / (kD * 2);  // 4 rows of K = 2048 per slot
 constexpr int kMaxLayers = 32;
 constexpr int kMaxGuRows = 128;                   // gate rows per CTA (needs >= 64 CTAs)
-constexpr unsigned kFull = 0xffffffffu;
 
 struct Layer {
   const __nv_bfloat16 *w_qkv, *q_norm, *k_norm, *w_o, *attn_norm, *w_gu, *w_down, *mlp_norm;
@@ -76,69 +73,15 @@ struct Args {
 };
 
 struct Smem {
-  alignas(128) uint8_t ring[kSlots][kSlotBytes];
+  Ring r;
   alignas(16) __nv_bfloat16 vec[kFfn];  // the phase's input vector
   alignas(16) float wo[kConsumerWarps][kHd];
   alignas(16) float qs[kHd];
   alignas(16) float ks[kHd];
   alignas(16) float vs[kHd];
-  float red[2][kConsumerWarps];
   float wm[kConsumerWarps], wl[kConsumerWarps];
   float gbuf[kMaxGuRows], ubuf[kMaxGuRows];  // gate and up values of this CTA's rows
-  int readers[kSlots];                       // warps done with each ring slot
-  uint64_t full[kSlots], empty[kSlots];
-  int abort;  // this CTA stops (read by the producer's waits)
-  int bad;    // consumer-wide result of the last grid barrier
 };
-
-__device__ __forceinline__ void split(int n, int g, int c, int& r0, int& r1) {
-  r0 = static_cast<int>(static_cast<long long>(c) * n / g);
-  r1 = static_cast<int>(static_cast<long long>(c + 1) * n / g);
-}
-
-__device__ __forceinline__ void consumer_sync() { named_barrier_sync(1, kConsumers); }
-// Consumer barrier that also tells every consumer whether this CTA has stopped; a CTA that stops sets the
-// grid's abort word, so that the other CTAs leave their next barrier at once.
-__device__ __forceinline__ bool consumers_stop(Smem& s, unsigned* sync) {
-  const bool stop = named_barrier_or(1, kConsumers, s.abort != 0);
-  if (stop && threadIdx.x == 0) atomicExch(sync + 2, 1u);
-  return stop;
-}
-
-__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
-      : "memory");
-}
-
-__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
-  f[0] = bf16lo(v.x); f[1] = bf16hi(v.x); f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
-  f[4] = bf16lo(v.z); f[5] = bf16hi(v.z); f[6] = bf16lo(v.w); f[7] = bf16hi(v.w);
-}
-
-__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<const uint32_t*>(&p);
-}
-
-__device__ __forceinline__ uint4 ldcg16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
-
-__device__ __forceinline__ float inv_rms(float sum_sq, int n, float eps) {
-  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum_sq, static_cast<float>(n)), eps)));
-}
-
-// Sum over the 256 consumer threads in a fixed order (warp butterfly, then the warps in order).
-__device__ __forceinline__ float consumer_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  consumer_sync();
-  float t = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) t += red[w];
-  return t;
-}
 
 // out[e] = bf16(res[e] + bf16(src[e] * inv * w[e])) for this thread's 8 elements e = 8 t .. 8 t + 7 of a
 // d-vector, inv from the sum of squares of src (decode.cu's BP_NORM_ADD_AFTER with a 256-thread team).
@@ -161,42 +104,6 @@ __device__ void add_norm_vec(const __nv_bfloat16* src, const __nv_bfloat16* res,
       make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
 }
 
-// This lane's share of a 2048-vector in shared memory: x[lane * 8 + 256 i + j] -> xr[8 i + j].
-__device__ __forceinline__ void load_lane_x(const Smem& s, float (&xr)[64]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    float f[8];
-    unpack8(*reinterpret_cast<const uint4*>(&s.vec[lane * 8 + 256 * i]), f);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) xr[8 * i + j] = f[j];
-  }
-}
-
-// The 4 rows of a K = 2048 chunk . x at once (their loads and FMAs interleave), fp32, fixed order.
-__device__ __forceinline__ void dot4x2048(const uint8_t* chunk, const float (&xr)[64], float (&out)[kRows2048]) {
-  const int lane = threadIdx.x & 31;
-  float acc[kRows2048][2];
-#pragma unroll
-  for (int r = 0; r < kRows2048; ++r) acc[r][0] = acc[r][1] = 0.0f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-#pragma unroll
-    for (int r = 0; r < kRows2048; ++r) {
-      float w[8];
-      unpack8(*reinterpret_cast<const uint4*>(chunk + r * kD * 2 + (lane * 8 + 256 * i) * 2), w);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) acc[r][j & 1] = fmaf(w[j], xr[8 * i + j], acc[r][j & 1]);
-    }
-  }
-#pragma unroll
-  for (int r = 0; r < kRows2048; ++r) out[r] = acc[r][0] + acc[r][1];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-    for (int r = 0; r < kRows2048; ++r) out[r] += __shfl_xor_sync(kFull, out[r], o);
-}
-
 // Row . vec for a bf16 row of 8192 in shared memory against the 8192-vector in s.vec.
 __device__ __forceinline__ float dot8192(const uint8_t* row, const Smem& s) {
   const int lane = threadIdx.x & 31;
@@ -215,28 +122,6 @@ __device__ __forceinline__ float dot8192(const uint8_t* row, const Smem& s) {
   return v;
 }
 
-// Waits until ring chunk j has landed; false when the CTA has stopped.
-__device__ __forceinline__ const uint8_t* acquire(Smem& s, uint32_t j) {
-  if (!mbar_wait(&s.full[j % kSlots], (j / kSlots) & 1u, &s.abort)) return nullptr;
-  return s.ring[j % kSlots];
-}
-
-// Grid barrier number `epoch` + 1: every CTA adds one to the arrival counter (release: the CTA's global
-// writes, ordered before it by the CTA barrier, become visible first) and waits (acquire) until the
-// counter reaches (epoch + 1) * gridDim.x. The counter only grows during a launch (the host zeroes it
-// before each launch), so there is no reset and no second word to publish.
-// The last of the `readers` warps done with ring chunk j gives its slot back to the producer.
-__device__ __forceinline__ void release(Smem& s, uint32_t j, int readers) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) {
-    const uint32_t slot = j % kSlots;
-    if (atomicAdd(&s.readers[slot], 1) == readers - 1) {
-      s.readers[slot] = 0;
-      mbar_arrive(&s.empty[slot]);
-    }
-  }
-}
-
 // Rows [r0, r1) of a K = 2048 weight, in 4-row ring chunks from chunk j0: warp w takes the chunks w,
 // w + 8, ... whole (one reader per chunk); out[row] = bf16(row . x). The warps run independently; a warp
 // whose wait fails (the CTA stops) leaves, and the end of the phase tells the others.
@@ -244,51 +129,15 @@ __device__ uint32_t gemv2048(Smem& s, uint32_t j0, int r0, int r1, const float (
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = (r1 - r0 + kRows2048 - 1) / kRows2048;
   for (int ch = warp; ch < nch; ch += kConsumerWarps) {
-    const uint8_t* slot = acquire(s, j0 + ch);
+    const uint8_t* slot = acquire(s.r, j0 + ch);
     if (slot == nullptr) break;
     float v[kRows2048];
     dot4x2048(slot, xr, v);
-    release(s, j0 + ch, 1);
-    if (lane < kRows2048 && r0 + ch * kRows2048 + lane < r1) {
-      float mine = v[0];
-#pragma unroll
-      for (int r = 1; r < kRows2048; ++r) mine = lane == r ? v[r] : mine;
-      out[r0 + ch * kRows2048 + lane] = __float2bfloat16_rn(mine);
-    }
+    release(s.r, j0 + ch, 1);
+    if (lane < kRows2048 && r0 + ch * kRows2048 + lane < r1)
+      out[r0 + ch * kRows2048 + lane] = __float2bfloat16_rn(lane_row(v));
   }
   return j0 + nch;
-}
-
-__device__ bool grid_sync(const Args& a, Smem& s, unsigned& epoch) {
-  consumer_sync();
-  if (threadIdx.x == 0) {
-    bool ok = true;
-    const unsigned target = (epoch + 1) * gridDim.x;
-    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(a.sync) : "memory");
-    const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 0;; ++it) {
-      unsigned v;
-      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(a.sync) : "memory");
-      if (v >= target) break;
-      if ((it & 63u) == 63u) {
-        if (*reinterpret_cast<volatile unsigned*>(a.sync + 2) != 0u) {
-          ok = false;
-          break;
-        }
-        if (globaltimer() - t0 > kWaitLimitNs) {
-          atomicExch(a.sync + 2, 1u);
-          atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
-          ok = false;
-          break;
-        }
-      }
-    }
-    epoch += 1;
-    s.bad = ok ? 0 : 1;
-    if (!ok) s.abort = 1;
-  }
-  consumer_sync();
-  return s.bad == 0;
 }
 
 // ---- the producer: this CTA's weight slices, in the consumers' order --------------------------------
@@ -335,40 +184,11 @@ struct Stream {
   }
 };
 
-constexpr int kPrefetchAhead = 12;  // chunks requested into L2 ahead of the copies (192 KB per SM)
-
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-}
-
-// Copies chunk after chunk into the ring and requests each chunk into L2 kPrefetchAhead chunks before its
-// copy, so that the copies hit L2 (a copy's latency bounds the ring's throughput). Farther requests would
-// not fit the L2 next to the other CTAs' streams.
-__device__ void producer(const Args& a, Smem& s, int c, int G, bool run) {
-  const uint64_t pol = l2_evict_first_policy();
-  const Stream st(c, G);
-  const int total = run ? st.per_layer * a.n_layers : 0;
-  int pf = 0;
-  uint32_t i = 0;
-  for (int k = 0; k < total; ++k) {
-    for (; pf < total && pf < k + kPrefetchAhead; ++pf) {
-      uint32_t nb;
-      const void* src = st.chunk(a, pf, nb);
-      prefetch_l2(src, nb);
-    }
-    const uint32_t slot = i % kSlots, use = i / kSlots;
-    if (use > 0 && !mbar_wait(&s.empty[slot], (use - 1) & 1u, &s.abort)) break;
-    uint32_t bytes;
-    const void* src = st.chunk(a, k, bytes);
-    mbar_arrive_expect_tx(&s.full[slot], bytes);
-    bulk_load(s.ring[slot], src, bytes, &s.full[slot], pol);
-    ++i;
-  }
-  // Every copy issued must land before the CTA may exit (the consumers may have stopped early).
-  int never = 0;
-  for (uint32_t j = i > static_cast<uint32_t>(kSlots) ? i - kSlots : 0u; j < i; ++j)
-    mbar_wait(&s.full[j % kSlots], (j / kSlots) & 1u, &never);
-}
+struct StreamSrc {
+  const Args& a;
+  Stream st;
+  __device__ const void* chunk(int k, uint32_t& bytes) const { return st.chunk(a, k, bytes); }
+};
 
 // ---- phase 2: one (head, chunk) unit of the attention ---------------------------------------------------
 __device__ void attention_unit(const Args& a, Smem& s, const Layer& L, int h, int chunk, long long p) {
@@ -429,15 +249,15 @@ __device__ void attention_unit(const Args& a, Smem& s, const Layer& L, int h, in
     sk += __shfl_xor_sync(kFull, sk, o);
   }
   if (lane == 0) {
-    s.red[0][warp] = sq;
-    s.red[1][warp] = sk;
+    s.r.red[0][warp] = sq;
+    s.r.red[1][warp] = sk;
   }
   consumer_sync();
   float tq = 0.0f, tk = 0.0f;
 #pragma unroll
   for (int w = 0; w < kConsumerWarps; ++w) {
-    tq += s.red[0][w];
-    tk += s.red[1][w];
+    tq += s.r.red[0][w];
+    tk += s.r.red[1][w];
   }
   const float inv_q = inv_rms(tq, kD, a.eps), inv_k = inv_rms(tk, kD, a.eps);
   const long long slot = p * kNH + h;
@@ -565,18 +385,18 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
     if (l == 0) {
       *reinterpret_cast<uint4*>(&s.vec[tid * 8]) = ldg16(a.x_in + tid * 8);
     } else {
-      add_norm_vec(a.dn, a.hres + ((l - 1) & 1) * kD, a.L[l - 1].mlp_norm, a.eps, s, s.red[0], true);
+      add_norm_vec(a.dn, a.hres + ((l - 1) & 1) * kD, a.L[l - 1].mlp_norm, a.eps, s, s.r.red[0], true);
     }
     consumer_sync();
     if (c == 0) *reinterpret_cast<uint4*>(xres + tid * 8) = *reinterpret_cast<const uint4*>(&s.vec[tid * 8]);
-    load_lane_x(s, xr);
+    load_lane_x(s.vec, xr);
     int r0, r1;
     split(kQkvRows, G, c, r0, r1);
     j = gemv2048(s, j, r0, r1, xr, a.y);
-    if (consumers_stop(s, a.sync) || !grid_sync(a, s, epoch)) return;
+    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch)) return;
     // ---- 2: attention
     for (int u = c; u < kNH * kChunks; u += G) attention_unit(a, s, L, u / kChunks, u % kChunks, p);
-    if (!grid_sync(a, s, epoch)) return;
+    if (!grid_sync(s.r, a.sync, epoch)) return;
     // ---- 3: att (merge of the partials) and o = W_o att
     {
       const int e = tid * 8, h = e / kHd, dd = e % kHd;
@@ -605,43 +425,38 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
                                                         pack_bf16x2(at[4], at[5]), pack_bf16x2(at[6], at[7]));
     }
     consumer_sync();
-    load_lane_x(s, xr);
+    load_lane_x(s.vec, xr);
     split(kD, G, c, r0, r1);
     j = gemv2048(s, j, r0, r1, xr, a.o);
-    if (consumers_stop(s, a.sync) || !grid_sync(a, s, epoch)) return;
+    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch)) return;
     // ---- 4: h = x + rmsnorm(o) * attn_norm; a = silu(W_gate h) * (W_up h)
-    add_norm_vec(a.o, xres, L.attn_norm, a.eps, s, s.red[0], true);
+    add_norm_vec(a.o, xres, L.attn_norm, a.eps, s, s.r.red[0], true);
     consumer_sync();
     if (c == 0) *reinterpret_cast<uint4*>(a.hres + (l & 1) * kD + tid * 8) = *reinterpret_cast<const uint4*>(&s.vec[tid * 8]);
-    load_lane_x(s, xr);
+    load_lane_x(s.vec, xr);
     split(kFfn, G, c, r0, r1);
     {
       // chunk 2m: gate rows r0 + 4m .., chunk 2m + 1: the same up rows; warp w takes the chunks w,
       // w + 8, ... whole
       const int npairs = (r1 - r0 + kRows2048 - 1) / kRows2048;
       for (int ch = warp; ch < 2 * npairs; ch += kConsumerWarps) {
-        const uint8_t* slot = acquire(s, j + ch);
+        const uint8_t* slot = acquire(s.r, j + ch);
         if (slot == nullptr) break;
         float v[kRows2048];
         dot4x2048(slot, xr, v);
-        release(s, j + ch, 1);
+        release(s.r, j + ch, 1);
         const int rl = (ch / 2) * kRows2048 + lane;
-        if (lane < kRows2048 && r0 + rl < r1) {
-          float mine = v[0];
-#pragma unroll
-          for (int r = 1; r < kRows2048; ++r) mine = lane == r ? v[r] : mine;
-          ((ch & 1) ? s.ubuf : s.gbuf)[rl] = mine;
-        }
+        if (lane < kRows2048 && r0 + rl < r1) ((ch & 1) ? s.ubuf : s.gbuf)[rl] = lane_row(v);
       }
       j += 2 * npairs;
     }
-    if (consumers_stop(s, a.sync)) return;
+    if (consumers_stop(s.r, a.sync)) return;
     for (int rl = tid; rl < r1 - r0; rl += kConsumers) {
       const float g = round_bf16(s.gbuf[rl]), up = round_bf16(s.ubuf[rl]);
       const float sl = round_bf16(static_cast<float>(g / (1.0 + exp(-static_cast<double>(g)))));
       a.a[r0 + rl] = __float2bfloat16_rn(__fmul_rn(sl, up));
     }
-    if (!grid_sync(a, s, epoch)) return;
+    if (!grid_sync(s.r, a.sync, epoch)) return;
     // ---- 5: dn = W_down a
 #pragma unroll
     for (int i = 0; i < kFfn / (kConsumers * 8); ++i)
@@ -649,19 +464,19 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
     consumer_sync();
     split(kD, G, c, r0, r1);
     for (int q = warp; q < r1 - r0; q += kConsumerWarps) {  // one row per chunk, one reader warp
-      const uint8_t* slot = acquire(s, j + q);
+      const uint8_t* slot = acquire(s.r, j + q);
       if (slot == nullptr) break;
       const float v = dot8192(slot, s);
       if (lane == 0) a.dn[r0 + q] = __float2bfloat16_rn(v);
-      release(s, j + q, 1);
+      release(s.r, j + q, 1);
     }
     j += r1 - r0;
-    if (consumers_stop(s, a.sync) || !grid_sync(a, s, epoch)) return;
+    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch)) return;
   }
   // ---- value = rmsnorm(x_L) * out_norm, x_L = h + rmsnorm(dn) * mlp_norm of the last block
   if (c != 0) return;
   const int last = a.n_layers - 1;
-  add_norm_vec(a.dn, a.hres + (last & 1) * kD, a.L[last].mlp_norm, a.eps, s, s.red[0], true);
+  add_norm_vec(a.dn, a.hres + (last & 1) * kD, a.L[last].mlp_norm, a.eps, s, s.r.red[0], true);
   consumer_sync();
   const int e = tid * 8;
   float f[8], wv[8];
@@ -669,7 +484,7 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
   float ss = 0.0f;
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
-  const float inv = inv_rms(consumer_sum(ss, s.red[1]), kD, a.eps);
+  const float inv = inv_rms(consumer_sum(ss, s.r.red[1]), kD, a.eps);
   unpack8(ldg16(a.out_norm + e), wv);
   float o[8];
 #pragma unroll
@@ -685,19 +500,13 @@ __global__ void __launch_bounds__(kThreads, 1) glob_step_kernel(Args a) {
   const int c = blockIdx.x, G = gridDim.x;
   const long long p = *a.pos;
   const bool valid = p >= 0 && p < a.max_pos;  // the same answer in every CTA
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kSlots; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);
-      s.readers[i] = 0;
-    }
-    s.abort = 0;
-    s.bad = 0;
-    mbar_fence_init();
-  }
+  if (threadIdx.x == 0) ring_init(s.r);
   __syncthreads();
   if (threadIdx.x >= kConsumers) {
-    if (threadIdx.x == kConsumers) producer(a, s, c, G, valid);
+    if (threadIdx.x == kConsumers) {
+      const StreamSrc src{a, Stream(c, G)};
+      produce(s.r, src, valid ? src.st.per_layer * a.n_layers : 0);
+    }
     return;
   }
   if (!valid) {  // host checks keep p in range; never index with a bad one

@@ -1,0 +1,260 @@
+// Machinery shared by the persistent decode kernels (glob_step.cu: the global-model step; loc_step.cu:
+// the local encoder and decoder steps): one CTA per SM (cooperative launch), 8 consumer warps and one
+// producer warp; the producer streams this CTA's weight rows in 16 KB 1-D bulk copies through a 12-slot
+// shared-memory ring (each chunk requested into L2 kPrefetchAhead chunks before its copy); the consumers
+// run the phases of the step, separated by grid barriers on one monotonic arrival counter.
+//
+// Every wait is bounded: a ring wait or a grid barrier that has not completed after kWaitLimitNs sets the
+// CTA's abort flag, the grid's abort word and the device error flag; every CTA then leaves once the bulk
+// copies it has in flight have landed.
+#pragma once
+
+#include "bp_common.cuh"
+#include "sm100.cuh"
+
+namespace bp {
+namespace persist {
+
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;  // 256
+constexpr int kThreads = kConsumers + 32;        // + the producer warp
+constexpr int kSlots = 12;
+constexpr int kSlotBytes = 16384;
+constexpr int kPrefetchAhead = 12;               // chunks requested into L2 ahead of their copy
+constexpr unsigned kFull = 0xffffffffu;
+
+// The ring and the CTA's control words; the first member of a kernel's shared-memory struct.
+struct Ring {
+  alignas(128) uint8_t slot[kSlots][kSlotBytes];
+  uint64_t full[kSlots], empty[kSlots];
+  int readers[kSlots];  // warps done with each slot
+  int issued[kSlots];   // the chunk most recently issued into each slot (-1: none yet)
+  int abort;            // this CTA stops (read by the producer's waits)
+  int bad;              // consumer-wide result of the last grid barrier
+  float red[2][kConsumerWarps];
+};
+
+// Thread 0, before the CTA's first barrier.
+__device__ __forceinline__ void ring_init(Ring& r) {
+  for (int i = 0; i < kSlots; ++i) {
+    mbar_init(&r.full[i], 1);
+    mbar_init(&r.empty[i], 1);
+    r.readers[i] = 0;
+    r.issued[i] = -1;
+  }
+  r.abort = 0;
+  r.bad = 0;
+  mbar_fence_init();
+}
+
+// Rows [r0, r1) of n rows that CTA c of G owns.
+__device__ __forceinline__ void split(int n, int g, int c, int& r0, int& r1) {
+  r0 = static_cast<int>(static_cast<long long>(c) * n / g);
+  r1 = static_cast<int>(static_cast<long long>(c + 1) * n / g);
+}
+
+__device__ __forceinline__ void consumer_sync() { named_barrier_sync(1, kConsumers); }
+
+// Consumer barrier that also tells every consumer whether this CTA has stopped; a CTA that stops sets the
+// grid's abort word (sync[2]), so that the other CTAs leave their next barrier at once.
+__device__ __forceinline__ bool consumers_stop(Ring& r, unsigned* sync) {
+  const bool stop = named_barrier_or(1, kConsumers, r.abort != 0);
+  if (stop && threadIdx.x == 0) atomicExch(sync + 2, 1u);
+  return stop;
+}
+
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
+      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+  f[0] = bf16lo(v.x); f[1] = bf16hi(v.x); f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
+  f[4] = bf16lo(v.z); f[5] = bf16hi(v.z); f[6] = bf16lo(v.w); f[7] = bf16hi(v.w);
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t*>(&p);
+}
+
+__device__ __forceinline__ uint4 pack8(const float (&o)[8]) {
+  return make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+}
+
+// 16 bytes through L2 (data written by other CTAs of the same launch).
+__device__ __forceinline__ uint4 ldcg16(const void* p) { return __ldcg(reinterpret_cast<const uint4*>(p)); }
+
+// 1 / sqrt(sum_sq / n + eps), each operation correctly rounded (decode.cu's RMSNorm).
+__device__ __forceinline__ float inv_rms(float sum_sq, int n, float eps) {
+  return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum_sq, static_cast<float>(n)), eps)));
+}
+
+// Sum over the 256 consumer threads in a fixed order (warp butterfly, then the warps in order).
+__device__ __forceinline__ float consumer_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFull, v, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  consumer_sync();
+  float t = 0.0f;
+#pragma unroll
+  for (int w = 0; w < kConsumerWarps; ++w) t += red[w];
+  return t;
+}
+
+// Waits until ring chunk j has landed; nullptr when the CTA has stopped.
+// An mbarrier wait names a phase by its parity only: waiting for use u of a slot returns at once while the
+// slot is still in use u - 1 (use u - 2 has the same parity and has completed), which happens when a warp
+// asks for chunk j before chunk j - kSlots has landed. So a warp first waits (bounded) until the producer
+// has issued chunk j into the slot, which it does only after chunk j - kSlots was released, i.e. had
+// landed; from then on the slot is in use u or later, and the parity wait is exact.
+__device__ __forceinline__ const uint8_t* acquire(Ring& r, uint32_t j) {
+  const uint32_t s = j % kSlots;
+  volatile int* issued = r.issued;
+  if (issued[s] < static_cast<int>(j)) {
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1; issued[s] < static_cast<int>(j); ++it) {
+      if ((it & 31u) == 0) {
+        if (*reinterpret_cast<volatile int*>(&r.abort)) return nullptr;
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          r.abort = 1;
+          atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
+          return nullptr;
+        }
+      }
+    }
+  }
+  if (!mbar_wait(&r.full[s], (j / kSlots) & 1u, &r.abort)) return nullptr;
+  return r.slot[s];
+}
+
+// The last of the `readers` warps done with ring chunk j gives its slot back to the producer.
+__device__ __forceinline__ void release(Ring& r, uint32_t j, int readers) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) {
+    const uint32_t s = j % kSlots;
+    if (atomicAdd(&r.readers[s], 1) == readers - 1) {
+      r.readers[s] = 0;
+      mbar_arrive(&r.empty[s]);
+    }
+  }
+}
+
+// Grid barrier number `epoch` + 1 (consumers only): every CTA adds one to the arrival counter sync[0]
+// (release: the CTA's global writes, ordered before it by the CTA barrier, become visible first) and waits
+// (acquire) until the counter reaches (epoch + 1) * gridDim.x. The counter only grows during a launch (the
+// host zeroes sync[0..3] before each launch). False when the step is aborted.
+__device__ __forceinline__ bool grid_sync(Ring& r, unsigned* sync, unsigned& epoch) {
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    bool ok = true;
+    const unsigned target = (epoch + 1) * gridDim.x;
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(sync) : "memory");
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 0;; ++it) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(sync) : "memory");
+      if (v >= target) break;
+      if ((it & 63u) == 63u) {
+        if (*reinterpret_cast<volatile unsigned*>(sync + 2) != 0u) {
+          ok = false;
+          break;
+        }
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          atomicExch(sync + 2, 1u);
+          atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+    epoch += 1;
+    r.bad = ok ? 0 : 1;
+    if (!ok) r.abort = 1;
+  }
+  consumer_sync();
+  return r.bad == 0;
+}
+
+// The producer: chunk k of `src` (src.chunk(k, bytes) -> global address) into the ring, k = 0 .. total-1,
+// each requested into L2 kPrefetchAhead chunks before its copy (requests run no farther ahead while the
+// ring is full: measured, that did not shorten the steps); then waits for every copy in flight.
+template <typename Src>
+__device__ void produce(Ring& r, const Src& src, int total) {
+  const uint64_t pol = l2_evict_first_policy();
+  int pf = 0;
+  uint32_t i = 0;
+  for (int k = 0; k < total; ++k) {
+    for (; pf < total && pf < k + kPrefetchAhead; ++pf) {
+      uint32_t nb;
+      const void* p = src.chunk(pf, nb);
+      prefetch_l2(p, nb);
+    }
+    const uint32_t s = i % kSlots, use = i / kSlots;
+    if (use > 0 && !mbar_wait(&r.empty[s], (use - 1) & 1u, &r.abort)) break;
+    uint32_t bytes;
+    const void* p = src.chunk(k, bytes);
+    mbar_arrive_expect_tx(&r.full[s], bytes);
+    bulk_load(r.slot[s], p, bytes, &r.full[s], pol);
+    *reinterpret_cast<volatile int*>(&r.issued[s]) = k;  // after the copy is on its way (see acquire)
+    ++i;
+  }
+  int never = 0;  // every copy issued must land before the CTA may exit
+  for (uint32_t j = i > static_cast<uint32_t>(kSlots) ? i - kSlots : 0u; j < i; ++j)
+    mbar_wait(&r.full[j % kSlots], (j / kSlots) & 1u, &never);
+}
+
+// This lane's share of a 2048-vector in shared memory: x[lane * 8 + 256 i + j] -> xr[8 i + j].
+__device__ __forceinline__ void load_lane_x(const __nv_bfloat16* vec, float (&xr)[64]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    float f[8];
+    unpack8(*reinterpret_cast<const uint4*>(vec + lane * 8 + 256 * i), f);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) xr[8 * i + j] = f[j];
+  }
+}
+
+// The 4 rows of a K = 2048 chunk (bf16, in shared memory) . x at once (their loads and FMAs interleave),
+// fp32, fixed order; every lane gets the 4 sums.
+__device__ __forceinline__ void dot4x2048(const uint8_t* chunk, const float (&xr)[64], float (&out)[4]) {
+  const int lane = threadIdx.x & 31;
+  float acc[4][2];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) acc[r][0] = acc[r][1] = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      float w[8];
+      unpack8(*reinterpret_cast<const uint4*>(chunk + r * 4096 + (lane * 8 + 256 * i) * 2), w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[r][j & 1] = fmaf(w[j], xr[8 * i + j], acc[r][j & 1]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) out[r] = acc[r][0] + acc[r][1];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) out[r] += __shfl_xor_sync(kFull, out[r], o);
+}
+
+// v[lane] for lane < 4 (the lane's own row of a 4-row result).
+__device__ __forceinline__ float lane_row(const float (&v)[4]) {
+  const int lane = threadIdx.x & 31;
+  float mine = v[0];
+#pragma unroll
+  for (int r = 1; r < 4; ++r) mine = lane == r ? v[r] : mine;
+  return mine;
+}
+
+}  // namespace persist
+}  // namespace bp

@@ -45,5 +45,6 @@ unsigned int read_and_clear_device_errors();
 unsigned int read_device_errors_tc();
 unsigned int read_device_errors_i8();
 unsigned int read_device_errors_glob();
+unsigned int read_device_errors_loc();
 
 }  // namespace bp

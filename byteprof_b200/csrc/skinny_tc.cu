@@ -616,7 +616,7 @@ namespace bp {
 BP_DEFINE_DEVICE_ERROR_READER(read_device_errors_tc)
 
 unsigned int read_and_clear_device_errors() {
-  return read_device_errors_tc() | read_device_errors_i8() | read_device_errors_glob();
+  return read_device_errors_tc() | read_device_errors_i8() | read_device_errors_glob() | read_device_errors_loc();
 }
 
 }  // namespace bp

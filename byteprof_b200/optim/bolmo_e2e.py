@@ -16,7 +16,10 @@ byte opens a patch), the decoder graph, then one device-to-host read of (token, 
 only synchronisation. Every projection is a skinny GEMM of this library (M = 1), the mLSTM steps are
 the fused scan, and the glue between them is the fused kernels of `decode_ops`. By default the global
 step is one persistent kernel (decode_ops.GlobStep, csrc/glob_step.cu); fused_glob=False runs it kernel
-by kernel (GlobalBlock.step).
+by kernel (GlobalBlock.step). fused_local=True runs each local step as one persistent kernel too
+(decode_ops.LocStep, csrc/loc_step.cu); it is off by default because on B200 it measures slower than the
+kernel-by-kernel local step (a persistent kernel cannot start streaming its weights before the previous
+piece has left the GPU, while each skinny GEMM starts under its predecessor).
 """
 
 from __future__ import annotations
@@ -24,7 +27,7 @@ from __future__ import annotations
 import torch
 
 from .bolmo_local import LocalLayer, rmsnorm
-from .decode_ops import DecodeAttention, GlobStep, add_norm, decode_finish, norm_add, rope_tables, swiglu
+from .decode_ops import DecodeAttention, GlobStep, LocStep, add_norm, decode_finish, norm_add, rope_tables, swiglu
 from .skinny import skinny_mm
 
 EPS = 1e-6
@@ -67,7 +70,7 @@ class BolmoDecoder:
     def __init__(self, device: torch.device | str = "cuda", seed: int = 0, d: int = 2048, vocab: int = 512,
                  local_heads: int = 4, local_dh: int = 512, local_ffn: int = 2816, global_layers: int = 16,
                  global_heads: int = 16, global_ffn: int = 8192, max_patches: int = 1024,
-                 rope_theta: float = 500000.0, fused_glob: bool = True):
+                 rope_theta: float = 500000.0, fused_glob: bool = True, fused_local: bool = False):
         device = torch.device(device)
         gen = torch.Generator(device=device).manual_seed(seed)
         self.device, self.d, self.vocab, self.max_patches = device, d, vocab, max_patches
@@ -102,6 +105,9 @@ class BolmoDecoder:
         self.fused_glob = fused_glob
         self.glob_kernel = GlobStep(self.blocks, self.dec_in_norm, self.cos, self.sin, max_patches, EPS) \
             if fused_glob else None
+        # the local steps as one persistent kernel each, or kernel by kernel (LocalLayer.step)
+        self.enc_kernel = LocStep(self.enc) if fused_local else None
+        self.dec_kernel = LocStep(self.dec) if fused_local else None
 
     def weights(self) -> dict[str, torch.Tensor]:
         """Every parameter by name (the CPU oracle rebuilds the model from these)."""
@@ -118,6 +124,10 @@ class BolmoDecoder:
 
     # ---- the three per-byte pieces (device only, graph-capturable) ----
     def enc_step(self, parity: int) -> None:
+        if self.enc_kernel is not None:
+            self.enc_kernel.enc(parity, self.embed, self.byte, self.enc_norm, self.w_patch, self.w_boundary, self.e,
+                                self.patch, self.boundary_logit)
+            return
         h = self.embed.index_select(0, self.byte)
         _, e = self.enc.step(h, rmsnorm(h, self.enc.norm1, EPS), parity, out_norm=self.enc_norm, want_sum=False)
         self.e.copy_(e)
@@ -135,6 +145,10 @@ class BolmoDecoder:
         self.pos.add_(1)
 
     def dec_step(self, parity: int) -> None:
+        if self.dec_kernel is not None:
+            self.dec_kernel.dec(parity, self.e, self.value, self.w_in, self.final_norm, self.lm_head,
+                                self.boundary_logit, self.logits, self.out)
+            return
         h, x = norm_add(skinny_mm(self.e, self.w_in), self.value, self.dec.norm1, EPS)
         _, xf = self.dec.step(h, x, parity, out_norm=self.final_norm, want_sum=False)
         skinny_mm(xf, self.lm_head, out=self.logits)

@@ -11,6 +11,8 @@ GEMMs (byteprof/optim/bolmo.py:32-136, bolmo_loop.py:36-64):
                              embedding, cache write, split attention)
   * decode_finish(logits, b, out)  out = [argmax(logits), sigmoid(b) >= 0.5]
   * GlobStep                 the whole global-model step (all OLMo-2 blocks) as one persistent kernel
+  * LocStep                  the local encoder or decoder step (one mLSTM layer and its heads) as one
+                             persistent kernel
 Every bf16 intermediate is rounded where a bf16 torch tensor would hold it. CUDA tensors only; a
 missing library raises.
 """
@@ -200,3 +202,48 @@ class GlobStep:
                       self.sin.data_ptr(), self.max_pos, self.eps, self.workspace.data_ptr(), self.workspace.numel(),
                       _lib.stream_of(x))
         return value_out
+
+
+class _LocLayer(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in ("norm1", "w_qkvo", "w_if", "b_if", "mh_norm", "w_out", "norm2", "w_gu",
+                                               "w_down", "c", "n_cur", "m_cur", "n_next", "m_next")]
+
+
+class LocStep:
+    """One local step of a Bolmo-shaped decoder (one mLSTM layer of d 2048, 4 heads x 512, SwiGLU 2816, and
+    the encoder's patch / boundary heads or the decoder's LM head and argmax) as one persistent kernel
+    (bp_loc_enc_step / bp_loc_dec_step). `layer` is a bolmo_local.LocalLayer; `parity` names the n / m
+    buffers holding the current state, as in LocalLayer.step."""
+
+    def __init__(self, layer):
+        self.layer = layer
+        c = layer.state[0]
+        w = (layer.norm1, layer.w_qkvo, layer.w_if, layer.b_if, layer.mh_norm, layer.w_out, layer.norm2, layer.w_gu,
+             layer.w_down)
+        for t in (*w, c, *layer.nm[0], *layer.nm[1]):
+            if not t.is_cuda or not t.is_contiguous():
+                raise ValueError("local-step weights and state must be contiguous CUDA tensors")
+        self.tables = []
+        for parity in (0, 1):
+            n_cur, m_cur = layer.nm[parity]
+            n_next, m_next = layer.nm[1 - parity]
+            self.tables.append(_LocLayer(*(t.data_ptr() for t in w), c.data_ptr(), n_cur.data_ptr(), m_cur.data_ptr(),
+                                         n_next.data_ptr(), m_next.data_ptr()))
+        self.workspace = torch.empty(int(_lib.lib().bp_loc_step_workspace_bytes()), dtype=torch.uint8, device=c.device)
+
+    def _common(self, parity: int):
+        layer = self.layer
+        return (layer.norm_eps, layer.gate_cap, layer.mlstm_eps, self.workspace.data_ptr(), self.workspace.numel(),
+                _lib.stream_of(self.workspace))
+
+    def enc(self, parity: int, embed, byte, enc_norm, w_patch, w_boundary, e_out, patch_out, boundary_logit) -> None:
+        with torch.cuda.device(embed.device):
+            _lib.call("bp_loc_enc_step", ctypes.addressof(self.tables[parity]), embed.data_ptr(), byte.data_ptr(),
+                      enc_norm.data_ptr(), w_patch.data_ptr(), w_boundary.data_ptr(), e_out.data_ptr(),
+                      patch_out.data_ptr(), boundary_logit.data_ptr(), *self._common(parity))
+
+    def dec(self, parity: int, e_in, value, w_in, final_norm, lm_head, boundary_logit, logits, out) -> None:
+        with torch.cuda.device(e_in.device):
+            _lib.call("bp_loc_dec_step", ctypes.addressof(self.tables[parity]), e_in.data_ptr(), value.data_ptr(),
+                      w_in.data_ptr(), final_norm.data_ptr(), lm_head.data_ptr(), boundary_logit.data_ptr(),
+                      logits.data_ptr(), out.data_ptr(), *self._common(parity))

@@ -17,7 +17,8 @@
  *                       byteprof/optim/mlstm_multistep.py:89-133 lazy_commit_kernel
  *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
  *   bp_mlstm_accept     byteprof/optim/mlstm_multistep.py:136-146 accept_kernel
- *   bp_rmsnorm_ex, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish, bp_glob_step
+ *   bp_rmsnorm_ex, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish, bp_glob_step,
+ *   bp_loc_enc_step, bp_loc_dec_step
  *                       the per-byte pieces of the minimal Bolmo loop: byteprof/optim/bolmo.py:32-136
  *                       (_layer_step, LocalLoop.enc_step / dec_step, GlobalStep.step) and
  *                       byteprof/optim/bolmo_loop.py:36-64 (MinimalPieces: norm, lm_head, argmax)
@@ -192,8 +193,8 @@ int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_nor
  * residual add) at patch position p = *pos, then value_out = rmsnorm(x_L) * out_norm and *pos = p + 1.
  * Per layer: w_qkv [3d, d], q_norm [d], k_norm [d], w_o [d, d], attn_norm [d], w_gu [2 ffn, d] (gate rows,
  * then up rows), w_down [d, ffn], mlp_norm [d], k_cache / v_cache [max_pos, 16, 128]; all bf16, 16-byte
- * aligned. cos_t / sin_t fp32 [max_pos, 64]. workspace: bp_glob_step_workspace_bytes() bytes, 16-byte
- * aligned, no initial content. Results equal the kernel-by-kernel path (bp_skinny_mm, bp_decode_attention,
+ * aligned. cos_t / sin_t fp32 [max_pos, 64]. workspace: the size bp_glob_step_workspace_bytes returns,
+ * 16-byte aligned, no initial content. Results equal the kernel-by-kernel path (bp_skinny_mm, bp_decode_attention,
  * bp_rmsnorm_ex, bp_swiglu) up to the summation order of the matrix-vector products. Not capturable
  * together with other work that needs the SMs meanwhile (one CTA per SM, all resident). Replaces
  * GlobalStep.step (byteprof/optim/bolmo.py:100-136).
@@ -214,6 +215,50 @@ size_t bp_glob_step_workspace_bytes(void);
 int bp_glob_step(const bp_glob_layer* layers, int n_layers, const void* x_in, const void* out_norm, void* value_out,
                  int64_t* pos, const float* cos_t, const float* sin_t, int max_pos, float eps, void* workspace,
                  size_t workspace_bytes, void* stream);
+
+/*
+ * One local step of a Bolmo-shaped byte decoder (d 2048; mLSTM 4 heads x 512; SwiGLU 2816; vocabulary 512)
+ * in a single persistent (cooperative) kernel. The layer: x = rmsnorm(h) * norm1; y = w_qkvo x (q | k | v |
+ * o, [4d, d]); g = cap * tanh((w_if x + b_if) / cap) ([2 NH, d], b_if fp32; input gates then forget gates);
+ * the mLSTM step on the state c [NH, 512, 512] (in place) and n [NH, 512], m [NH] (fp32, read from
+ * n_cur / m_cur, written to n_next / m_next); z = sigmoid(o) * rmsnorm_head(h_mlstm) * mh_norm [NH, 512];
+ * h2 = h + w_out z; output = h2 + w_down (silu(W_gate x2) * W_up x2), x2 = rmsnorm(h2) * norm2, w_gu
+ * [2 * 2816, d] (gate rows, then up rows), w_down [d, 2816]. All weights bf16, 16-byte aligned. Each
+ * call needs the workspace size bp_loc_step_workspace_bytes returns (16-byte aligned, no initial
+ * content) and the whole GPU while it runs.
+ *   bp_loc_enc_step: h = embed[*byte] (embed [512, d]); e_out = rmsnorm(output) * enc_norm; patch_out =
+ *     w_patch e (bf16 [d]); *boundary_logit = w_boundary . e (fp32; w_boundary [1, d]). A byte outside
+ *     [0, 512) writes NaN and leaves the state alone.
+ *   bp_loc_dec_step: h = bf16(w_in e_in + value); logits = lm_head (rmsnorm(output) * final_norm) (fp32
+ *     [512]); out[0] = argmax(logits) (torch order), out[1] = sigmoid(*boundary_logit) >= 0.5.
+ * Results equal the kernel-by-kernel step (bp_skinny_mm, bp_rmsnorm_ex, bp_gate_softcap, bp_mlstm_scan,
+ * bp_swiglu) except for summation orders. Replaces LocalLoop.enc_step / dec_step with the norm, out
+ * projection, LM head and argmax of MinimalPieces (byteprof/optim/bolmo.py:32-97, bolmo_loop.py:36-64).
+ */
+typedef struct bp_loc_layer {
+  const void* norm1;
+  const void* w_qkvo;
+  const void* w_if;
+  const float* b_if;
+  const void* mh_norm;
+  const void* w_out;
+  const void* norm2;
+  const void* w_gu;
+  const void* w_down;
+  float* c;
+  const float* n_cur;
+  const float* m_cur;
+  float* n_next;
+  float* m_next;
+} bp_loc_layer;
+size_t bp_loc_step_workspace_bytes(void);
+int bp_loc_enc_step(const bp_loc_layer* layer, const void* embed, const int64_t* byte, const void* enc_norm,
+                    const void* w_patch, const void* w_boundary, void* e_out, void* patch_out, float* boundary_logit,
+                    float eps, float gate_cap, float mlstm_eps, void* workspace, size_t workspace_bytes, void* stream);
+int bp_loc_dec_step(const bp_loc_layer* layer, const void* e_in, const void* value, const void* w_in,
+                    const void* final_norm, const void* lm_head, const float* boundary_logit, float* logits,
+                    int64_t* out, float eps, float gate_cap, float mlstm_eps, void* workspace, size_t workspace_bytes,
+                    void* stream);
 
 /*
  * End of a decode step: out[0] = argmax(logits[0:n]) (torch.argmax order: NaN largest, lowest index on

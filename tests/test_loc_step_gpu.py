@@ -1,0 +1,135 @@
+"""The local encoder and decoder steps as one persistent kernel each (bp_loc_enc_step / bp_loc_dec_step,
+csrc/loc_step.cu) against the same steps kernel by kernel (LocalLayer.step with the skinny GEMMs, the scan
+and the decode.cu glue), from the same weights and recurrent state. The two differ in summation orders
+(CUDA-core dot products against tensor-core tiles, the mLSTM unit's sums), so a bf16 rounding lands one step
+apart now and then and the layer's noise-dominated heads spread it; the outputs and the new state stay
+within a few percent normwise and strongly correlated. Also: CUDA-graph replays equal eager launches, and a
+byte outside the vocabulary writes NaN and leaves the state alone."""
+
+import numpy as np
+import pytest
+import torch
+
+from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+from helpers import to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(seed=7):
+    m = BolmoDecoder(seed=seed, global_layers=1, fused_local=True)
+    g = torch.Generator(device="cuda").manual_seed(seed + 1)
+    for layer in (m.enc, m.dec):  # a non-trivial recurrent state
+        c, n, mm = layer.state
+        c.copy_(torch.randn(c.shape, generator=g, device="cuda") * 0.05)
+        n.copy_(torch.randn(n.shape, generator=g, device="cuda") * 0.5)
+        mm.copy_(torch.randn(mm.shape, generator=g, device="cuda"))
+    m.value.copy_(torch.randn(m.value.shape, generator=g, device="cuda").to(torch.bfloat16))
+    m.e.copy_(torch.randn(m.e.shape, generator=g, device="cuda").to(torch.bfloat16))
+    return m
+
+
+def _snap(layer):
+    return [t.clone() for t in (*layer.state, *layer.nm[1])]
+
+
+def _restore(layer, snap):
+    for t, v in zip((*layer.state, *layer.nm[1]), snap):
+        t.copy_(v)
+
+
+def _stats(a, b):
+    a, b = to_np(a).ravel().astype(np.float64), to_np(b).ravel().astype(np.float64)
+    err = float(np.abs(a - b).max() / np.abs(b).max())
+    corr = float(np.corrcoef(a, b)[0, 1])
+    return err, corr
+
+
+def _run(m, which, fused):
+    kern = m.enc_kernel if which == "enc" else m.dec_kernel
+    if which == "enc":
+        m.enc_kernel = kern if fused else None
+        m.enc_step(0)
+        m.enc_kernel = kern
+    else:
+        m.dec_kernel = kern if fused else None
+        m.dec_step(0)
+        m.dec_kernel = kern
+    torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("byte", [0, 65, 255, 511])
+def test_encoder_step_matches_the_kernel_by_kernel_step(byte):
+    m = _model()
+    snap = _snap(m.enc)
+    m.byte.fill_(byte)
+    _run(m, "enc", fused=False)
+    ref = [m.e.clone(), m.patch.clone(), m.boundary_logit.clone(), m.enc.state[0].clone(), m.enc.nm[1][0].clone(),
+           m.enc.nm[1][1].clone()]
+    _restore(m.enc, snap)
+    _run(m, "enc", fused=True)
+    got = [m.e, m.patch, m.boundary_logit, m.enc.state[0], m.enc.nm[1][0], m.enc.nm[1][1]]
+    names = ["e", "patch", "boundary", "C", "n", "m"]
+    stats = {nm: _stats(g, r) for nm, g, r in zip(names, got, ref) if nm != "boundary"}
+    stats["boundary"] = float(abs(float(got[2]) - float(ref[2])))
+    print(byte, stats)
+    for nm in ("e", "patch"):
+        assert stats[nm][0] <= 0.05 and stats[nm][1] >= 0.995, (nm, stats[nm])
+    for nm in ("C", "n"):
+        assert stats[nm][0] <= 0.02 and stats[nm][1] >= 0.9999, (nm, stats[nm])
+    assert stats["m"][0] <= 1e-5, stats["m"]
+    assert stats["boundary"] <= 0.05 * max(1.0, abs(float(ref[2])))
+    # the current buffers were only read
+    assert all(torch.equal(a, b) for a, b in zip((m.enc.nm[0][0], m.enc.nm[0][1]), (snap[1], snap[2])))
+
+
+def test_decoder_step_matches_the_kernel_by_kernel_step():
+    m = _model(11)
+    snap = _snap(m.dec)
+    m.boundary_logit.fill_(0.3)
+    _run(m, "dec", fused=False)
+    ref_logits, ref_state = m.logits.clone(), m.dec.state[0].clone()
+    _restore(m.dec, snap)
+    m.out.zero_()
+    _run(m, "dec", fused=True)
+    err, corr = _stats(m.logits, ref_logits)
+    cerr, ccorr = _stats(m.dec.state[0], ref_state)
+    print({"logits": (err, corr), "C": (cerr, ccorr)})
+    assert err <= 0.05 and corr >= 0.995, (err, corr)
+    assert cerr <= 0.02 and ccorr >= 0.9999, (cerr, ccorr)
+    lg = m.logits.float()
+    assert int(m.out[0]) == int(torch.argmax(lg)) and int(m.out[1]) == 1  # sigmoid(0.3) >= 0.5
+
+
+def test_graph_replays_equal_eager_launches():
+    m = _model(3)
+    snap_e, snap_d = _snap(m.enc), _snap(m.dec)
+    m.byte.fill_(42)
+    m.enc_step(0)
+    m.dec_step(0)
+    eager = [m.e.clone(), m.patch.clone(), m.logits.clone(), m.out.clone(), m.enc.state[0].clone()]
+    _restore(m.enc, snap_e)
+    _restore(m.dec, snap_d)
+    ge, gd = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ge):
+        m.enc_step(0)
+    with torch.cuda.graph(gd):
+        m.dec_step(0)
+    _restore(m.enc, snap_e)
+    _restore(m.dec, snap_d)
+    ge.replay()
+    gd.replay()
+    torch.cuda.synchronize()
+    got = [m.e, m.patch, m.logits, m.out, m.enc.state[0]]
+    assert all(torch.equal(a, b) for a, b in zip(got, eager))
+
+
+def test_a_byte_outside_the_vocabulary_writes_nan_and_leaves_the_state():
+    m = _model(5)
+    snap = _snap(m.enc)
+    m.byte.fill_(512)
+    m.enc_step(0)
+    torch.cuda.synchronize()
+    assert torch.isnan(m.e.float()).all() and torch.isnan(m.patch.float()).all()
+    assert torch.isnan(m.boundary_logit).all()
+    assert all(torch.equal(a, b) for a, b in zip((*m.enc.state, *m.enc.nm[1]), snap))
