@@ -16,7 +16,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libbp_kernels.so"
 
 BP_OK = 0
-BP_DTYPE_BF16, BP_DTYPE_F32, BP_DTYPE_INT8 = 0, 1, 2
+BP_DTYPE_BF16, BP_DTYPE_F32, BP_DTYPE_INT8, BP_DTYPE_INT4 = 0, 1, 2, 3
 _DTYPE_CODE = {torch.bfloat16: BP_DTYPE_BF16, torch.float32: BP_DTYPE_F32, torch.int8: BP_DTYPE_INT8}
 
 # name -> (restype, argtypes); must match include/bp_kernels.h
@@ -32,7 +32,7 @@ _SIGNATURES = {
     "bp_gemv_int8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
                              c_void_p]),
     "bp_skinny_mm_int4": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_int,
-                                  c_int, c_int, c_int, c_int, c_void_p]),
+                                  c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bp_rmsnorm": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_longlong, c_int, c_int, c_float, c_void_p]),
     "bp_rmsnorm_ex": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_longlong, c_void_p, c_longlong,
                               c_void_p, c_longlong, c_int, c_int, c_float, c_int, c_void_p]),

@@ -321,7 +321,9 @@ bool tc_path_enabled() {
 }  // namespace bp
 
 extern "C" size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype) {
-  if (M <= 0 || N <= 0 || K <= 0 || (w_dtype != BP_DTYPE_BF16 && w_dtype != BP_DTYPE_INT8)) return 0;
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  if (w_dtype == BP_DTYPE_INT4) return bp::skinny_i4tc_workspace_bytes(N, K);
+  if (w_dtype != BP_DTYPE_BF16 && w_dtype != BP_DTYPE_INT8) return 0;
   return bp::skinny_tc_workspace_bytes(N, K, w_dtype == BP_DTYPE_INT8);
 }
 

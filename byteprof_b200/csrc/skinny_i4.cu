@@ -8,8 +8,9 @@
 // holds code j in its low nibble and code j + 64 in its high nibble; the 32 rows of a row tile and one group
 // are one contiguous 2 KB block. scale [K / 128, N] bf16, zero [K / 128, N] fp16.
 //
-// B200 design (CUDA cores: a tensor-core MMA costs the same for N = 16 as for N = 128, so int4 weights
-// widened to bf16 would make the MMA issue rate, not HBM, the limit at this size):
+// This is the CUDA-core kernel, used without a workspace, for shapes the tensor-core kernel does not take
+// (N not a multiple of 8, unaligned scale or zero) and with BP_SKINNY_PATH=fma; skinny_i4tc.cu is the
+// tensor-core kernel. Design:
 //  * A warp covers 8 rows of a row tile: lane l reads bytes [16 l, 16 l + 16) of the 512-byte slice of
 //    each group block, i.e. row l / 4, chunk c = l % 4 (codes 16 c .. 16 c + 15 and 64 + 16 c .. + 15):
 //    every load instruction of the warp reads 512 contiguous bytes, streamed with an L2 evict-first policy
@@ -26,6 +27,7 @@
 //  * The K partition depends on (N, K) only, so a row's result does not depend on M.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
+#include <stdlib.h>
 
 #include "bp_common.cuh"
 #include "skinny_internal.h"
@@ -255,6 +257,12 @@ int launch_i4(I4Args a, cudaStream_t st) {
   return BP_OK;
 }
 
+// BP_SKINNY_PATH=fma forces the CUDA-core kernel (read at every call; for comparisons).
+bool tc_path_requested() {
+  const char* e = getenv("BP_SKINNY_PATH");
+  return !(e != nullptr && e[0] == 'f');
+}
+
 int dispatch_i4(const I4Args& a, int m, cudaStream_t st) {
   switch (m) {
 #define BP_CASE(MM) \
@@ -271,7 +279,7 @@ int dispatch_i4(const I4Args& a, int m, cudaStream_t st) {
 
 extern "C" int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_packed, const void* scale,
                                  const void* zero, void* y, long long ldy, int y_dtype, int M, int N, int K,
-                                 int tile_rows, void* stream) {
+                                 int tile_rows, void* workspace, size_t workspace_bytes, void* stream) {
   using namespace bp;
   clear_error();
   if (M < 0 || N < 0 || K < 0) return fail(BP_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d K=%d)", M, N, K);
@@ -310,11 +318,16 @@ extern "C" int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_
   a.G = K / kGroup;
   a.g_chunk = a.G;
   a.gb = 1;
+  // The tensor-core kernel for every row chunk or for none: the kernel choice depends on the shape, the
+  // alignment and the workspace only, so a row's result does not depend on M.
+  const bool tc = !(workspace == nullptr && workspace_bytes == 0) && tc_path_requested() &&
+                  skinny_i4tc_supported(x, ldx, w_packed, scale, zero, 1, N, K);
   for (int r0 = 0; r0 < M; r0 += 16) {
     const int m = M - r0 < 16 ? M - r0 : 16;
     a.x = static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r0) * ldx;
     a.y = static_cast<char*>(y) + static_cast<long long>(r0) * ldy * static_cast<long long>(ysz);
-    st = dispatch_i4(a, m, s);
+    st = tc ? launch_skinny_i4tc(a.x, ldx, w_packed, scale, zero, a.y, ldy, a.y_f32, m, N, K, workspace, workspace_bytes, s)
+            : dispatch_i4(a, m, s);
     if (st != BP_OK) return st;
   }
   return BP_OK;

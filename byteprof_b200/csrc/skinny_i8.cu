@@ -37,6 +37,7 @@
 //    flight, frees TMEM and returns.
 #include <cudaTypedefs.h>
 
+#include "digits.cuh"
 #include "skinny_internal.h"
 #include "sm100.cuh"
 
@@ -45,14 +46,12 @@ namespace {
 
 constexpr int kBK = 128;                   // K per unit: one 128-byte swizzle row of int8
 constexpr int kRows = 16;                  // activation rows per launch
-constexpr int kPlanes = 4;                 // base-256 digits per activation
+constexpr int kPlanes = kDigitPlanes;      // base-256 digits per activation
 constexpr int kAM = kRows * kPlanes;       // MMA M
 constexpr int kABytes = kAM * kBK;         // 8 KB
 constexpr int kThreads = 224;              // weight TMA, MMA, digit TMA, 4 epilogue warps
 constexpr int kEpiWarp0 = 3;
 constexpr int kGroup = 128;                // epilogue threads
-constexpr int kFracBits = 29;
-constexpr int kNonFinite = 0x7fffffff;     // row exponent marker: the row holds an Inf or a NaN
 constexpr int kMaxClusterSplit = 8;        // portable cluster size
 constexpr size_t kExpBytes = 1024;         // workspace: row exponents after the tile counters, then the digits
 
@@ -120,74 +119,6 @@ __device__ __forceinline__ void wait_drain(uint64_t* bar, uint32_t parity) {
       atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
       return;
     }
-  }
-}
-
-// D[tmem] (+)= A[smem] . B[smem]^T with signed 8-bit A and B and an int32 accumulator.
-__device__ __forceinline__ void umma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                        uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}"
-      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-// Instruction descriptor: int32 accumulator, signed 8-bit A and B, both K-major, N and M.
-__host__ __device__ constexpr uint32_t umma_idesc_s8(int m, int n) {
-  return (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
-         (static_cast<uint32_t>(m >> 4) << 24);
-}
-
-// Exponent e with 2^e <= max|x| < 2^(e+1) from the largest |x| bit pattern of a bf16 row.
-__device__ __forceinline__ int row_exponent(uint32_t amax_bits) {
-  if (amax_bits >= 0x7f80u) return kNonFinite;
-  if (amax_bits == 0) return 0;
-  const int ef = static_cast<int>(amax_bits >> 7);
-  return ef == 0 ? -127 : ef - 127;  // subnormal maximum: 2^-127 bounds it from above by 2^-126
-}
-
-// X = x / 2^(e - 29) rounded to nearest (ties to even) for one bf16 bit pattern; |X| < 2^30.
-__device__ __forceinline__ int fixed_point(uint32_t b, int e) {
-  const int ef = static_cast<int>((b >> 7) & 0xffu);
-  int mant = static_cast<int>(b & 0x7fu);
-  int f = -126;
-  if (ef != 0) {
-    mant |= 0x80;
-    f = ef - 127;
-  }
-  const int sh = f - e + (kFracBits - 7);  // x = mant * 2^(f - 7) = mant * 2^sh * 2^(e - 29); sh <= 23
-  int X;
-  if (sh >= 0) {
-    X = mant << sh;
-  } else {
-    const int r = -sh;
-    X = r >= 9 ? 0 : (mant + (1 << (r - 1)) - 1 + ((mant >> r) & 1)) >> r;  // mant < 2^8: r >= 9 rounds to 0
-  }
-  return (b & 0x8000u) ? -X : X;
-}
-
-// 8 bf16 activations (one 16-byte chunk) -> 8 bytes of each of the 4 digit planes: X = d0 + 2^8 d1 +
-// 2^16 d2 + 2^24 d3 with every d_p in [-128, 127] (|X| < 2^30 keeps d3 within [-64, 64]).
-__device__ __forceinline__ void digitise8(const uint4& v, int e, uint32_t (&pl)[kPlanes][2]) {
-  const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-  for (int p = 0; p < kPlanes; ++p) pl[p][0] = pl[p][1] = 0;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int X = fixed_point((wv[j >> 1] >> (16 * (j & 1))) & 0xffffu, e);
-    const int d0 = static_cast<int>(static_cast<int8_t>(X & 0xff));
-    const int r1 = (X - d0) >> 8;
-    const int d1 = static_cast<int>(static_cast<int8_t>(r1 & 0xff));
-    const int r2 = (r1 - d1) >> 8;
-    const int d2 = static_cast<int>(static_cast<int8_t>(r2 & 0xff));
-    const int d3 = (r2 - d2) >> 8;
-    const int sh = 8 * (j & 3);
-    pl[0][j >> 2] |= (static_cast<uint32_t>(d0) & 0xffu) << sh;
-    pl[1][j >> 2] |= (static_cast<uint32_t>(d1) & 0xffu) << sh;
-    pl[2][j >> 2] |= (static_cast<uint32_t>(d2) & 0xffu) << sh;
-    pl[3][j >> 2] |= (static_cast<uint32_t>(d3) & 0xffu) << sh;
   }
 }
 

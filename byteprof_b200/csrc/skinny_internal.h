@@ -32,10 +32,22 @@ bool skinny_i8_supported(const void* x, long long ldx, const void* w, int M, int
 int launch_skinny_i8(const void* x, long long ldx, const void* w, const void* w_scale, void* y, long long ldy, int y_f32,
                      int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+// int4 group-128 weights on the tensor cores (skinny_i4tc.cu): workspace bytes for an N x K weight, whether
+// the problem fits (16-byte aligned x, w, scale, zero; ldx a multiple of 8; N a multiple of 8; K a
+// multiple of 128 up to 131072; 1 <= M <= 16), and the launch (prep kernel + main kernel).
+size_t skinny_i4tc_workspace_bytes(int N, int K);
+bool skinny_i4tc_supported(const void* x, long long ldx, const void* w, const void* scale, const void* zero, int M,
+                           int N, int K);
+int launch_skinny_i4tc(const void* x, long long ldx, const uint8_t* w, const void* scale, const void* zero, void* y,
+                       long long ldy, int y_f32, int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t stream);
+
 // Shared host helpers (skinny_tc.cu): a 2D tensor map with 128-byte swizzle, the SM count of the current
 // device, and whether programmatic dependent launch is on (BP_DISABLE_PDL=1 turns it off).
 int tc_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, uint64_t inner, uint64_t outer,
                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapL2promotion promo);
+// Any rank (1-5): dims and box innermost first, strides (bytes) of dims 1.. ; zero fill out of bounds.
+int tc_encode(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+              const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo);
 int tc_sm_count();
 bool tc_pdl_enabled();
 
@@ -44,6 +56,7 @@ bool tc_pdl_enabled();
 unsigned int read_and_clear_device_errors();
 unsigned int read_device_errors_tc();
 unsigned int read_device_errors_i8();
+unsigned int read_device_errors_i4tc();
 unsigned int read_device_errors_glob();
 unsigned int read_device_errors_loc();
 

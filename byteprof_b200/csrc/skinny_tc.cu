@@ -507,6 +507,24 @@ int tc_encode_2d(CUtensorMap* map, CUtensorMapDataType dtype, const void* base, 
   return BP_OK;
 }
 
+int tc_encode(CUtensorMap* map, CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+              const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle, CUtensorMapL2promotion promo) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return fail(BP_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank) st[i] = strides[i];
+  }
+  CUresult r = fn(map, dtype, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st, b, e,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, promo, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(BP_ERR_CUDA, "cuTensorMapEncodeTiled (rank %d) failed (%d)", rank, static_cast<int>(r));
+  return BP_OK;
+}
+
 int tc_sm_count() {
   static int cached[64] = {0};
   int dev = 0;
@@ -616,7 +634,8 @@ namespace bp {
 BP_DEFINE_DEVICE_ERROR_READER(read_device_errors_tc)
 
 unsigned int read_and_clear_device_errors() {
-  return read_device_errors_tc() | read_device_errors_i8() | read_device_errors_glob() | read_device_errors_loc();
+  return read_device_errors_tc() | read_device_errors_i8() | read_device_errors_i4tc() | read_device_errors_glob() |
+         read_device_errors_loc();
 }
 
 }  // namespace bp

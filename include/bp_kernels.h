@@ -47,7 +47,8 @@ enum {
 enum {
   BP_DTYPE_BF16 = 0,
   BP_DTYPE_F32 = 1,
-  BP_DTYPE_INT8 = 2
+  BP_DTYPE_INT8 = 2,
+  BP_DTYPE_INT4 = 3 /* byteprof's tile-major int4 group-128 format (bp_skinny_mm_int4) */
 };
 
 /* Version of this ABI (major * 100 + minor). */
@@ -82,10 +83,11 @@ int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const
                  size_t workspace_bytes, void* stream);
 
 /*
- * Workspace bytes bp_skinny_mm needs for this problem on the current device (0: none needed). The
- * stream-K partial sums of the tensor-core paths live there (int8: also the activations' digit planes,
- * 64 K bytes, and exact int64 partials, about 9.5 MB on 148 SMs; byteprof/optim/skinny.py:125 allocates
- * its split-K workspace per call instead).
+ * Workspace bytes bp_skinny_mm (w_dtype BP_DTYPE_BF16 or BP_DTYPE_INT8) or bp_skinny_mm_int4
+ * (w_dtype BP_DTYPE_INT4) needs for this problem on the current device (0: none needed). The
+ * stream-K partial sums of the tensor-core paths live there (int8 and int4: also the activations'
+ * digit planes, 64 K bytes; int8: exact int64 partials, about 9.5 MB on 148 SMs;
+ * byteprof/optim/skinny.py:125 allocates its split-K workspace per call instead).
  */
 size_t bp_skinny_workspace_bytes(int M, int N, int K, int w_dtype);
 
@@ -119,13 +121,19 @@ int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, i
  *             code j (low nibble) and code j + 64 (high nibble); padding rows are zero
  *   scale     bf16 [K / 128, N];  zero  fp16 [K / 128, N]
  *   x         bf16, 16-byte aligned, ldx a multiple of 8; y as in bp_skinny_mm (bf16 or fp32)
+ *   workspace, workspace_bytes  as in bp_skinny_mm, sized by bp_skinny_workspace_bytes(M, N, K,
+ *             BP_DTYPE_INT4); NULL with 0 bytes selects the CUDA-core kernel, which needs none
  * K must be a multiple of 128 and tile_rows 32 (the format's default; other values return
- * BP_ERR_UNSUPPORTED). Any M (16 rows per launch). No workspace: split-K partials meet in
- * distributed shared memory. Replaces skinny_mm with uint8 weights / _skinny_kernel MODE 3
- * (byteprof/optim/skinny.py:1-19, 46-63, 136-166).
+ * BP_ERR_UNSUPPORTED). Any M (16 rows per launch). With a workspace, N a multiple of 8 and scale and
+ * zero 16-byte aligned, the tensor-core kernel runs: x written exactly as fixed point (as for int8
+ * weights), exact integer group sums, a row of x holding Inf or NaN gives a NaN row of y. Otherwise
+ * the CUDA-core kernel runs (split-K partials meet in distributed shared memory). Either way a row's
+ * result does not depend on M or on the other rows. Replaces skinny_mm with uint8 weights /
+ * _skinny_kernel MODE 3 (byteprof/optim/skinny.py:1-19, 46-63, 136-166).
  */
 int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_packed, const void* scale, const void* zero,
-                      void* y, long long ldy, int y_dtype, int M, int N, int K, int tile_rows, void* stream);
+                      void* y, long long ldy, int y_dtype, int M, int N, int K, int tile_rows, void* workspace,
+                      size_t workspace_bytes, void* stream);
 
 /*
  * Row-wise RMSNorm, bf16 in and out, fp32 arithmetic: y[r, :] = x[r, :] * rsqrt(mean(x[r, :]^2) + eps) * w.

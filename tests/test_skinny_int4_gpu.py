@@ -112,3 +112,78 @@ def test_other_tile_heights_are_refused():
     packed, scale, zero = S.quantize_int4(w, tile_rows=16)
     with pytest.raises(_lib.KernelError, match="32"):
         S.skinny_mm(x_rows(2, 256, 1), packed, scale, zero)
+
+
+# ---- the tensor-core kernel (skinny_i4tc.cu): taken with a workspace, N % 8 == 0 and aligned operands ----
+
+TC_ODD = [(136, 128), (520, 384), (1000, 1152), (8, 256), (2056, 640)]  # partial 128- and 32-row tiles
+
+
+@pytest.mark.parametrize("n,k", TC_ODD)
+def test_tensor_core_kernel_on_partial_tiles(n, k):
+    _, args = make_weights("int4", n, k, seed=n % 13)
+    wd = deq_np("int4", args)
+    for m in list(range(1, 18)) + [33]:
+        x = x_rows(m, k, seed=100 + m)
+        y = S.skinny_mm(x, *args, out=torch.empty(m, n, device="cuda", dtype=torch.float32))
+        assert skinny_ref.nerr(to_np(y), to_np(x), wd) < 1e-5, m
+
+
+@pytest.mark.parametrize("n,k", [(2048, 2048), (1000, 1152), (100352, 2048)])
+@pytest.mark.parametrize("m", [1, 4, 7, 16])
+def test_tensor_core_and_cuda_core_kernels_agree(n, k, m, monkeypatch):
+    _, args = make_weights("int4", n, k, seed=3)
+    x = x_rows(m, k, seed=m)
+    tc = S.skinny_mm(x, *args, out=torch.empty(m, n, device="cuda", dtype=torch.float32))
+    monkeypatch.setenv("BP_SKINNY_PATH", "fma")
+    cc = S.skinny_mm(x, *args, out=torch.empty(m, n, device="cuda", dtype=torch.float32))
+    d = (tc - cc).abs().max().item() / cc.abs().max().item()
+    assert d < 1e-5, d
+
+
+def test_a_non_finite_activation_row_gives_a_nan_row():
+    _, args = make_weights("int4", 1024, 2048, seed=8)
+    x = x_rows(5, 2048, seed=8)
+    ref = S.skinny_mm(x, *args)
+    x[2, 100] = float("inf")
+    x[4, 7] = float("nan")
+    y = S.skinny_mm(x, *args)
+    assert torch.isnan(y[2]).all() and torch.isnan(y[4]).all()
+    assert torch.equal(y[[0, 1, 3]], ref[[0, 1, 3]])
+
+
+def _call_int4(x, args, y, ws, ws_bytes):
+    packed, scale, zero = args
+    m, k = x.shape
+    _lib.call("bp_skinny_mm_int4", x.data_ptr(), k, packed.data_ptr(), scale.data_ptr(), zero.data_ptr(), y.data_ptr(),
+              y.stride(0), _lib.dtype_code(y.dtype), m, y.shape[1], k, packed.shape[2], ws, ws_bytes,
+              torch.cuda.current_stream().cuda_stream)
+
+
+def test_without_a_workspace_the_cuda_core_kernel_runs():
+    _, args = make_weights("int4", 2048, 2048, seed=6)
+    x = x_rows(3, 2048, seed=6)
+    y = torch.empty(3, 2048, device="cuda", dtype=torch.float32)
+    _call_int4(x, args, y, None, 0)
+    torch.cuda.synchronize()
+    assert skinny_ref.nerr(to_np(y), to_np(x), deq_np("int4", args)) < 1e-4
+
+
+def test_a_short_workspace_is_refused():
+    _, args = make_weights("int4", 2048, 2048, seed=6)
+    x = x_rows(3, 2048, seed=6)
+    y = torch.empty(3, 2048, device="cuda", dtype=torch.bfloat16)
+    need = _lib.lib().bp_skinny_workspace_bytes(3, 2048, 2048, _lib.BP_DTYPE_INT4)
+    ws = torch.zeros(need - 1024, dtype=torch.uint8, device="cuda")
+    with pytest.raises(_lib.KernelError, match="workspace"):
+        _call_int4(x, args, y, ws.data_ptr(), ws.numel())
+
+
+def test_the_tile_counters_are_left_at_zero():
+    for n, k, m in [(2048, 2048, 1), (8192, 2048, 16), (1000, 1152, 5)]:
+        _, args = make_weights("int4", n, k, seed=n % 7)
+        S.skinny_mm(x_rows(m, k, seed=m), *args)
+    torch.cuda.synchronize()
+    ws = _lib._workspaces[torch.cuda.current_device()]
+    assert int(ws[:32768].count_nonzero()) == 0
+    assert _lib.device_errors() == 0
