@@ -26,7 +26,8 @@
 //    from L2 but lands behind the weight boxes of the SM's copy queue, about 2 us after it is requested,
 //    so the digit ring must run many groups ahead of the MMAs.
 //  * Warp roles: 0 weight copies; 1 MMA issue and TMEM owner; 2-5 epilogue (warp w reads TMEM lanes
-//    32 (w % 4) ..); 6-9 unpack, each warp a whole group in turn (group j to warp j % 4), the nibbles into
+//    32 (w % 4) ..); 6-9 unpack, each warp a whole group in turn (group j to warp j % W, W = 4, or 3 with
+//    three unpacked-tile slots), the nibbles into
 //    the 128-byte-swizzled K-major layout the MMA reads (bytes 0-63 of a row are the low nibbles and
 //    64-127 the high ones, as in the format); 10 digit copies, once the prep kernel has finished.
 //  * Every barrier operation and tcgen05 instruction costs the issuing thread some 50-150 cycles, so the
@@ -63,6 +64,14 @@ template <int kNB>
 constexpr int a_slots() {  // unpacked tiles (groups)
   return kNB <= 32 ? 5 : 3;
 }
+// Unpack warps in use: at most the number of unpacked-tile slots. A warp waits for its slot to be free
+// only once per group it takes, so the wait for group j is known to follow the release of group
+// j - warps - slots; with warps <= slots that is at least group j - 2 slots, and the slot's parity wait
+// cannot be satisfied by a release two uses old.
+template <int kNB>
+constexpr int unpack_warps() {
+  return a_slots<kNB>() < 4 ? a_slots<kNB>() : 4;
+}
 template <int kNB>
 constexpr int digit_slots() {  // groups of digit tiles: 32 KB (64 KB for 48 and 64 digit rows)
   return (kNB <= 32 ? 32 * 1024 : 64 * 1024) / (kNB * kGroup);
@@ -72,7 +81,6 @@ constexpr int kEpiWarp0 = 2;
 constexpr int kUnpackWarp0 = 6;
 constexpr int kDigitWarp = 10;
 constexpr int kEpiThreads = 128;
-constexpr int kUnpackWarps = 4;
 constexpr size_t kExpBytes = 1024;
 
 struct I4Args {
@@ -352,10 +360,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= kUnpackWarp0) {
     // ---- unpack: packed row r (64 bytes) -> unpacked row r (128 bytes, 128-byte swizzle) ----
-    // Warp uw unpacks groups j = uw, uw + 4, ... Lane l handles 16-byte chunk cp of the packed rows
+    // Warp uw unpacks groups j = uw, uw + kUW, ... Lane l handles 16-byte chunk cp of the packed rows
     // r = 32 it + 8 a + rsel (it, a = 0..3): the eight lanes of each shared-memory phase take rows r and
     // r ^ 5 (four chunks each), so their reads fall in both halves of the banks and their swizzled stores
     // in both halves of the row.
+    constexpr int kUW = unpack_warps<kNB>();
     const int uw = warp - kUnpackWarp0;
     const int i8 = lane & 7, pi = (lane >> 3) & 3;
     const int rsel = i8 < 4 ? pi : (pi ^ 5);
@@ -365,13 +374,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int hi_off = rsel * kGroup + (((cp + 4) ^ rsel) << 4);
     int j = 0;  // group sequence number
     bool ok = true;
-    for (int i = 0; i < n_units && ok; ++i) {
+    for (int i = 0; i < n_units && ok && uw < kUW; ++i) {
       const int st = i % WSU;
       const int g0 = static_cast<int>((u0 + i) % UG) * GB;
       const int ng = G - g0 < GB ? G - g0 : GB;
       bool have_stage = false;
       for (int gg = 0; gg < ng; ++gg, ++j) {
-        if ((j & (kUnpackWarps - 1)) != uw) continue;
+        if (j % kUW != uw) continue;
         if (!have_stage) {
           if (!mbar_wait(&s.full[st], static_cast<uint32_t>(i / WSU) & 1u, abort)) {
             ok = false;
