@@ -199,11 +199,17 @@ __device__ __forceinline__ void store_value(const I4Args& a, int m, int row, flo
 
 // Row exponents, the digit matrix [G][4 M][128] (group-major: one group's planes of all rows are one
 // contiguous tile) and the group sums Xg[g][m] = sum_{k in g} X[m, k] (exact in int64, rounded once to
-// fp32) of the M activation rows, one CTA per row. Values k = base + 2048 j + 8 t (t the thread) are one
-// 16-byte chunk; each half-warp covers one group. The first 8192 values stay in registers between the
+// fp32) of the M activation rows, one CTA per row. Values k = base + 1024 j + 8 t (t the thread) are one
+// 16-byte chunk; each half-warp covers one group. The first 4096 values stay in registers between the
 // exponent pass and the digit pass.
-__global__ void __launch_bounds__(256) i4_prep_kernel(const __nv_bfloat16* x, long long ldx, int M, int K, int* exps,
-                                                      uint8_t* digits, float* xg) {
+// The CTA is small (128 threads, at most 40 registers each) so that it fits on an SM beside a CTA of the
+// main kernel (352 threads x 168 registers of the SM's 65536): launched early, it must not hold an SM
+// that the main kernel's CTAs need, or the CTA left without one starts only when this kernel has ended.
+constexpr int kPrepThreads = 128;
+__global__ void __launch_bounds__(kPrepThreads, 12) i4_prep_kernel(const __nv_bfloat16* x, long long ldx, int M, int K,
+                                                                int* exps, uint8_t* digits, float* xg) {
+  constexpr int kChunk = 8 * kPrepThreads;  // values per chunk row of the CTA
+  constexpr int kPass = 4 * kChunk;
   pdl_launch_dependents();  // the main kernel may start streaming weights now
   pdl_wait_prior_grids();   // x may come from the previous kernel
   const int m = blockIdx.x;
@@ -211,10 +217,10 @@ __global__ void __launch_bounds__(256) i4_prep_kernel(const __nv_bfloat16* x, lo
   const __nv_bfloat16* xr = x + static_cast<long long>(m) * ldx;
   uint32_t amax = 0;
   uint4 keep[4];
-  for (int base = 0; base < K; base += 8192) {
+  for (int base = 0; base < K; base += kPass) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int k = base + 2048 * j + 8 * static_cast<int>(threadIdx.x);
+      const int k = base + kChunk * j + 8 * static_cast<int>(threadIdx.x);
       const uint4 v = k < K ? __ldcg(reinterpret_cast<const uint4*>(xr + k)) : make_uint4(0, 0, 0, 0);
       if (base == 0) keep[j] = v;
       const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
@@ -224,23 +230,23 @@ __global__ void __launch_bounds__(256) i4_prep_kernel(const __nv_bfloat16* x, lo
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) amax = max(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  __shared__ uint32_t red[8];
+  __shared__ uint32_t red[kPrepThreads / 32];
   __shared__ int e_row;
   if (lane == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   if (threadIdx.x == 0) {
     uint32_t mx = 0;
-    for (int w = 0; w < 8; ++w) mx = max(mx, red[w]);
+    for (int w = 0; w < kPrepThreads / 32; ++w) mx = max(mx, red[w]);
     e_row = row_exponent(mx);
     exps[m] = e_row;
   }
   __syncthreads();
   const bool nonfinite = e_row == kNonFinite;  // the row's output is NaN; its digits and sums are zero
   const int e = nonfinite ? 0 : e_row;
-  for (int base = 0; base < K; base += 8192) {  // the loop bound is uniform over the CTA
+  for (int base = 0; base < K; base += kPass) {  // the loop bound is uniform over the CTA
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const int k = base + 2048 * j + 8 * static_cast<int>(threadIdx.x);
+      const int k = base + kChunk * j + 8 * static_cast<int>(threadIdx.x);
       const bool in = k < K;  // uniform over each half-warp (K is a multiple of 128)
       uint4 v = base == 0 ? keep[j] : (in ? __ldcg(reinterpret_cast<const uint4*>(xr + k)) : make_uint4(0, 0, 0, 0));
       if (nonfinite) v = make_uint4(0, 0, 0, 0);
@@ -696,7 +702,7 @@ int launch_skinny_i4tc(const void* x, long long ldx, const uint8_t* w, const voi
   {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(M, 1, 1);
-    cfg.blockDim = dim3(256, 1, 1);
+    cfg.blockDim = dim3(kPrepThreads, 1, 1);
     cfg.stream = stream;
     cfg.attrs = pdl;
     cfg.numAttrs = npdl;
