@@ -8,9 +8,9 @@
 // holds code j in its low nibble and code j + 64 in its high nibble; the 32 rows of a row tile and one group
 // are one contiguous 2 KB block. scale [K / 128, N] bf16, zero [K / 128, N] fp16.
 //
-// This is the CUDA-core kernel, used without a workspace, for shapes the tensor-core kernel does not take
-// (N not a multiple of 8, unaligned scale or zero) and with BP_SKINNY_PATH=fma; skinny_i4tc.cu is the
-// tensor-core kernel. Design:
+// This is the CUDA-core kernel, used below LM-head size (see tc_path_for), without a workspace, for shapes
+// the tensor-core kernel does not take (N not a multiple of 8, unaligned scale or zero) and with
+// BP_SKINNY_PATH=fma; skinny_i4tc.cu is the tensor-core kernel. Design:
 //  * A warp covers 8 rows of a row tile: lane l reads bytes [16 l, 16 l + 16) of the 512-byte slice of
 //    each group block, i.e. row l / 4, chunk c = l % 4 (codes 16 c .. 16 c + 15 and 64 + 16 c .. + 15):
 //    every load instruction of the warp reads 512 contiguous bytes, streamed with an L2 evict-first policy
@@ -257,10 +257,21 @@ int launch_i4(I4Args a, cudaStream_t st) {
   return BP_OK;
 }
 
-// BP_SKINNY_PATH=fma forces the CUDA-core kernel (read at every call; for comparisons).
-bool tc_path_requested() {
+// Which kernel a shape gets. The tensor-core kernel is bound by its MMA rate near 2 TB/s at M <= 4 and
+// has a fixed cost of some 10 us per call (the prep kernel and the pipeline fill); the CUDA-core kernel is
+// bound by its shared-memory reads of the activations, which grow with M. Measured on the OLMo-2-1B
+// shapes: at M = 1 the CUDA-core kernel is 1.5-3x faster below LM-head size and equal on the LM head; at
+// M = 16 the tensor-core kernel is 2-4x faster from 8192 x 2048 up. The choice must not depend on M (a
+// row's result would then depend on M), so it is by size: tensor cores from 2^26 weights (the LM head),
+// which serve the batch-1 decoder as well as the CUDA-core kernel and the verification of many drafted
+// positions far better. BP_SKINNY_PATH=fma forces the CUDA-core kernel, BP_SKINNY_PATH=tc the
+// tensor-core kernel on every shape it takes (read at every call; for comparisons and tests).
+constexpr long long kTcMinWeights = 1LL << 26;
+bool tc_path_for(int N, int K) {
   const char* e = getenv("BP_SKINNY_PATH");
-  return !(e != nullptr && e[0] == 'f');
+  if (e != nullptr && e[0] == 'f') return false;
+  if (e != nullptr && e[0] == 't') return true;
+  return static_cast<long long>(N) * K >= kTcMinWeights;
 }
 
 int dispatch_i4(const I4Args& a, int m, cudaStream_t st) {
@@ -320,7 +331,7 @@ extern "C" int bp_skinny_mm_int4(const void* x, long long ldx, const uint8_t* w_
   a.gb = 1;
   // The tensor-core kernel for every row chunk or for none: the kernel choice depends on the shape, the
   // alignment and the workspace only, so a row's result does not depend on M.
-  const bool tc = !(workspace == nullptr && workspace_bytes == 0) && tc_path_requested() &&
+  const bool tc = !(workspace == nullptr && workspace_bytes == 0) && tc_path_for(N, K) &&
                   skinny_i4tc_supported(x, ldx, w_packed, scale, zero, 1, N, K);
   for (int r0 = 0; r0 < M; r0 += 16) {
     const int m = M - r0 < 16 ? M - r0 : 16;

@@ -29,8 +29,22 @@ def x_rows(m, k, seed):
     return torch.randn(m, k, generator=g, device="cuda").to(torch.bfloat16)
 
 
+@pytest.fixture(params=["default", "tc"])
+def path(request, monkeypatch):
+    """The kernel choice by size (the CUDA-core kernel below LM-head size), or the tensor-core kernel
+    forced on every shape it takes (BP_SKINNY_PATH=tc)."""
+    if request.param == "tc":
+        monkeypatch.setenv("BP_SKINNY_PATH", "tc")
+    return request.param
+
+
+@pytest.fixture
+def tc_path(monkeypatch):
+    monkeypatch.setenv("BP_SKINNY_PATH", "tc")
+
+
 @pytest.mark.parametrize("n,k", REAL + ODD)
-def test_matches_oracle_for_every_m(n, k):
+def test_matches_oracle_for_every_m(n, k, path):
     _, args = make_weights("int4", n, k)
     wd = deq_np("int4", args)
     worst = 0.0
@@ -51,7 +65,7 @@ def test_fp32_output_is_close_to_the_exact_dequantized_product(n, k, m):
     assert skinny_ref.nerr(to_np(y), to_np(x), deq_np("int4", args)) < 1e-4
 
 
-def test_rows_do_not_depend_on_the_other_rows():
+def test_rows_do_not_depend_on_the_other_rows(path):
     _, args = make_weights("int4", 2048, 2048, seed=2)
     x = x_rows(16, 2048, seed=2)
     full = S.skinny_mm(x, *args)
@@ -120,7 +134,7 @@ TC_ODD = [(136, 128), (520, 384), (1000, 1152), (8, 256), (2056, 640)]  # partia
 
 
 @pytest.mark.parametrize("n,k", TC_ODD)
-def test_tensor_core_kernel_on_partial_tiles(n, k):
+def test_tensor_core_kernel_on_partial_tiles(n, k, tc_path):
     _, args = make_weights("int4", n, k, seed=n % 13)
     wd = deq_np("int4", args)
     for m in list(range(1, 18)) + [33]:
@@ -134,6 +148,7 @@ def test_tensor_core_kernel_on_partial_tiles(n, k):
 def test_tensor_core_and_cuda_core_kernels_agree(n, k, m, monkeypatch):
     _, args = make_weights("int4", n, k, seed=3)
     x = x_rows(m, k, seed=m)
+    monkeypatch.setenv("BP_SKINNY_PATH", "tc")
     tc = S.skinny_mm(x, *args, out=torch.empty(m, n, device="cuda", dtype=torch.float32))
     monkeypatch.setenv("BP_SKINNY_PATH", "fma")
     cc = S.skinny_mm(x, *args, out=torch.empty(m, n, device="cuda", dtype=torch.float32))
@@ -141,7 +156,7 @@ def test_tensor_core_and_cuda_core_kernels_agree(n, k, m, monkeypatch):
     assert d < 1e-5, d
 
 
-def test_a_non_finite_activation_row_gives_a_nan_row():
+def test_a_non_finite_activation_row_gives_a_nan_row(tc_path):
     _, args = make_weights("int4", 1024, 2048, seed=8)
     x = x_rows(5, 2048, seed=8)
     ref = S.skinny_mm(x, *args)
@@ -169,7 +184,7 @@ def test_without_a_workspace_the_cuda_core_kernel_runs():
     assert skinny_ref.nerr(to_np(y), to_np(x), deq_np("int4", args)) < 1e-4
 
 
-def test_a_short_workspace_is_refused():
+def test_a_short_workspace_is_refused(tc_path):
     _, args = make_weights("int4", 2048, 2048, seed=6)
     x = x_rows(3, 2048, seed=6)
     y = torch.empty(3, 2048, device="cuda", dtype=torch.bfloat16)
@@ -179,7 +194,7 @@ def test_a_short_workspace_is_refused():
         _call_int4(x, args, y, ws.data_ptr(), ws.numel())
 
 
-def test_the_tile_counters_are_left_at_zero():
+def test_the_tile_counters_are_left_at_zero(tc_path):
     for n, k, m in [(2048, 2048, 1), (8192, 2048, 16), (1000, 1152, 5)]:
         _, args = make_weights("int4", n, k, seed=n % 7)
         S.skinny_mm(x_rows(m, k, seed=m), *args)
@@ -187,3 +202,15 @@ def test_the_tile_counters_are_left_at_zero():
     ws = _lib._workspaces[torch.cuda.current_device()]
     assert int(ws[:32768].count_nonzero()) == 0
     assert _lib.device_errors() == 0
+
+
+def test_the_default_kernel_is_chosen_by_size_only(monkeypatch):
+    """Below 2^26 weights the CUDA-core kernel, from there the tensor-core kernel, for every M."""
+    for (n, k), kind in [((2048, 8192), "fma"), ((100352, 2048), "tc")]:
+        _, args = make_weights("int4", n, k, seed=11)
+        for m in (1, 16):
+            x = x_rows(m, k, seed=20 + m)
+            monkeypatch.delenv("BP_SKINNY_PATH", raising=False)
+            default = S.skinny_mm(x, *args)
+            monkeypatch.setenv("BP_SKINNY_PATH", kind)
+            assert torch.equal(default, S.skinny_mm(x, *args)), (n, k, m)
