@@ -220,3 +220,22 @@ def test_one_workspace_serves_alternating_shapes(kinds):
         x = x_rows(9, k, seed=n % 13)
         y = S.skinny_mm(x, *args)
         assert skinny_ref.nerr(to_np(y), to_np(x), deq_np(kind, args)) < TOL, (kind, n, k)
+
+
+@pytest.mark.parametrize("n,k", [(136, 1000), (2048, 1032), (520, 200), (8192, 1000)])
+@pytest.mark.parametrize("m", [1, 5, 16])
+def test_k_not_a_multiple_of_64_reads_nothing_past_k(n, k, m):
+    """Activation rows padded with NaN past K (row stride K + 64): the tensor-core path reads its last,
+    partial k-block as zeros beyond K, so the padding never reaches y."""
+    from byteprof_b200 import _lib
+    _, (w,) = make_weights("bf16", n, k, seed=k % 17)
+    x = x_rows(m, k, seed=m)
+    big = torch.full((m, k + 64), float("nan"), device="cuda", dtype=torch.bfloat16)
+    big[:, :k] = x
+    y = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    ws, ws_bytes = _lib.skinny_workspace(x.device, m, n, k, _lib.BP_DTYPE_BF16)
+    _lib.call("bp_skinny_mm", big.data_ptr(), k + 64, w.data_ptr(), _lib.BP_DTYPE_BF16, None, y.data_ptr(), n,
+              _lib.BP_DTYPE_BF16, m, n, k, ws, ws_bytes, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert not torch.isnan(y).any()
+    assert torch.equal(y, S.skinny_mm(x, w))
