@@ -7,6 +7,7 @@ are ordered with the surrounding torch work and can be captured in CUDA graphs.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from ctypes import c_float, c_int, c_longlong, c_size_t, c_void_p
 from pathlib import Path
@@ -89,12 +90,18 @@ def exported_symbols() -> list[str]:
     return list(_SIGNATURES)
 
 
+_fns: dict[str, object] = {}
+
+
 def call(name: str, *args) -> None:
     """Calls an entry point and raises KernelError on a non-zero status."""
-    L = lib()
-    st = getattr(L, name)(*args)
+    fn = _fns.get(name)
+    if fn is None:
+        fn = getattr(lib(), name)
+        _fns[name] = fn
+    st = fn(*args)
     if st != BP_OK:
-        msg = L.bp_last_error().decode(errors="replace")
+        msg = lib().bp_last_error().decode(errors="replace")
         raise KernelError(name, st, msg)
 
 
@@ -109,9 +116,26 @@ def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(t: torch.Tensor) -> int:
-    """torch's current stream on the tensor's device, as a raw cudaStream_t."""
+    """torch's current stream on the tensor's device, as a raw cudaStream_t (torch's own raw query when
+    it has one: a Stream object costs more host time than the launch it is for)."""
+    if _raw_stream is not None:
+        return _raw_stream(t.device.index)
     return torch.cuda.current_stream(t.device).cuda_stream
+
+
+_NO_SWITCH = contextlib.nullcontext()
+
+
+def on_device(t: torch.Tensor):
+    """torch.cuda.device(t.device), or nothing when that device is already current (the usual case;
+    entering and leaving the context costs a few microseconds of host time per call)."""
+    if t.device.index == torch.cuda.current_device():
+        return _NO_SWITCH
+    return torch.cuda.device(t.device)
 
 
 def require_cuda(*tensors: torch.Tensor) -> None:

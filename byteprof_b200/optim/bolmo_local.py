@@ -43,7 +43,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | No
     if x.stride(1) != 1 or y.stride(1) != 1 or w.numel() != cols:
         raise ValueError("rmsnorm needs unit column strides and w of cols entries")
     _lib.require_cuda(x, w, y)
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         _lib.call("bp_rmsnorm", x.data_ptr(), x.stride(0), w.data_ptr(), y.data_ptr(), y.stride(0), rows, cols, eps,
                   _lib.stream_of(x))
     return y

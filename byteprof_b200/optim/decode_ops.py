@@ -56,7 +56,7 @@ def rmsnorm_ex(x: torch.Tensor, w: torch.Tensor, eps: float, mode: int = NORM_PL
     if w.numel() != cols:
         raise ValueError("w must hold cols values")
     _lib.require_cuda(x, w, res, s_out, y)
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         _lib.call("bp_rmsnorm_ex", x.data_ptr(), ldx, w.data_ptr(), 1, _lib.ptr(res), ldres, _lib.ptr(s_out), lds,
                   y.data_ptr(), _rows(y)[1], rows, cols, eps, mode, _lib.stream_of(x))
     return y
@@ -85,7 +85,7 @@ def norm_gate(h: torch.Tensor, o: torch.Tensor, w: torch.Tensor, eps: float, out
         raise ValueError("o and out need unit column strides and S rows")
     _bf16(h, o, w, out)
     _lib.require_cuda(h, o, w, out)
-    with torch.cuda.device(h.device):
+    with _lib.on_device(h):
         _lib.call("bp_rmsnorm_ex", h.data_ptr(), h.stride(0), w.data_ptr(), nh, o.data_ptr(), o.stride(0), None, 0,
                   out.data_ptr(), out.stride(0), s * nh, dh, eps, NORM_GATE, _lib.stream_of(h))
     return out
@@ -98,7 +98,7 @@ def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     y = out if out is not None else torch.empty(rows, ffn, dtype=torch.bfloat16, device=gu.device)
     _bf16(gu, y)
     _lib.require_cuda(gu, y)
-    with torch.cuda.device(gu.device):
+    with _lib.on_device(gu):
         _lib.call("bp_swiglu", gu.data_ptr(), ld, y.data_ptr(), _rows(y)[1], rows, ffn, _lib.stream_of(gu))
     return y
 
@@ -109,7 +109,7 @@ def gate_softcap(g: torch.Tensor, bias: torch.Tensor | None, cap: float) -> torc
     if g.dtype != torch.float32 or (bias is not None and (bias.dtype != torch.float32 or bias.numel() != g.shape[1])):
         raise ValueError("fp32 g and bias of n values expected")
     _lib.require_cuda(g, bias)
-    with torch.cuda.device(g.device):
+    with _lib.on_device(g):
         _lib.call("bp_gate_softcap", g.data_ptr(), ld, _lib.ptr(bias), g.data_ptr(), ld, rows, g.shape[1], cap,
                   _lib.stream_of(g))
     return g
@@ -122,7 +122,7 @@ def decode_finish(logits: torch.Tensor, boundary_logit: torch.Tensor | None, out
     if boundary_logit is not None and boundary_logit.dtype != torch.float32:
         raise ValueError("fp32 boundary logit expected")
     _lib.require_cuda(logits, boundary_logit, out)
-    with torch.cuda.device(logits.device):
+    with _lib.on_device(logits):
         _lib.call("bp_decode_finish", logits.data_ptr(), logits.numel(), _lib.ptr(boundary_logit), out.data_ptr(),
                   _lib.stream_of(logits))
     return out
@@ -158,7 +158,7 @@ class DecodeAttention:
         y = out if out is not None else torch.empty(1, d, dtype=torch.bfloat16, device=qkv.device)
         _bf16(q_norm, k_norm, y)
         _lib.require_cuda(qkv, q_norm, k_norm, cos, sin, pos, y)
-        with torch.cuda.device(qkv.device):
+        with _lib.on_device(qkv):
             _lib.call("bp_decode_attention", qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(),
                       sin.data_ptr(), pos.data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(), y.data_ptr(),
                       self.nh, self.hd, self.max_pos, eps, self.hd ** -0.5, _lib.stream_of(qkv))
@@ -196,7 +196,7 @@ class GlobStep:
         if pos.dtype != torch.int64:
             raise ValueError("pos must be a device int64")
         _lib.require_cuda(x, value_out, pos)
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x):
             _lib.call("bp_glob_step", ctypes.addressof(self.layers), len(self.keep), x.data_ptr(),
                       self.out_norm.data_ptr(), value_out.data_ptr(), pos.data_ptr(), self.cos.data_ptr(),
                       self.sin.data_ptr(), self.max_pos, self.eps, self.workspace.data_ptr(), self.workspace.numel(),
@@ -237,13 +237,13 @@ class LocStep:
                 _lib.stream_of(self.workspace))
 
     def enc(self, parity: int, embed, byte, enc_norm, w_patch, w_boundary, e_out, patch_out, boundary_logit) -> None:
-        with torch.cuda.device(embed.device):
+        with _lib.on_device(embed):
             _lib.call("bp_loc_enc_step", ctypes.addressof(self.tables[parity]), embed.data_ptr(), byte.data_ptr(),
                       enc_norm.data_ptr(), w_patch.data_ptr(), w_boundary.data_ptr(), e_out.data_ptr(),
                       patch_out.data_ptr(), boundary_logit.data_ptr(), *self._common(parity))
 
     def dec(self, parity: int, e_in, value, w_in, final_norm, lm_head, boundary_logit, logits, out) -> None:
-        with torch.cuda.device(e_in.device):
+        with _lib.on_device(e_in):
             _lib.call("bp_loc_dec_step", ctypes.addressof(self.tables[parity]), e_in.data_ptr(), value.data_ptr(),
                       w_in.data_ptr(), final_norm.data_ptr(), lm_head.data_ptr(), boundary_logit.data_ptr(),
                       logits.data_ptr(), out.data_ptr(), *self._common(parity))

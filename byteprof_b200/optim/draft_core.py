@@ -30,7 +30,7 @@ def mlstm_scan(state_in: tuple[torch.Tensor, ...], q: torch.Tensor, k: torch.Ten
     if h is not None and h.shape[0] < t:
         raise ValueError("h has fewer positions than q")
     _lib.require_cuda(*state_in, *state_out, q, k, v, i, f, h)
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         _lib.call("bp_mlstm_scan", state_in[0].data_ptr(), state_in[1].data_ptr(), state_in[2].data_ptr(),
                   q.data_ptr(), k.data_ptr(), v.data_ptr(), i.data_ptr(), f.data_ptr(), _lib.ptr(h),
                   state_out[0].data_ptr(), state_out[1].data_ptr(), state_out[2].data_ptr(), None, None, None,

@@ -67,7 +67,7 @@ def multistep_fw(cur: tuple[torch.Tensor, ...], q: torch.Tensor, k: torch.Tensor
     if h.shape[0] < t:
         raise ValueError("h has fewer positions than q")
     _lib.require_cuda(*cur, q, k, v, i, f, h, nstart, mstart)
-    with torch.cuda.device(q.device):
+    with _lib.on_device(q):
         _lib.call("bp_mlstm_scan", cur[0].data_ptr(), cur[1].data_ptr(), cur[2].data_ptr(), q.data_ptr(), k.data_ptr(),
                   v.data_ptr(), i.data_ptr(), f.data_ptr(), h.data_ptr(), None, None, None, nstart.data_ptr(),
                   mstart.data_ptr(), None, t, nh, dq, dv, q.stride(0), v.stride(0), i.stride(0), h.stride(0),
@@ -83,7 +83,7 @@ def lazy_commit(cur: tuple[torch.Tensor, ...], k: torch.Tensor, v: torch.Tensor,
     if length.dtype != torch.int64 or length.numel() != 1:
         raise ValueError("length must be a one-element int64 device tensor")
     _lib.require_cuda(*cur, k, v, i, f, length, nstart, mstart)
-    with torch.cuda.device(k.device):
+    with _lib.on_device(k):
         # q is not read for the state: k stands in so that every prefetched address is valid.
         _lib.call("bp_mlstm_scan", cur[0].data_ptr(), nstart.data_ptr(), mstart.data_ptr(), k.data_ptr(),
                   k.data_ptr(), v.data_ptr(), i.data_ptr(), f.data_ptr(), None, cur[0].data_ptr(), cur[1].data_ptr(),
@@ -100,5 +100,5 @@ def accept(ids: torch.Tensor, tok: torch.Tensor, out: torch.Tensor, s: int, smax
     if ids.numel() < s or tok.numel() < s or out.numel() <= smax:
         raise ValueError("ids/tok need s entries and out smax + 1")
     _lib.require_cuda(ids, tok, out)
-    with torch.cuda.device(out.device):
+    with _lib.on_device(out):
         _lib.call("bp_mlstm_accept", ids.data_ptr(), tok.data_ptr(), out.data_ptr(), s, smax, _lib.stream_of(out))

@@ -81,7 +81,7 @@ def skinny_mm(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = Non
     if kind == "int4":
         if scale.dtype != torch.bfloat16 or zero.dtype != torch.float16:
             raise ValueError("int4 scale must be bf16 and zero fp16 (as quantize_int4 makes them for bf16 weights)")
-        with torch.cuda.device(x.device):
+        with _lib.on_device(x):
             ws, ws_bytes = _lib.skinny_workspace(x.device, m, n, k, _lib.BP_DTYPE_INT4)
             _lib.call("bp_skinny_mm_int4", x.data_ptr(), k, w.data_ptr(), scale.data_ptr(), zero.contiguous().data_ptr(),
                       y.data_ptr(), y.stride(0), _lib.dtype_code(y.dtype), m, n, k, w.shape[2], ws, ws_bytes,
@@ -90,7 +90,7 @@ def skinny_mm(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = Non
     if scale is not None and kind == "int8" and scale.dtype != torch.bfloat16:
         scale = scale.to(torch.bfloat16)
     wcode = _lib.dtype_code(w.dtype)
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         ws, ws_bytes = _lib.skinny_workspace(x.device, m, n, k, wcode)
         _lib.call("bp_skinny_mm", x.data_ptr(), k, w.data_ptr(), wcode, _lib.ptr(scale if kind == "int8" else None),
                   y.data_ptr(), y.stride(0), _lib.dtype_code(y.dtype), m, n, k, ws, ws_bytes, _lib.stream_of(x))

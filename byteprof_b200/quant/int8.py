@@ -37,7 +37,7 @@ def gemv_int8(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, cfg: tuple[
     x = x.contiguous()
     if scale.dtype != torch.bfloat16:
         scale = scale.to(torch.bfloat16)
-    with torch.cuda.device(x.device):
+    with _lib.on_device(x):
         ws, ws_bytes = _lib.skinny_workspace(x.device, 1, n, k, _lib.BP_DTYPE_INT8)
         _lib.call("bp_gemv_int8", x.data_ptr(), w.contiguous().data_ptr(), scale.contiguous().data_ptr(), y.data_ptr(),
                   _lib.dtype_code(y.dtype), n, k, ws, ws_bytes, _lib.stream_of(x))
