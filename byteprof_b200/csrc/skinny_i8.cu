@@ -531,7 +531,7 @@ I8Partition i8_partition(int N, int K) {
     // few tiles: 128-row tiles, each tile's K range split over a cluster of S CTAs
     p.tn = 128;
     p.tiles = tiles128;
-    int S = sms / p.tiles;
+    int S = 2 * sms / p.tiles;  // two CTAs fit per SM: two producers per SM (as in the bf16 kernel)
     if (S > kMaxClusterSplit) S = kMaxClusterSplit;
     if (S > p.kblocks) S = p.kblocks;
     p.S = S < 1 ? 1 : S;

@@ -401,8 +401,11 @@ Partition partition(int N, int K) {
   p.units = static_cast<long long>(p.tiles) * p.kblocks;
   const int sms = tc_sm_count();
   if (2 * p.tiles <= sms) {
-    // few tiles: split each tile's K range over a cluster of S CTAs (no workspace, no global fix-up)
-    int S = sms / p.tiles;
+    // few tiles: split each tile's K range over a cluster of S CTAs (no workspace, no global fix-up). Two
+    // CTAs fit per SM, so S = 2 SMs / tiles: every SM then runs two producers, and a single producer issuing
+    // a weight and an activation copy per stage streams well below the SM's share of HBM (measured on
+    // 8192 x 2048: 9.9 us with S = 2, 8.5 us with S = 4)
+    int S = 2 * sms / p.tiles;
     if (S > kMaxClusterSplit) S = kMaxClusterSplit;
     if (S > p.kblocks) S = p.kblocks;
     p.S = S < 1 ? 1 : S;
