@@ -632,7 +632,7 @@ def cpu_sweep(max_calls: int, min_seconds: float, max_seconds: float, threads: i
             break
     dt = time.perf_counter() - t0
     return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "calls": calls,
-            "seconds": round(dt, 2)}
+            "seconds": round(dt, 2), "seconds_raw": dt}
 
 
 def run_reference(args) -> int:
@@ -644,10 +644,10 @@ def run_reference(args) -> int:
     cpu_sweep(max_calls=args.warmup, min_seconds=0.0, max_seconds=60.0, threads=threads)
     res = cpu_sweep(max_calls=args.steps, min_seconds=0.0, max_seconds=150.0, threads=threads)
     sample = (f"{res['calls']} of {args.steps} steps (one sweep cell = one F.linear call per step, cells in sweep "
-              f"order) in {res['seconds']} s, torch bf16 on the host = byteprof SkinnyLinear's CPU branch")
+              f"order) in {res['seconds_raw']:.4f} s, torch bf16 on the host = byteprof SkinnyLinear's CPU branch")
     line = {"metric": METRIC, "value": res["value"], "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
             "steps": res["calls"], "warmup": args.warmup,
-            "ms_per_step": round(res["seconds"] * 1e3 / max(1, res["calls"]), 3),
+            "ms_per_step": round(res["seconds_raw"] * 1e3 / max(1, res["calls"]), 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "BASELINE configs[1]: bf16 skinny sweep M in {1,2,4,8,16} x OLMo-2-1B shapes",
                        "shapes": [f"{n}x{k}" for n, k in SHAPES], "ms": list(MS)},
