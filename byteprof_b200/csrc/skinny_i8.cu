@@ -54,6 +54,7 @@ constexpr int kEpiWarp0 = 3;
 constexpr int kGroup = 128;                // epilogue threads
 constexpr int kMaxClusterSplit = 8;        // portable cluster size
 constexpr size_t kExpBytes = 1024;         // workspace: row exponents after the tile counters, then the digits
+constexpr int kL2Ahead = 7;                // units requested into L2 beyond the weight ring at the start
 
 // TN = 256: stream-K, one CTA per SM with 160 KB of weights in flight. TN = 128: cluster split-K, where a
 // CTA streams only a few units: a shorter ring, so that two CTAs fit per SM and the next call's CTAs start
@@ -270,6 +271,14 @@ __global__ void __launch_bounds__(kThreads, I8Cfg<TN>::kMinBlocks)
         mbar_arrive_expect_tx(&s.full[st], Cfg::kWBytes);
         tma_load_2d_hint(s.w[st], &tw, &s.full[st], kb * kBK, t * TN, pol);
         issued = i + 1;
+        if (i == kWStages - 1) {
+          // The ring is full before the digits (the prep kernel's output) can arrive: request the next units
+          // into L2, so that the ring refills from L2 once the MMAs start.
+          for (int j = kWStages; j < n_units && j < kWStages + kL2Ahead; ++j) {
+            const long long uj = u0 + j;
+            tma_prefetch_l2_2d(&tw, static_cast<int>(uj % KB) * kBK, static_cast<int>(uj / KB) * TN);
+          }
+        }
       }
       for (int st = 0; st < kWStages && st < issued; ++st) {  // drain
         const int i_last = st + kWStages * ((issued - 1 - st) / kWStages);

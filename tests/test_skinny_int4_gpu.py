@@ -94,7 +94,7 @@ def test_kernel_writes_only_the_output_block(m):
     assert skinny_ref.nerr(to_np(out), to_np(x), deq_np("int4", args)) < TOL
 
 
-def test_cuda_graph_replay_equals_eager():
+def test_cuda_graph_replay_equals_eager(path):
     _, args = make_weights("int4", 2816, 2048, seed=5)
     x = x_rows(4, 2048, seed=5)
     y = torch.empty(4, 2816, device="cuda", dtype=torch.bfloat16)
