@@ -54,8 +54,22 @@ struct ScanArgs {
   int T, NH, DV;
   long long str_qk, str_v, str_if, str_h;
   int gate_f32;
+  int stage_c;  // C moves through shared memory with 16-byte copies (c_in and c_out 16-byte aligned)
   float qk_scale, eps;
 };
+
+// The CTA's [DQ x 16] fp32 block of C moves between global memory and the compute threads' registers
+// through shared memory, so that every warp access covers whole 64-byte rows (with per-thread scalar
+// accesses a warp touches 16 rows x 8 bytes, four times the L2 requests for the same bytes). Word of
+// (row r, column c): row r sits in physical row r ^ ((r >> 5) & 1), its 16-byte chunk c / 4 in slot
+// (c / 4) ^ ((r >> 3) & 3). A compute thread's access to rows 8l + e (l = 0..15, e fixed) then spreads
+// the 32 lanes over 16 banks (two lanes per bank, the minimum for the warp's two columns), while 8
+// consecutive rows stay one contiguous 512-byte run for the chunk copies.
+__device__ __forceinline__ int stage_word(int r, int c) {
+  return (r ^ ((r >> 5) & 1)) * kBV + (((c >> 2) ^ ((r >> 3) & 3)) << 2) + (c & 3);
+}
+
+__device__ __forceinline__ void compute_sync(int nthreads) { asm volatile("bar.sync 1, %0;" ::"r"(nthreads) : "memory"); }
 
 template <typename T>
 __device__ __forceinline__ float to_f(T v);
@@ -160,20 +174,20 @@ __device__ __forceinline__ void gate_chunk(const ScanArgs& a, int head, int j, i
     const float sig = __fdiv_rn(1.0f, d);
     fl = static_cast<float>(log(static_cast<double>(sig)));
   }
-  // The stabiliser recurrence is sequential (each fp32 add rounds): every lane runs it.
+  // The stabiliser recurrence is sequential (each fp32 add rounds): every lane runs it, over the
+  // chunk's valid positions only (`count` is the same in every lane).
+  const int count = min(kGC, n_steps - j * kGC);
   float m_prev = m_run, my_m = 0.0f, my_a = 0.0f;
-  for (int t = 0; t < kGC; ++t) {
+  for (int t = 0; t < count; ++t) {
     const float flt = __shfl_sync(0xffffffffu, fl, t);
     const float ivt = __shfl_sync(0xffffffffu, iv, t);
-    if (j * kGC + t < n_steps) {
-      const float sum = __fadd_rn(flt, m_prev);
-      const float mn = fmaxf(sum, ivt);
-      if (lane == t) {
-        my_m = mn;
-        my_a = __fsub_rn(sum, mn);
-      }
-      m_prev = mn;
+    const float sum = __fadd_rn(flt, m_prev);
+    const float mn = fmaxf(sum, ivt);
+    if (lane == t) {
+      my_m = mn;
+      my_a = __fsub_rn(sum, mn);
     }
+    m_prev = mn;
   }
   m_run = m_prev;
   if (s < n_steps) {
@@ -190,6 +204,7 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
   __shared__ __align__(16) T ring[kDepth][Cfg::STAGE];
   __shared__ float g_f[64], g_i[64], g_mx[64];
   __shared__ float hb[2][kBV];
+  extern __shared__ __align__(16) float cst[];  // [DQ x 16] C staging (stage_word layout) when a.stage_c
 
   const int head = blockIdx.y;
   const int c0 = blockIdx.x * kBV;
@@ -249,6 +264,17 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
     }
     for (int s = 0; s < kDepth - 1; ++s) issue(s);
     gate_chunk<T>(a, head, 0, n_steps, m_run, g_f, g_i, g_mx);
+  } else if (a.stage_c) {
+    // 16-byte chunk i = (row i / 4, columns 4 (i % 4) ..): a warp copies 8 whole rows per instruction
+    for (int i = tid; i < DQ * 4; i += Cfg::NCOMP)
+      cp_async16(cst + stage_word(i >> 2, 4 * (i & 3)), cbase + static_cast<long long>(i >> 2) * a.DV + 4 * (i & 3));
+    cp_async_commit();
+    cp_async_wait<0>();
+    compute_sync(Cfg::NCOMP);
+#pragma unroll
+    for (int ch = 0; ch < Cfg::CH; ++ch)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) creg[ch * 8 + e] = cst[stage_word((l + Cfg::TPC * ch) * 8 + e, col)];
   } else {
 #pragma unroll
     for (int ch = 0; ch < Cfg::CH; ++ch)
@@ -292,7 +318,7 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
         qn_prev = qn;
       }
       __syncwarp();
-      if ((t & (kGC - 1)) == 0) gate_chunk<T>(a, head, t / kGC + 1, n_steps, m_run, g_f, g_i, g_mx);
+      if ((t & (kGC - 1)) == 0 && t + kGC < n_steps) gate_chunk<T>(a, head, t / kGC + 1, n_steps, m_run, g_f, g_i, g_mx);
     } else {
       float hs = 0.0f;
       if constexpr (sizeof(T) == 2) {
@@ -347,10 +373,29 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
       }
     }
   }
+  // ---- epilogue -----------------------------------------------------------------------------------
+  // The compute threads write C first (it needs nothing from the producer), so that the stores are
+  // under way while the barrier below hands the producer the last position's h sums.
+  if (!producer && a.c_out != nullptr) {
+    float* obase = a.c_out + static_cast<long long>(head) * DQ * a.DV + c0;
+    if (a.stage_c) {
+#pragma unroll
+      for (int ch = 0; ch < Cfg::CH; ++ch)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) cst[stage_word((l + Cfg::TPC * ch) * 8 + e, col)] = creg[ch * 8 + e];
+      compute_sync(Cfg::NCOMP);
+      for (int i = tid; i < DQ * 4; i += Cfg::NCOMP)
+        *reinterpret_cast<float4*>(obase + static_cast<long long>(i >> 2) * a.DV + 4 * (i & 3)) =
+            *reinterpret_cast<const float4*>(cst + stage_word(i >> 2, 4 * (i & 3)));
+    } else {
+#pragma unroll
+      for (int ch = 0; ch < Cfg::CH; ++ch)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) obase[static_cast<long long>((l + Cfg::TPC * ch) * 8 + e) * a.DV + col] = creg[ch * 8 + e];
+    }
+  }
   cp_async_wait<0>();
   __syncthreads();
-
-  // ---- epilogue -----------------------------------------------------------------------------------
   if (producer) {
     if (want_h && n_steps > 0 && lane < kBV) {
       const int t = n_steps - 1;
@@ -364,12 +409,6 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
         for (int r = 0; r < Cfg::RPL; ++r) a.n_out[head * DQ + prow(r)] = nreg[r];
       if (a.m_out != nullptr && lane == 0) a.m_out[head] = m_run;
     }
-  } else if (a.c_out != nullptr) {
-    float* obase = a.c_out + static_cast<long long>(head) * DQ * a.DV + c0;
-#pragma unroll
-    for (int ch = 0; ch < Cfg::CH; ++ch)
-#pragma unroll
-      for (int e = 0; e < 8; ++e) obase[static_cast<long long>((l + Cfg::TPC * ch) * 8 + e) * a.DV + col] = creg[ch * 8 + e];
   }
 }
 
@@ -384,11 +423,29 @@ __global__ void accept_kernel(const int64_t* ids, const int64_t* tok, int64_t* o
   out[smax] = n;
 }
 
+// Opts the kernel into `bytes` of dynamic shared memory, once per device.
+template <typename K>
+int allow_dynamic_smem(K kernel, size_t bytes, bool* done) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return fail(BP_ERR_CUDA, "cudaGetDevice failed");
+  if (done[dev]) return BP_OK;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "cudaFuncSetAttribute(smem %zu): %s", bytes, cudaGetErrorString(e));
+  done[dev] = true;
+  return BP_OK;
+}
+
 template <int DQ, typename T>
 int launch_scan(const ScanArgs& a, cudaStream_t s) {
   using Cfg = ScanCfg<DQ, T>;
   dim3 grid(a.DV / kBV, a.NH, 1);
-  mlstm_scan_kernel<DQ, T><<<grid, Cfg::NTHREADS, 0, s>>>(a);
+  const size_t smem = a.stage_c ? static_cast<size_t>(DQ) * kBV * sizeof(float) : 0;
+  static bool attr_done[64] = {};
+  if (smem > 0) {
+    const int st = allow_dynamic_smem(mlstm_scan_kernel<DQ, T>, smem, attr_done);
+    if (st != BP_OK) return st;
+  }
+  mlstm_scan_kernel<DQ, T><<<grid, Cfg::NTHREADS, smem, s>>>(a);
   return check_launch("mlstm scan launch");
 }
 
@@ -442,6 +499,7 @@ extern "C" int bp_mlstm_scan(const float* c_in, const float* n_in, const float* 
   a.T = T; a.NH = NH; a.DV = DV;
   a.str_qk = str_t_qk; a.str_v = str_t_v; a.str_if = str_t_if; a.str_h = str_t_h;
   a.gate_f32 = gate_dtype == BP_DTYPE_F32;
+  a.stage_c = al16(c_in) && (c_out == nullptr || al16(c_out));
   a.qk_scale = qk_scale; a.eps = eps;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   return dtype == BP_DTYPE_BF16 ? dispatch_dq<__nv_bfloat16>(a, DQ, s) : dispatch_dq<float>(a, DQ, s);
