@@ -539,14 +539,14 @@ def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 2
     return out
 
 
-def scan_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
-    """NH=4, dk=dv=512, T positions from a zero state, h and the final state."""
-    from byteprof_b200.optim.draft_core import mlstm_scan
-
-    nh, d = 4, 512
-    out = {}
-    for t in SCAN_TS:
-        g0 = torch.Generator(device=device).manual_seed(500 + t)
+def scan_problems(device: torch.device, t: int, nh: int = 4, d: int = 512) -> list:
+    """Independent scan problems of T positions (BASELINE configs[3] shapes and distributions), enough of
+    them that their states, inputs and outputs together exceed RING_BYTES (> 2x L2): a graph that runs
+    them one after another reads every state from DRAM, not from L2."""
+    per = 3 * nh * d * d * 4 + t * (4 * nh * d * 2 + 2 * nh * 4)  # C in + out (+ slack), q, k, v, h, i, f
+    out = []
+    for r in range(max(2, math.ceil(RING_BYTES / per))):
+        g0 = torch.Generator(device=device).manual_seed(500 + 7919 * r + t)
         q, k, v = ((torch.randn(t, nh, d, generator=g0, device=device) / d ** 0.5).to(torch.bfloat16) for _ in range(3))
         i = torch.randn(t, nh, 1, generator=g0, device=device)
         f = torch.randn(t, nh, 1, generator=g0, device=device) + 3.0
@@ -554,14 +554,56 @@ def scan_cells(device: torch.device, peak: float, reps: int = 20) -> dict:
                  torch.zeros(1, nh, 1, device=device))
         st_out = tuple(torch.empty_like(s) for s in st_in)
         h = torch.empty(t, nh, d, device=device, dtype=torch.bfloat16)
-        g = capture(lambda: mlstm_scan(st_in, q, k, v, i, f, h, st_out, 1e-6))
-        time_graph_replays(g, 3)
-        us = time_graph_replays(g, reps) * 1e3 / reps
-        # minimum traffic: state read + written once, plus q, k, v, i, f in and h out per position
-        nbytes = 2 * (nh * d * d * 4 + nh * d * 4 + nh * 4) + t * (3 * nh * d * 2 + 2 * nh * 4 + nh * d * 2)
-        out[f"T{t}"] = {"us": round(us, 2), "us_per_step": round(us / t, 4), "gbs": round(nbytes / (us * 1e-6) / 1e9, 1)}
-        del g
+        out.append((st_in, q, k, v, i, f, h, st_out))
     return out
+
+
+def scan_bytes(t: int, nh: int = 4, d: int = 512) -> int:
+    """Minimum traffic of one scan: state read + written once, plus q, k, v, i, f in and h out per position."""
+    return 2 * (nh * d * d * 4 + nh * d * 4 + nh * 4) + t * (3 * nh * d * 2 + 2 * nh * 4 + nh * d * 2)
+
+
+def scan_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
+    """NH=4, dk=dv=512, T positions from a zero state, h and the final state. One graph
+    runs a rotation of independent problems larger than L2 (cold state); time per scan = replay / problems."""
+    from byteprof_b200.optim.draft_core import mlstm_scan
+
+    out = {}
+    for t in SCAN_TS:
+        probs = scan_problems(device, t)
+        g = capture(lambda: [mlstm_scan(p[0], *p[1:7], p[7], 1e-6) for p in probs])
+        time_graph_replays(g, 3)
+        us = time_graph_replays(g, reps) * 1e3 / (reps * len(probs))
+        out[f"T{t}"] = {"us": round(us, 2), "us_per_step": round(us / t, 4),
+                        "gbs": round(scan_bytes(t) / (us * 1e-6) / 1e9, 1), "problems_in_rotation": len(probs)}
+        del g, probs
+        torch.cuda.empty_cache()
+    return out
+
+
+def run_scan_case(args, t: int) -> int:
+    """`--case scan,T`: the scan alone over its cold rotation (for ncu captures): W eager warm-up scans, then
+    K timed scans on the current stream, CUDA events. Prints us per scan and GB/s of minimum traffic."""
+    from byteprof_b200.optim.draft_core import mlstm_scan
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    probs = scan_problems(dev, t)
+    for j in range(args.warmup):
+        p = probs[j % len(probs)]
+        mlstm_scan(p[0], *p[1:7], p[7], 1e-6)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for j in range(args.steps):
+        p = probs[(args.warmup + j) % len(probs)]
+        mlstm_scan(p[0], *p[1:7], p[7], 1e-6)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) * 1e3 / args.steps
+    print(json.dumps({"case": f"scan|T{t}", "us": round(us, 3), "gbs": round(scan_bytes(t) / (us * 1e-6) / 1e9, 1),
+                      "bytes": scan_bytes(t), "launches": args.warmup + args.steps}), flush=True)
+    return 0
 
 
 def e2e_sweep(sweep: Sweep, steps: int) -> tuple[float, int, int]:
@@ -784,6 +826,8 @@ def run_case(args) -> int:
     from byteprof_b200.quant.int8 import quantize_rowwise_int8
 
     parts = args.case.split(",")
+    if parts[0] == "scan":
+        return run_scan_case(args, int(parts[1]))
     n, k, m = (int(v) for v in parts[:3])
     kind = parts[3] if len(parts) > 3 else "bf16"
     dev = torch.device("cuda", 0)
@@ -848,7 +892,7 @@ def main(argv=None) -> int:
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the per-cell, int8, scan and CPU passes")
-    ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8|int4]: time one sweep cell alone (ncu captures)")
+    ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8|int4] or scan,T: time one sweep cell or one scan alone (ncu captures)")
     ap.add_argument("--graph", action="store_true", help="with --case: time a CUDA graph of the weight ring")
     ap.add_argument("--decode", type=int, default=0, metavar="N",
                     help="only N bytes of the Bolmo-shaped decode, each opening a patch (short runs for ncu)")

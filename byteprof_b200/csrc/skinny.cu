@@ -337,10 +337,14 @@ extern "C" int bp_device_errors(unsigned int* flags) {
   return check_launch("device error read");
 }
 
-extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale, void* y,
-                            long long ldy, int y_dtype, int M, int N, int K, void* workspace, size_t workspace_bytes,
-                            void* stream) {
-  using namespace bp;
+namespace bp {
+namespace {
+
+// The body of bp_skinny_mm. `cuda_cores` keeps every row chunk on the CUDA-core kernel (bp_gemv_int8's
+// rule below); otherwise the tensor-core kernel takes every shape it supports.
+int skinny_entry(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale, void* y,
+                 long long ldy, int y_dtype, int M, int N, int K, void* workspace, size_t workspace_bytes,
+                 void* stream, bool cuda_cores) {
   clear_error();
   if (M < 0 || N < 0 || K < 0) return fail(BP_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d K=%d)", M, N, K);
   if (w_dtype != BP_DTYPE_BF16 && w_dtype != BP_DTYPE_INT8)
@@ -380,7 +384,7 @@ extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_d
     const int m = M - r0 < 16 ? M - r0 : 16;
     a.x = static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r0) * ldx;
     a.y = static_cast<char*>(y) + static_cast<long long>(r0) * ldy * static_cast<long long>(ysz);
-    if (tc_path_enabled() && skinny_tc_supported(a.x, ldx, w, m, N, K, is8))
+    if (!cuda_cores && tc_path_enabled() && skinny_tc_supported(a.x, ldx, w, m, N, K, is8))
       st = launch_skinny_tc(a.x, ldx, w, w_scale, a.y, ldy, a.y_f32, m, N, K, is8, workspace, workspace_bytes, s);
     else
       st = is8 ? dispatch_m<int8_t>(a, m, vec, s) : dispatch_m<__nv_bfloat16>(a, m, vec, s);
@@ -389,7 +393,25 @@ extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_d
   return BP_OK;
 }
 
+}  // namespace
+}  // namespace bp
+
+extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale, void* y,
+                            long long ldy, int y_dtype, int M, int N, int K, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  return bp::skinny_entry(x, ldx, w, w_dtype, w_scale, y, ldy, y_dtype, M, N, K, workspace, workspace_bytes, stream,
+                          false);
+}
+
+// One activation row only, so the kernel may depend on the shape and M = 1 together: with N <= 4096 output
+// rows the tensor-core kernel has at most 32 weight tiles and two launches (digit prep + main) of fixed
+// latency, and the CUDA-core kernel's single launch is faster (measured, cold L2: 2048 x 2048 4.4 us
+// against 6.6, 2048 x 8192 7.9 against 11.0); from 8192 rows the tensor-core kernel is (8192 x 2048 8.2
+// against 9.6 us).
+constexpr int kGemvCudaCoreMaxN = 4096;
+
 extern "C" int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,
                             void* workspace, size_t workspace_bytes, void* stream) {
-  return bp_skinny_mm(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, workspace, workspace_bytes, stream);
+  return bp::skinny_entry(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, workspace, workspace_bytes, stream,
+                          N <= kGemvCudaCoreMaxN);
 }

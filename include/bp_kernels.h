@@ -108,7 +108,8 @@ int bp_skinny_mm_static_scratch(const void* x, long long ldx, const void* w, int
 
 /*
  * int8 weight-only GEMV for one activation row: y[1, N] = scale[n] * sum_k x[k] * q[n, k].
- * bp_skinny_mm with M = 1 and int8 weights, including its workspace rule
+ * bp_skinny_mm with M = 1 and int8 weights, including its workspace rule, except that with N <= 4096 it
+ * always takes the CUDA-core kernel (one launch; faster than the tensor-core kernel's two at that size)
  * (byteprof/quant/triton_int8.py:15-47).
  */
 int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,

@@ -34,6 +34,26 @@ def test_gemv_real_shapes_batch_one(n, k):
     _close(gemv_int8(x, q, s), _ref(x, q, s))
 
 
+@pytest.mark.parametrize("n,k,cuda_cores", [(2048, 2048, True), (4096, 2048, True), (2048, 8192, True),
+                                            (4104, 2048, False), (8192, 2048, False)])
+def test_gemv_kernel_choice_by_output_rows(n, k, cuda_cores, monkeypatch):
+    """gemv_int8 takes the CUDA-core kernel up to 4096 output rows and the tensor-core kernel above: its
+    output is bit-identical to skinny_mm at M = 1 forced onto that kernel (BP_SKINNY_PATH=fma) or left on
+    its default (the tensor-core kernel for these aligned shapes)."""
+    from byteprof_b200.optim.skinny import skinny_mm
+
+    g = torch.Generator().manual_seed(n + k)
+    q, s = quantize_rowwise_int8((torch.randn(n, k, generator=g) * 0.02).to("cuda", torch.bfloat16))
+    x = torch.randn(1, k, generator=g).to("cuda", torch.bfloat16)
+    y = gemv_int8(x, q, s)
+    _close(y, _ref(x, q, s))
+    if cuda_cores:
+        monkeypatch.setenv("BP_SKINNY_PATH", "fma")
+    want = skinny_mm(x, q, s)
+    monkeypatch.delenv("BP_SKINNY_PATH", raising=False)
+    assert torch.equal(y, want)
+
+
 @pytest.mark.parametrize("n,k", [(37, 1000), (1, 8), (3, 129), (1025, 2049), (16, 2047), (7, 5000), (24, 128)])
 def test_gemv_odd_sizes_not_multiples_of_block(n, k):
     q, s = quantize_rowwise_int8((torch.randn(n, k) * 0.05).to("cuda", torch.bfloat16))
