@@ -14,9 +14,10 @@
 //  * A warp covers 8 rows of a row tile: lane l reads bytes [16 l, 16 l + 16) of the 512-byte slice of
 //    each group block, i.e. row l / 4, chunk c = l % 4 (codes 16 c .. 16 c + 15 and 64 + 16 c .. + 15):
 //    every load instruction of the warp reads 512 contiguous bytes, streamed with an L2 evict-first policy
-//    through a U-deep register pipeline. A CTA (8 warps) covers 64 rows; split-K over groups forms a
-//    thread-block cluster along y whose partials are added through distributed shared memory in rank
-//    order (deterministic, no workspace).
+//    through a U-deep register pipeline. From M = 8 each lane serves two such row sets (a warp 16 rows),
+//    so every staged activation it reads feeds two rows. A CTA (8 warps) covers 64 or 128 rows; split-K
+//    over groups forms a thread-block cluster along y whose partials are added through distributed
+//    shared memory in rank order (deterministic, no workspace).
 //  * A byte b becomes two exact fp32 values: a byte permute gives 0x43bb0000; masking the high nibble
 //    away leaves 0x430L0000 = 128 + lo, and the high nibble moved down to bits 16-19 gives 0x430H0000 =
 //    128 + hi (the nibble must stay clear of bit 23, the exponent's lowest bit). Per group the lane
@@ -24,7 +25,10 @@
 //    sum of its 32 activations (staged once per CTA): the group term sum (q - zero) x, q - zero exact.
 //  * Activations are staged per CTA in shared memory as fp32, four floats of padding per 32 so that the
 //    four chunks a warp reads at once fall in different banks.
-//  * The K partition depends on (N, K) only, so a row's result does not depend on M.
+//  * The K partition depends on (N, K) only (counted in 64-row CTAs whatever the rows per lane), so a
+//    row's result does not depend on M.
+//  * A row tile past the last one the packed tensor holds (the last CTA of an odd tile count) is never
+//    read: those rows read the last tile instead, with scale 0, and are not stored.
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <stdlib.h>
@@ -69,41 +73,59 @@ __device__ __forceinline__ void store_y(const I4Args& a, int m, int row, float v
     static_cast<__nv_bfloat16*>(a.y)[m * a.ldy + row] = __float2bfloat16_rn(v);
 }
 
-template <int M, int U>
+// R weight rows per lane: rows warp * 8R + 8r + lane / 4 of the CTA's 64R (r < R), so each load
+// instruction of a warp still reads 512 contiguous bytes, and every staged activation a lane reads from
+// shared memory serves R rows (at R = 2 half the shared-memory reads per FMA). A row's arithmetic (its
+// FMA chains, the lane shuffles, the split order) does not depend on R.
+template <int M, int U, int R>
 __global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
   extern __shared__ float xs[];  // [M][padded_len(gb)] activations, then [M][gb][4][2] chunk sums
-  __shared__ float part[kRowsPerCta * M];
+  __shared__ float part[kRowsPerCta * R * M];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.x * kRowsPerCta + warp * 8 + (lane >> 2);
   const int c = lane & 3;
-  const bool rv = row < a.N;
   const int g0 = blockIdx.y * a.g_chunk;
   const int g1 = min(a.G, g0 + a.g_chunk);
   const int plen = padded_len(a.gb);
   float* xsum = xs + M * plen;
+  const int ntiles = (a.N + kTileRows - 1) / kTileRows;  // row tiles the packed tensor holds
 
-  // this lane's 16 bytes of group g: ((t G + g) 32 + r) 64 + 16 c  (padding rows of the format are zero)
-  const int t = row / kTileRows, rr = row % kTileRows;
-  const uint8_t* wl = a.w + (static_cast<long long>(t) * a.G * kTileRows + rr) * 64 + 16 * c;
+  // this lane's 16 bytes of group g of row r: ((t G + g) 32 + rr) 64 + 16 c (padding rows of a tile are
+  // zero). A row past the last tile reads the last tile instead (valid memory; its scale is 0 and its
+  // result is not stored).
+  int row[R];
+  bool rv[R];
+  const uint8_t* wl[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    row[r] = blockIdx.x * (kRowsPerCta * R) + warp * 8 * R + 8 * r + (lane >> 2);
+    rv[r] = row[r] < a.N;
+    const int t = min(row[r] / kTileRows, ntiles - 1), rr = row[r] % kTileRows;
+    wl[r] = a.w + (static_cast<long long>(t) * a.G * kTileRows + rr) * 64 + 16 * c;
+  }
   const long long gstride = static_cast<long long>(kTileRows) * 64;
   const uint64_t pol = l2_evict_first_policy();
 
-  float acc[M];
+  float acc[R][M];
 #pragma unroll
-  for (int m = 0; m < M; ++m) acc[m] = 0.0f;
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < M; ++m) acc[r][m] = 0.0f;
 
-  uint4 buf[U];
-  float sc[U], zc[U];
+  uint4 buf[U][R];
+  float sc[U][R], zc[U][R];
   auto fetch = [&](int g, int slot_u) {
     // (slot_u is a compile-time index after unrolling)
-    if (g < g1) {
-      buf[slot_u] = ldg_stream16(wl + g * gstride, pol);
-      sc[slot_u] = rv ? __bfloat162float(a.scale[static_cast<long long>(g) * a.N + row]) : 0.0f;
-      zc[slot_u] = rv ? __half2float(a.zero[static_cast<long long>(g) * a.N + row]) : 0.0f;
-    } else {
-      buf[slot_u] = make_uint4(0, 0, 0, 0);
-      sc[slot_u] = zc[slot_u] = 0.0f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      if (g < g1) {
+        buf[slot_u][r] = ldg_stream16(wl[r] + g * gstride, pol);
+        sc[slot_u][r] = rv[r] ? __bfloat162float(a.scale[static_cast<long long>(g) * a.N + row[r]]) : 0.0f;
+        zc[slot_u][r] = rv[r] ? __half2float(a.zero[static_cast<long long>(g) * a.N + row[r]]) : 0.0f;
+      } else {
+        buf[slot_u][r] = make_uint4(0, 0, 0, 0);
+        sc[slot_u][r] = zc[slot_u][r] = 0.0f;
+      }
     }
   };
 #pragma unroll
@@ -141,40 +163,51 @@ __global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
       const int g = gg + u;
       if (g < g1) {
         const int gl = g - bb;
-        const uint32_t words[4] = {buf[u].x, buf[u].y, buf[u].z, buf[u].w};
-        float plo[M], phi[M];
+        float plo[R][M], phi[R][M];
 #pragma unroll
-        for (int m = 0; m < M; ++m) plo[m] = phi[m] = 0.0f;
+        for (int r = 0; r < R; ++r)
+#pragma unroll
+          for (int m = 0; m < M; ++m) plo[r][m] = phi[r][m] = 0.0f;
 #pragma unroll
         for (int jq = 0; jq < 4; ++jq) {
-          float flo[4], fhi[4];
+          float flo[R][4], fhi[R][4];
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const uint32_t r = __byte_perm(words[jq], 0x43u, 0x4055u | (static_cast<uint32_t>(b) << 8));
-            flo[b] = __uint_as_float(r & 0xFF0FFFFFu);                            // 128 + low nibble
-            fhi[b] = __uint_as_float(((r >> 4) & 0x000F0000u) | 0x43000000u);  // 128 + high nibble
+          for (int r = 0; r < R; ++r) {
+            const uint32_t word = jq == 0 ? buf[u][r].x : (jq == 1 ? buf[u][r].y : (jq == 2 ? buf[u][r].z : buf[u][r].w));
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t v = __byte_perm(word, 0x43u, 0x4055u | (static_cast<uint32_t>(b) << 8));
+              flo[r][b] = __uint_as_float(v & 0xFF0FFFFFu);                            // 128 + low nibble
+              fhi[r][b] = __uint_as_float(((v >> 4) & 0x000F0000u) | 0x43000000u);  // 128 + high nibble
+            }
           }
 #pragma unroll
           for (int m = 0; m < M; ++m) {
             const float4 xl = *reinterpret_cast<const float4*>(xs + m * plen + xs_index(gl * kGroup + 16 * c + 4 * jq));
             const float4 xh =
                 *reinterpret_cast<const float4*>(xs + m * plen + xs_index(gl * kGroup + 64 + 16 * c + 4 * jq));
-            plo[m] = fmaf(flo[0], xl.x, plo[m]);
-            plo[m] = fmaf(flo[1], xl.y, plo[m]);
-            plo[m] = fmaf(flo[2], xl.z, plo[m]);
-            plo[m] = fmaf(flo[3], xl.w, plo[m]);
-            phi[m] = fmaf(fhi[0], xh.x, phi[m]);
-            phi[m] = fmaf(fhi[1], xh.y, phi[m]);
-            phi[m] = fmaf(fhi[2], xh.z, phi[m]);
-            phi[m] = fmaf(fhi[3], xh.w, phi[m]);
+#pragma unroll
+            for (int r = 0; r < R; ++r) {
+              plo[r][m] = fmaf(flo[r][0], xl.x, plo[r][m]);
+              plo[r][m] = fmaf(flo[r][1], xl.y, plo[r][m]);
+              plo[r][m] = fmaf(flo[r][2], xl.z, plo[r][m]);
+              plo[r][m] = fmaf(flo[r][3], xl.w, plo[r][m]);
+              phi[r][m] = fmaf(fhi[r][0], xh.x, phi[r][m]);
+              phi[r][m] = fmaf(fhi[r][1], xh.y, phi[r][m]);
+              phi[r][m] = fmaf(fhi[r][2], xh.z, phi[r][m]);
+              phi[r][m] = fmaf(fhi[r][3], xh.w, phi[r][m]);
+            }
           }
         }
-        const float cz = 128.0f + zc[u];
 #pragma unroll
-        for (int m = 0; m < M; ++m) {
-          const float* sm = xsum + ((m * a.gb + gl) * 4 + c) * 2;
-          const float grp = (plo[m] + phi[m]) - cz * (sm[0] + sm[1]);
-          acc[m] = fmaf(sc[u], grp, acc[m]);
+        for (int r = 0; r < R; ++r) {
+          const float cz = 128.0f + zc[u][r];
+#pragma unroll
+          for (int m = 0; m < M; ++m) {
+            const float* sm = xsum + ((m * a.gb + gl) * 4 + c) * 2;
+            const float grp = (plo[r][m] + phi[r][m]) - cz * (sm[0] + sm[1]);
+            acc[r][m] = fmaf(sc[u][r], grp, acc[r][m]);
+          }
         }
       }
     }
@@ -182,31 +215,38 @@ __global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
 
   // the row's 4 chunk lanes -> every one of them holds the row sum
 #pragma unroll
-  for (int m = 0; m < M; ++m) {
-    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], 1);
-    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], 2);
-  }
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], 1);
+      acc[r][m] += __shfl_xor_sync(0xffffffffu, acc[r][m], 2);
+    }
 
   if (gridDim.y == 1) {
 #pragma unroll
-    for (int m = 0; m < M; ++m)
-      if ((m & 3) == c && rv) store_y(a, m, row, acc[m]);
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int m = 0; m < M; ++m)
+        if ((m & 3) == c && rv[r]) store_y(a, m, row[r], acc[r][m]);
     return;
   }
-  const int lr = warp * 8 + (lane >> 2);
 #pragma unroll
-  for (int m = 0; m < M; ++m)
-    if ((m & 3) == c) part[lr * M + m] = acc[m];
+  for (int r = 0; r < R; ++r) {
+    const int lr = warp * 8 * R + 8 * r + (lane >> 2);  // row[r] - the CTA's first row
+#pragma unroll
+    for (int m = 0; m < M; ++m)
+      if ((m & 3) == c) part[lr * M + m] = acc[r][m];
+  }
   cg::cluster_group cluster = cg::this_cluster();
   cluster.sync();
   const int S = gridDim.y;
   const int rank = static_cast<int>(cluster.block_rank());
-  for (int e = rank + S * threadIdx.x; e < kRowsPerCta * M; e += S * kThreads) {
-    const int r = blockIdx.x * kRowsPerCta + e / M, m = e % M;
-    if (r >= a.N) continue;
+  for (int e = rank + S * threadIdx.x; e < kRowsPerCta * R * M; e += S * kThreads) {
+    const int rw = blockIdx.x * (kRowsPerCta * R) + e / M, m = e % M;
+    if (rw >= a.N) continue;
     float s = 0.0f;
     for (int q = 0; q < S; ++q) s += cluster.map_shared_rank(part, q)[e];
-    store_y(a, m, r, s);
+    store_y(a, m, rw, s);
   }
   cluster.sync();  // keep this CTA's partials alive until every peer has read them
 }
@@ -216,11 +256,20 @@ constexpr int pipeline_depth() {
   return M <= 4 ? 4 : (M <= 8 ? 3 : 2);
 }
 
+// Rows per lane: two from M = 8, where the shared-memory reads of the staged activations bound the kernel
+// (M = 16, cold L2: 2048 x 2048 29.6 -> 23.5 us, 8192 x 2048 65.9 -> 49.5, 2048 x 8192 82.8 -> 63.0); one
+// below, where the CTA count matters more (M = 4 with two: 2048 x 2048 7.0 -> 8.1 us).
+template <int M>
+constexpr int rows_per_lane() {
+  return M >= 8 ? 2 : 1;
+}
+
 template <int M>
 int launch_i4(I4Args a, cudaStream_t st) {
   constexpr int U = pipeline_depth<M>();
+  constexpr int R = rows_per_lane<M>();
+  // split from (N, K) only, counted as for one row per lane: about two 64-row CTAs per SM in total
   const int row_ctas = (a.N + kRowsPerCta - 1) / kRowsPerCta;
-  // split from (N, K) only: about two CTAs per SM in total
   const int target = 2 * tc_sm_count();
   int S = (target + row_ctas - 1) / row_ctas;
   S = S < 1 ? 1 : (S > kMaxSplit ? kMaxSplit : S);
@@ -237,7 +286,7 @@ int launch_i4(I4Args a, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(M) * (padded_len(gb) + gb * 8) * sizeof(float);
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(row_ctas, S, 1);
+  cfg.gridDim = dim3((a.N + kRowsPerCta * R - 1) / (kRowsPerCta * R), S, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -251,7 +300,7 @@ int launch_i4(I4Args a, cudaStream_t st) {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
   }
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_i4_kernel<M, U>, a);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_i4_kernel<M, U, R>, a);
   if (e != cudaSuccess)
     return fail(BP_ERR_CUDA, "int4 skinny launch (M=%d N=%d K=%d split=%d): %s", M, a.N, a.K, S, cudaGetErrorString(e));
   return BP_OK;
