@@ -15,7 +15,8 @@
 //    each group block, i.e. row l / 4, chunk c = l % 4 (codes 16 c .. 16 c + 15 and 64 + 16 c .. + 15):
 //    every load instruction of the warp reads 512 contiguous bytes, streamed with an L2 evict-first policy
 //    through a U-deep register pipeline. From M = 8 each lane serves two such row sets (a warp 16 rows),
-//    so every staged activation it reads feeds two rows. A CTA (8 warps) covers 64 or 128 rows; split-K
+//    so every staged activation it reads feeds two rows. A CTA covers 64 rows (8 warps, or 4 warps of
+//    two rows per lane: half the threads, so two CTAs of ~230 registers a thread fit an SM); split-K
 //    over groups forms a thread-block cluster along y whose partials are added through distributed
 //    shared memory in rank order (deterministic, no workspace).
 //  * A byte b becomes two exact fp32 values: a byte permute gives 0x43bb0000; masking the high nibble
@@ -25,8 +26,7 @@
 //    sum of its 32 activations (staged once per CTA): the group term sum (q - zero) x, q - zero exact.
 //  * Activations are staged per CTA in shared memory as fp32, four floats of padding per 32 so that the
 //    four chunks a warp reads at once fall in different banks.
-//  * The K partition depends on (N, K) only (counted in 64-row CTAs whatever the rows per lane), so a
-//    row's result does not depend on M.
+//  * The K partition depends on (N, K) only, so a row's result does not depend on M.
 //  * A row tile past the last one the packed tensor holds (the last CTA of an odd tile count) is never
 //    read: those rows read the last tile instead, with scale 0, and are not stored.
 #include <cooperative_groups.h>
@@ -73,14 +73,15 @@ __device__ __forceinline__ void store_y(const I4Args& a, int m, int row, float v
     static_cast<__nv_bfloat16*>(a.y)[m * a.ldy + row] = __float2bfloat16_rn(v);
 }
 
-// R weight rows per lane: rows warp * 8R + 8r + lane / 4 of the CTA's 64R (r < R), so each load
-// instruction of a warp still reads 512 contiguous bytes, and every staged activation a lane reads from
-// shared memory serves R rows (at R = 2 half the shared-memory reads per FMA). A row's arithmetic (its
-// FMA chains, the lane shuffles, the split order) does not depend on R.
+// R weight rows per lane: rows warp * 8R + 8r + lane / 4 of the CTA's 64 (r < R; 8 / R warps), so each
+// load instruction of a warp still reads 512 contiguous bytes, and every staged activation a lane reads
+// from shared memory serves R rows (at R = 2 half the shared-memory reads per FMA). The grid and a row's
+// arithmetic (its FMA chains, the lane shuffles, the split order) do not depend on R.
 template <int M, int U, int R>
-__global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
+__global__ void __launch_bounds__(kThreads / R) skinny_i4_kernel(const I4Args a) {
+  constexpr int kThr = kThreads / R;
   extern __shared__ float xs[];  // [M][padded_len(gb)] activations, then [M][gb][4][2] chunk sums
-  __shared__ float part[kRowsPerCta * R * M];
+  __shared__ float part[kRowsPerCta * M];
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = lane & 3;
@@ -98,7 +99,7 @@ __global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
   const uint8_t* wl[R];
 #pragma unroll
   for (int r = 0; r < R; ++r) {
-    row[r] = blockIdx.x * (kRowsPerCta * R) + warp * 8 * R + 8 * r + (lane >> 2);
+    row[r] = blockIdx.x * kRowsPerCta + warp * 8 * R + 8 * r + (lane >> 2);
     rv[r] = row[r] < a.N;
     const int t = min(row[r] / kTileRows, ntiles - 1), rr = row[r] % kTileRows;
     wl[r] = a.w + (static_cast<long long>(t) * a.G * kTileRows + rr) * 64 + 16 * c;
@@ -139,7 +140,7 @@ __global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
       const int gn = min(a.gb, g1 - gg);
       __syncthreads();  // the previous batch is consumed
       const int vecs = M * gn * (kGroup / 8);
-      for (int i = threadIdx.x; i < vecs; i += kThreads) {
+      for (int i = threadIdx.x; i < vecs; i += kThr) {
         const int m = i / (gn * (kGroup / 8)), kv = (i - m * gn * (kGroup / 8)) * 8;
         const uint4 v = ldg16(a.x + m * a.ldx + static_cast<long long>(gg) * kGroup + kv);
         float* d = xs + m * plen + xs_index(kv);
@@ -147,7 +148,7 @@ __global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
         *reinterpret_cast<float4*>(d + 4) = make_float4(bf16lo(v.z), bf16hi(v.z), bf16lo(v.w), bf16hi(v.w));
       }
       __syncthreads();
-      for (int i = threadIdx.x; i < M * gn * 8; i += kThreads) {
+      for (int i = threadIdx.x; i < M * gn * 8; i += kThr) {
         const int m = i / (gn * 8), rest = i - m * gn * 8, gl = rest >> 3, cc = (rest >> 1) & 3, h = rest & 1;
         const float* p = xs + m * plen + xs_index(gl * kGroup + 64 * h + 16 * cc);
         float s = 0.0f;
@@ -241,8 +242,8 @@ __global__ void __launch_bounds__(kThreads) skinny_i4_kernel(const I4Args a) {
   cluster.sync();
   const int S = gridDim.y;
   const int rank = static_cast<int>(cluster.block_rank());
-  for (int e = rank + S * threadIdx.x; e < kRowsPerCta * R * M; e += S * kThreads) {
-    const int rw = blockIdx.x * (kRowsPerCta * R) + e / M, m = e % M;
+  for (int e = rank + S * threadIdx.x; e < kRowsPerCta * M; e += S * kThr) {
+    const int rw = blockIdx.x * kRowsPerCta + e / M, m = e % M;
     if (rw >= a.N) continue;
     float s = 0.0f;
     for (int q = 0; q < S; ++q) s += cluster.map_shared_rank(part, q)[e];
@@ -257,8 +258,9 @@ constexpr int pipeline_depth() {
 }
 
 // Rows per lane: two from M = 8, where the shared-memory reads of the staged activations bound the kernel
-// (M = 16, cold L2: 2048 x 2048 29.6 -> 23.5 us, 8192 x 2048 65.9 -> 49.5, 2048 x 8192 82.8 -> 63.0); one
-// below, where the CTA count matters more (M = 4 with two: 2048 x 2048 7.0 -> 8.1 us).
+// (M = 16, cold L2, 64-row CTAs of 4 warps: 2048 x 2048 29.6 -> 13.2 us, 8192 x 2048 65.9 -> 50.9,
+// 2048 x 8192 82.8 -> 35.1; 128-row CTAs of 8 warps gave 23.5 / 49.5 / 63.0, their 8-CTA clusters of
+// full-SM CTAs running in two waves); one below.
 template <int M>
 constexpr int rows_per_lane() {
   return M >= 8 ? 2 : 1;
@@ -268,7 +270,7 @@ template <int M>
 int launch_i4(I4Args a, cudaStream_t st) {
   constexpr int U = pipeline_depth<M>();
   constexpr int R = rows_per_lane<M>();
-  // split from (N, K) only, counted as for one row per lane: about two 64-row CTAs per SM in total
+  // split from (N, K) only: about two 64-row CTAs per SM in total
   const int row_ctas = (a.N + kRowsPerCta - 1) / kRowsPerCta;
   const int target = 2 * tc_sm_count();
   int S = (target + row_ctas - 1) / row_ctas;
@@ -286,8 +288,8 @@ int launch_i4(I4Args a, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(M) * (padded_len(gb) + gb * 8) * sizeof(float);
 
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((a.N + kRowsPerCta * R - 1) / (kRowsPerCta * R), S, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.gridDim = dim3(row_ctas, S, 1);
+  cfg.blockDim = dim3(kThreads / R, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
