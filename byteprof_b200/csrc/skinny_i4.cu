@@ -14,7 +14,7 @@
 //  * A warp covers 8 rows of a row tile: lane l reads bytes [16 l, 16 l + 16) of the 512-byte slice of
 //    each group block, i.e. row l / 4, chunk c = l % 4 (codes 16 c .. 16 c + 15 and 64 + 16 c .. + 15):
 //    every load instruction of the warp reads 512 contiguous bytes, streamed with an L2 evict-first policy
-//    through a U-deep register pipeline. From M = 8 each lane serves two such row sets (a warp 16 rows),
+//    through a U-deep register pipeline. From M = 2 each lane serves two such row sets (a warp 16 rows),
 //    so every staged activation it reads feeds two rows. A CTA covers 64 rows (8 warps, or 4 warps of
 //    two rows per lane: half the threads, so two CTAs of ~230 registers a thread fit an SM); split-K
 //    over groups forms a thread-block cluster along y whose partials are added through distributed
@@ -257,13 +257,14 @@ constexpr int pipeline_depth() {
   return M <= 4 ? 4 : (M <= 8 ? 3 : 2);
 }
 
-// Rows per lane: two from M = 8, where the shared-memory reads of the staged activations bound the kernel
-// (M = 16, cold L2, 64-row CTAs of 4 warps: 2048 x 2048 29.6 -> 13.2 us, 8192 x 2048 65.9 -> 50.9,
-// 2048 x 8192 82.8 -> 35.1; 128-row CTAs of 8 warps gave 23.5 / 49.5 / 63.0, their 8-CTA clusters of
-// full-SM CTAs running in two waves); one below.
+// Rows per lane: two from M = 2, where the shared-memory reads of the staged activations bound the kernel
+// (cold L2, 64-row CTAs of 4 warps; M = 16: 2048 x 2048 29.6 -> 13.2 us, 8192 x 2048 65.9 -> 50.9,
+// 2048 x 8192 82.8 -> 35.1; M = 4: 6.9 -> 6.4, 16.3 -> 14.7, 16.0 -> 15.1; 128-row CTAs of 8 warps gave
+// 23.5 / 49.5 / 63.0 at M = 16, their 8-CTA clusters of full-SM CTAs running in two waves); one at
+// M = 1, which is bound by HBM.
 template <int M>
 constexpr int rows_per_lane() {
-  return M >= 8 ? 2 : 1;
+  return M >= 2 ? 2 : 1;
 }
 
 template <int M>
