@@ -583,7 +583,9 @@ def scan_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
 
 def run_scan_case(args, t: int) -> int:
     """`--case scan,T`: the scan alone over its cold rotation (for ncu captures): W eager warm-up scans, then
-    K timed scans on the current stream, CUDA events. Prints us per scan and GB/s of minimum traffic."""
+    K timed scans on the current stream, CUDA events (eager: at small T the host's launch cost, not the
+    device time; `--graph` times a graph of the rotation instead). Prints us per scan and GB/s of minimum
+    traffic."""
     from byteprof_b200.optim.draft_core import mlstm_scan
 
     dev = torch.device("cuda", 0)
@@ -593,6 +595,14 @@ def run_scan_case(args, t: int) -> int:
         p = probs[j % len(probs)]
         mlstm_scan(p[0], *p[1:7], p[7], 1e-6)
     torch.cuda.synchronize()
+    if args.graph:  # one graph of the rotation, replayed: device time per scan without host gaps
+        gr = capture(lambda: [mlstm_scan(p[0], *p[1:7], p[7], 1e-6) for p in probs])
+        reps = max(1, args.steps // len(probs))
+        time_graph_replays(gr, 2)
+        us = time_graph_replays(gr, reps) * 1e3 / (reps * len(probs))
+        print(json.dumps({"case": f"scan|T{t}", "us": round(us, 3), "gbs": round(scan_bytes(t) / (us * 1e-6) / 1e9, 1),
+                          "bytes": scan_bytes(t), "graph": True}), flush=True)
+        return 0
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for j in range(args.steps):
@@ -893,7 +903,7 @@ def main(argv=None) -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--quick", action="store_true", help="skip the per-cell, int8, scan and CPU passes")
     ap.add_argument("--case", default=None, help="N,K,M[,bf16|int8|int4] or scan,T: time one sweep cell or one scan alone (ncu captures)")
-    ap.add_argument("--graph", action="store_true", help="with --case: time a CUDA graph of the weight ring")
+    ap.add_argument("--graph", action="store_true", help="with --case: time a CUDA graph of the weight ring (or of the scan rotation)")
     ap.add_argument("--decode", type=int, default=0, metavar="N",
                     help="only N bytes of the Bolmo-shaped decode, each opening a patch (short runs for ncu)")
     ap.add_argument("--decode-pos", type=int, default=0, metavar="P",
