@@ -48,6 +48,14 @@ METRIC = "skinny-GEMM HBM GB/s (% of peak, cold L2) at M=1-16"
 PEAK_FALLBACK_GBS = 6650.0
 
 
+def workload_config(world: int) -> dict:
+    """The workload both arms run (identical in the reference arm's line and ours)."""
+    return {"workload": "BASELINE configs[1]: bf16 skinny sweep M in {1,2,4,8,16} x OLMo-2-1B shapes",
+            "shapes": [f"{n}x{k}" for n, k in SHAPES], "ms": list(MS), "parallelism": f"replicas x{world}",
+            "l2": "cold: per-shape weight ring >= 256 MiB (> 2x L2)", "weights": "N(0, 0.02) bf16, x ~ N(0, 1)",
+            "step": "one step = the 20 calls of the sweep"}
+
+
 def alg_bytes(m: int, n: int, k: int, kind: str = "bf16") -> int:
     """Bytes one call must move: the weights once (int8: + the [N] scale; int4: packed codes + the
     [K/128, N] bf16 scale and fp16 zero), the activations and the output."""
@@ -89,6 +97,18 @@ def max_over_ranks(x: float, device: torch.device | None = None) -> float:
     t = torch.tensor([x], dtype=torch.float64, device=device or "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def gather_over_ranks(x: float, device: torch.device | None = None) -> list[float]:
+    """x from every rank, in rank order ([x] when not distributed)."""
+    import torch.distributed as dist
+
+    if not (dist.is_available() and dist.is_initialized()):
+        return [x]
+    t = torch.tensor([x], dtype=torch.float64, device=device or "cpu")
+    out = [torch.zeros_like(t) for _ in range(dist.get_world_size())]
+    dist.all_gather(out, t)
+    return [float(v.item()) for v in out]
 
 
 # ---- clocks -----------------------------------------------------------------------------------------
@@ -207,8 +227,19 @@ def time_graph_replays(g: torch.cuda.CUDAGraph, reps: int) -> float:
     return a.elapsed_time(b)
 
 
+def _graph_us_per_call(fn, calls: int, reps: int) -> float:
+    g = capture(fn)
+    time_graph_replays(g, 2)
+    us = time_graph_replays(g, reps) * 1e3 / (reps * calls)
+    del g
+    return us
+
+
 def cell_times(sweep: Sweep, peak: float, reps: int = 5) -> dict:
-    """Per (shape, M): a graph of one call per ring member, replayed; us per call and GB/s."""
+    """Per (shape, M): a graph of one call per ring member, replayed; us per call and GB/s. Beside it the
+    library reference timed the same way on the same ring: cuBLAS (torch.mm into the same output), as the
+    reference's own harness times bf16 cuBLAS beside its kernel (byteprof tools/skinny_bench.py:93-94);
+    `vs_cublas` = cuBLAS time / our time."""
     from byteprof_b200.optim.skinny import skinny_mm
 
     cells = {}
@@ -216,13 +247,11 @@ def cell_times(sweep: Sweep, peak: float, reps: int = 5) -> dict:
         ring = sweep.rings[si]
         for m in MS:
             x, y = sweep.x[si][:m], sweep.y[si][:m]
-            g = capture(lambda: [skinny_mm(x, w, out=y) for w in ring])
-            time_graph_replays(g, 2)
-            ms = time_graph_replays(g, reps)
-            us = ms * 1e3 / (reps * len(ring))
+            us = _graph_us_per_call(lambda: [skinny_mm(x, w, out=y) for w in ring], len(ring), reps)
+            lib_us = _graph_us_per_call(lambda: [torch.mm(x, w.t(), out=y) for w in ring], len(ring), reps)
             gbs = alg_bytes(m, n, k) / (us * 1e-6) / 1e9
-            cells[f"{n}x{k}|M{m}"] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
-            del g
+            cells[f"{n}x{k}|M{m}"] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                                      "cublas_us": round(lib_us, 3), "vs_cublas": round(lib_us / us, 3)}
     return cells
 
 
@@ -238,15 +267,23 @@ def int8_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
                 for _ in range(ring_n)]
         x = torch.randn(max(INT8_MS), k, generator=g0, device=device).to(torch.bfloat16)
         y = torch.empty(max(INT8_MS), n, device=device, dtype=torch.bfloat16)
+        wdq = torch.empty(n, k, device=device, dtype=torch.bfloat16)
+
+        def library(xm, ym):  # Int8Linear's M > 1 path: dequantize to the activation dtype, then cuBLAS
+            for q, s in ring:
+                torch.mul(q, s[:, None], out=wdq)
+                torch.mm(xm, wdq.t(), out=ym)
+
         for m in INT8_MS:
-            g = capture(lambda: [skinny_mm(x[:m], q, s, out=y[:m]) for q, s in ring])
-            time_graph_replays(g, 2)
-            us = time_graph_replays(g, reps) * 1e3 / (reps * ring_n)
+            us = _graph_us_per_call(lambda: [skinny_mm(x[:m], q, s, out=y[:m]) for q, s in ring], ring_n, reps)
+            lib_us = _graph_us_per_call(lambda: library(x[:m], y[:m]), ring_n, reps)
             gbs = alg_bytes(m, n, k, "int8") / (us * 1e-6) / 1e9
-            out[f"{n}x{k}|M{m}"] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
-            del g
-        del ring
+            out[f"{n}x{k}|M{m}"] = {"us": round(us, 3), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                                    "library_us": round(lib_us, 3), "vs_library": round(lib_us / us, 3)}
+        del ring, wdq
     torch.cuda.empty_cache()
+    out["library"] = ("torch dequantize (q * scale to bf16) + cuBLAS torch.mm: byteprof Int8Linear's path for more "
+                      "than one row (byteprof/quant/integrate.py:38-46)")
     return out
 
 
@@ -563,20 +600,47 @@ def scan_bytes(t: int, nh: int = 4, d: int = 512) -> int:
     return 2 * (nh * d * d * 4 + nh * d * 4 + nh * 4) + t * (3 * nh * d * 2 + 2 * nh * 4 + nh * d * 2)
 
 
+def torch_scan(st_in, q, k, v, i, f, h, st_out, eps: float) -> None:
+    """The comparison arm of the scan: the same recurrence written in stock torch ops, one position after
+    another (the eager step of byteprof's reference formulation in fp32, as the minimal loop's torch path
+    would run it without the fused kernel)."""
+    import torch.nn.functional as F
+
+    c, n, m = (t.clone() for t in st_in)
+    c, n, m = c[0], n[0], m.view(-1)
+    dq = q.shape[-1]
+    for t in range(q.shape[0]):
+        ig, fg = i[t, :, 0], f[t, :, 0]
+        flog = F.logsigmoid(fg)
+        m_new = torch.maximum(flog + m, ig)
+        fa, ia = torch.exp(flog + m - m_new), torch.exp(ig - m_new)
+        qf, kf, vf = q[t].float() * dq ** -0.5, k[t].float(), v[t].float()
+        c = fa[:, None, None] * c + ia[:, None, None] * (kf[:, :, None] * vf[:, None, :])
+        n = fa[:, None] * n + ia[:, None] * kf
+        den = torch.maximum((qf * n).sum(-1).abs(), torch.exp(-m_new)) + eps
+        h[t].copy_(torch.einsum("hd,hde->he", qf, c) / den[:, None])
+        m = m_new
+    st_out[0][0].copy_(c)
+    st_out[1][0].copy_(n)
+    st_out[2].view(-1).copy_(m)
+
+
 def scan_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
     """NH=4, dk=dv=512, T positions from a zero state, h and the final state. One graph
-    runs a rotation of independent problems larger than L2 (cold state); time per scan = replay / problems."""
+    runs a rotation of independent problems larger than L2 (cold state); time per scan = replay / problems.
+    `torch_us`: the same rotation through `torch_scan` (stock torch ops), timed the same way."""
     from byteprof_b200.optim.draft_core import mlstm_scan
 
     out = {}
     for t in SCAN_TS:
         probs = scan_problems(device, t)
-        g = capture(lambda: [mlstm_scan(p[0], *p[1:7], p[7], 1e-6) for p in probs])
-        time_graph_replays(g, 3)
-        us = time_graph_replays(g, reps) * 1e3 / (reps * len(probs))
+        us = _graph_us_per_call(lambda: [mlstm_scan(p[0], *p[1:7], p[7], 1e-6) for p in probs], len(probs), reps)
+        sub = probs[:max(2, min(len(probs), 512 // t))]  # bound the torch graph's node count at long T
+        lib_us = _graph_us_per_call(lambda: [torch_scan(p[0], *p[1:7], p[7], 1e-6) for p in sub], len(sub), 2)
         out[f"T{t}"] = {"us": round(us, 2), "us_per_step": round(us / t, 4),
-                        "gbs": round(scan_bytes(t) / (us * 1e-6) / 1e9, 1), "problems_in_rotation": len(probs)}
-        del g, probs
+                        "gbs": round(scan_bytes(t) / (us * 1e-6) / 1e9, 1), "problems_in_rotation": len(probs),
+                        "torch_us": round(lib_us, 2), "vs_torch": round(lib_us / us, 2)}
+        del probs, sub
         torch.cuda.empty_cache()
     return out
 
@@ -616,12 +680,12 @@ def run_scan_case(args, t: int) -> int:
     return 0
 
 
-def e2e_sweep(sweep: Sweep, steps: int) -> tuple[float, int, int]:
+def e2e_sweep(sweep: Sweep, steps: int, min_seconds: float) -> tuple[float, int, int, int]:
     """The sweep through the public API with pinned host activations in and outputs out every step. Each
     call's output has its own device buffer, and its copy to the host runs on a second stream as soon as
     the call has finished, while the next calls compute (the overlap a caller gets from two streams); a
-    step ends when every output is on the host. Returns (device ms for `steps` steps, h2d bytes / step,
-    d2h bytes / step)."""
+    step ends when every output is on the host. Runs at least `steps` steps and at least `min_seconds`.
+    Returns (device ms of the timed steps, steps, h2d bytes / step, d2h bytes / step)."""
     from byteprof_b200.optim.skinny import skinny_mm
 
     xh = [x.cpu().pin_memory() for x in sweep.x]
@@ -651,58 +715,68 @@ def e2e_sweep(sweep: Sweep, steps: int) -> tuple[float, int, int]:
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     a.record()
-    for s in range(steps):
-        one(s)
+    t0, done_steps = time.perf_counter(), 0
+    while done_steps < steps or time.perf_counter() - t0 < min_seconds:
+        one(done_steps)
+        done_steps += 1
     b.record()
     torch.cuda.synchronize()
-    return a.elapsed_time(b), h2d, d2h
+    return a.elapsed_time(b), done_steps, h2d, d2h
 
 
 # ---- CPU path (reference arm and cpu_baseline) ------------------------------------------------------
 
-def cpu_sweep(max_calls: int, min_seconds: float, max_seconds: float, threads: int) -> dict:
-    """The reference's CPU path (F.linear on the host, bf16) over the sweep cells, one cell per call in
-    sweep order (call c runs cell c mod 20). Stops after max_calls calls, or earlier once max_seconds
-    have passed; runs at least until min_seconds have passed or max_calls is reached."""
-    from oracle.cpu_path import linear_cpu
+class CpuSweep:
+    """The reference's CPU path (F.linear on the host in bf16, byteprof SkinnyLinear's branch for CPU tensors)
+    over the same sweep: one step = the 20 calls, one per (shape, M), in sweep order. The weights are made
+    once; every call reads its whole weight matrix (the LM head's 411 MB exceeds the host caches)."""
 
-    torch.set_num_threads(threads)
-    g = torch.Generator().manual_seed(0)
-    ws = [(torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16) for n, k in SHAPES]
-    xs = [torch.randn(max(MS), k, generator=g).to(torch.bfloat16) for n, k in SHAPES]
-    cells = [(si, m) for si in range(len(SHAPES)) for m in MS]
-    for si in range(len(SHAPES)):  # first-touch of the weights and the BLAS setup
-        linear_cpu(xs[si][:1], ws[si])
-    nbytes, calls, t0 = 0, 0, time.perf_counter()
-    while calls < max_calls or time.perf_counter() - t0 < min_seconds:
-        si, m = cells[calls % len(cells)]
-        n, k = SHAPES[si]
-        linear_cpu(xs[si][:m], ws[si])
-        nbytes += alg_bytes(m, n, k)
-        calls += 1
-        if time.perf_counter() - t0 > max_seconds:
-            break
-    dt = time.perf_counter() - t0
-    return {"value": round(nbytes / dt / 1e9, 3), "unit": "GB/s", "cores": threads, "calls": calls,
-            "seconds": round(dt, 2), "seconds_raw": dt}
+    def __init__(self, threads: int):
+        torch.set_num_threads(threads)
+        self.threads = threads
+        g = torch.Generator().manual_seed(0)
+        self.ws = [(torch.randn(n, k, generator=g) * 0.02).to(torch.bfloat16) for n, k in SHAPES]
+        self.xs = [torch.randn(max(MS), k, generator=g).to(torch.bfloat16) for n, k in SHAPES]
+        self.bytes_per_step = sum(alg_bytes(m, n, k) for n, k in SHAPES for m in MS)
+
+    def step(self) -> None:
+        from oracle.cpu_path import linear_cpu
+
+        for si in range(len(SHAPES)):
+            for m in MS:
+                linear_cpu(self.xs[si][:m], self.ws[si])
+
+    def run(self, max_steps: int, min_seconds: float, max_seconds: float) -> dict:
+        """Whole sweeps until max_steps (and at least min_seconds), stopping early after max_seconds."""
+        steps, t0 = 0, time.perf_counter()
+        while steps < max_steps or time.perf_counter() - t0 < min_seconds:
+            self.step()
+            steps += 1
+            if time.perf_counter() - t0 > max_seconds:
+                break
+        dt = time.perf_counter() - t0
+        return {"value": round(self.bytes_per_step * steps / dt / 1e9, 3), "unit": "GB/s", "cores": self.threads,
+                "steps": steps, "seconds": round(dt, 2), "seconds_raw": dt}
 
 
 def run_reference(args) -> int:
-    """Reference arm: rank 0 times the reference's CPU path; one step = one sweep cell (bounded sample)."""
+    """Reference arm: rank 0 times the reference's CPU path for the same sweep, one step = one whole sweep
+    (bounded: at most 150 s of timed steps). The other ranks exit without work."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    cpu_sweep(max_calls=args.warmup, min_seconds=0.0, max_seconds=60.0, threads=threads)
-    res = cpu_sweep(max_calls=args.steps, min_seconds=0.0, max_seconds=150.0, threads=threads)
-    sample = (f"{res['calls']} of {args.steps} steps (one sweep cell = one F.linear call per step, cells in sweep "
-              f"order) in {res['seconds_raw']:.4f} s, torch bf16 on the host = byteprof SkinnyLinear's CPU branch")
+    cpu = CpuSweep(threads)
+    cpu.run(max_steps=args.warmup, min_seconds=0.0, max_seconds=60.0)
+    res = cpu.run(max_steps=args.steps, min_seconds=0.0, max_seconds=150.0)
+    sample = (f"{res['steps']} of {args.steps} steps, each the whole 20-call sweep (F.linear per cell, cells in "
+              f"sweep order), {res['seconds_raw']:.3f} s, torch bf16 on the host = byteprof SkinnyLinear's CPU "
+              f"branch; rank 0 only")
     line = {"metric": METRIC, "value": res["value"], "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus,
-            "steps": res["calls"], "warmup": args.warmup,
-            "ms_per_step": round(res["seconds_raw"] * 1e3 / max(1, res["calls"]), 4),
+            "steps": res["steps"], "warmup": args.warmup,
+            "ms_per_step": round(res["seconds_raw"] * 1e3 / max(1, res["steps"]), 4),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE configs[1]: bf16 skinny sweep M in {1,2,4,8,16} x OLMo-2-1B shapes",
-                       "shapes": [f"{n}x{k}" for n, k in SHAPES], "ms": list(MS)},
+            "config": workload_config(world), "timing": "wall clock on the host, all host threads",
             "cpu_baseline": {"kind": "port", "cores": threads, "value": res["value"], "unit": "GB/s", "sample": sample},
             "e2e": {"value": res["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -753,10 +827,10 @@ def run_ours(args) -> int:
     del graphs
     value = world * sweep.bytes_per_step * args.steps / (ms_total * 1e-3) / 1e9
 
-    e2e_steps = max(3, args.steps // 20)
-    e2e_ms, h2d, d2h = e2e_sweep(sweep, e2e_steps)
-    e2e_ms = max_over_ranks(e2e_ms, device)
-    e2e_value = world * sweep.bytes_per_step * e2e_steps / (e2e_ms * 1e-3) / 1e9
+    e2e_ms, e2e_steps, h2d, d2h = e2e_sweep(sweep, max(50, args.steps), min_seconds=1.0)
+    # every rank ran its own number of steps: the slowest rank's rate sets the whole job's
+    e2e_per_step = max_over_ranks(e2e_ms / e2e_steps, device)
+    e2e_value = world * sweep.bytes_per_step / (e2e_per_step * 1e-3) / 1e9
 
     extras = {}
     if not args.quick:
@@ -765,6 +839,10 @@ def run_ours(args) -> int:
         extras["scan"] = scan_cells(device, peak)
         extras["verify"] = verify_cells(device, peak)
         extras["decode"] = decode_cells(device, peak, seed=rank)
+        # one independent stream per GPU: bytes/s of every rank and their sum (each rank decodes its own model)
+        per_rank = gather_over_ranks(extras["decode"]["bytes_per_s"], device)
+        extras["decode"]["per_rank_bytes_per_s"] = per_rank
+        extras["decode"]["aggregate_bytes_per_s"] = round(sum(per_rank), 1)
 
     if rank == 0:
         # dominant kernel = the sweep cell with the largest device time per step
@@ -775,23 +853,24 @@ def run_ours(args) -> int:
             achieved = alg_bytes(m_, n_, k_) / (cells[dom_key]["us"] * 1e-6) / 1e9
         else:
             dom_key, achieved = "sweep", value / world
-        traffic = _traffic_from_profiles(dom_key)
+        traffic, traffic_src = _traffic_from_profiles(dom_key)
+        m1 = [c["frac"] for key, c in cells.items() if key.endswith("|M1")]
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_total / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "BASELINE configs[1]: bf16 skinny sweep M in {1,2,4,8,16} x OLMo-2-1B shapes",
-                       "shapes": [f"{n}x{k}" for n, k in SHAPES], "ms": list(MS),
-                       "parallelism": f"replicas x{world}", "l2": "cold: per-shape weight ring >= 256 MiB (> 2x L2)",
-                       "weights": "N(0, 0.02) bf16, x ~ N(0, 1)", "timing": "CUDA graph per step, CUDA events"},
+            "config": workload_config(world), "timing": "CUDA graph per step, CUDA events on the replay stream",
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": f"skinny_mm cell {dom_key} (largest time share)"},
+                         "traffic_source": traffic_src, "kernel": f"skinny_mm cell {dom_key} (largest time share)",
+                         "achieved_from": "algorithmic bytes of the cell / its CUDA-event time per call, this run"},
             "frac_of_peak": round(value / world / peak, 4),
             "mean_cell_frac": round(statistics.mean(c["frac"] for c in cells.values()), 4) if cells else None,
+            "min_m1_cell_frac": round(min(m1), 4) if m1 else None,
             "cells": cells,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps, "api": "byteprof_b200.optim.skinny.skinny_mm, eager, pinned host x in / y out (outputs copied on a second stream)"},
+                    "steps": e2e_steps, "ms_per_step": round(e2e_per_step, 4),
+                    "api": "byteprof_b200.optim.skinny.skinny_mm, eager, pinned host x in / y out (outputs copied on a second stream)"},
             "gpu_launches": sweep.calls_per_step * args.steps,
             "clocks": clk.summary(),
             **extras,
@@ -806,9 +885,11 @@ def run_ours(args) -> int:
     return 0
 
 
-def _traffic_from_profiles(cell: str):
-    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of `cell` from a committed
-    ncu summary under profiles/ (lines `cell: <N>x<K>|M<m>` and `dram_bytes_per_launch: <bytes>`)."""
+def _traffic_from_profiles(cell: str) -> tuple[int | None, str | None]:
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) of `cell` as an earlier ncu capture
+    measured it, from the committed summary under profiles/ that names the cell (lines `cell: <N>x<K>|M<m>`
+    and `dram_bytes_per_launch: <bytes>`), with that file's path; (None, None) when no summary covers it.
+    The figure is a stored capture, not measured in this run (a profiler run is never a bench run)."""
     for p in sorted((ROOT / "profiles").glob("*.md")):
         cell_line = traffic = None
         for line in p.read_text().splitlines():
@@ -817,16 +898,18 @@ def _traffic_from_profiles(cell: str):
             elif line.startswith("dram_bytes_per_launch:"):
                 traffic = int(line.split(":", 1)[1].strip())
         if cell_line == cell and traffic is not None:
-            return traffic
-    return None
+            return traffic, f"ncu capture summarised in profiles/{p.name}"
+    return None, None
 
 
 def _cpu_baseline() -> dict:
     threads = os.cpu_count() or 1
-    res = cpu_sweep(max_calls=20, min_seconds=10.0, max_seconds=30.0, threads=threads)
+    cpu = CpuSweep(threads)
+    cpu.run(max_steps=1, min_seconds=0.0, max_seconds=30.0)
+    res = cpu.run(max_steps=2, min_seconds=10.0, max_seconds=30.0)
     return {"value": res["value"], "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{res['calls']} F.linear calls over the 20 sweep cells in sweep order ({res['seconds']} s), "
-                      "torch bf16 on the host = byteprof SkinnyLinear's CPU branch"}
+            "sample": f"{res['steps']} whole sweeps (20 F.linear calls each, cells in sweep order) in "
+                      f"{res['seconds']} s, torch bf16 on the host = byteprof SkinnyLinear's CPU branch"}
 
 
 def run_case(args) -> int:

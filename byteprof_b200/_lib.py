@@ -56,6 +56,8 @@ _SIGNATURES = {
                               c_int, c_int, c_int, c_int, c_longlong, c_longlong, c_longlong, c_longlong,
                               c_int, c_int, c_float, c_float, c_void_p]),
     "bp_mlstm_accept": (c_int, [c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p]),
+    "bp_mlstm_commit_state": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong,
+                                      c_longlong, c_longlong, c_void_p, c_int, c_int, c_void_p]),
     "bp_device_errors": (c_int, [ctypes.POINTER(ctypes.c_uint)]),
 }
 

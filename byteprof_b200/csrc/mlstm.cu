@@ -423,6 +423,47 @@ __global__ void accept_kernel(const int64_t* ids, const int64_t* tok, int64_t* o
   out[smax] = n;
 }
 
+// State commit of the drafting loop: cur <- hist[slot] for the three tensors of one layer's state, the slot
+// (the accepted length) read on the device so that a CUDA graph replays the commit for whatever length the
+// round accepted. Segment j copies cnt[j] floats from src[j] + slot * cnt[j] to dst[j]; 16-byte copies when
+// every address and count allows, single floats otherwise. A slot outside [0, slots) fills cur with NaN and
+// reads nothing.
+struct CommitArgs {
+  const float* src[3];
+  float* dst[3];
+  long long cnt[3];
+  const void* slot;
+  int slot_bytes;  // 4 (int32) or 8 (int64)
+  int slots;
+  int vec;  // 1: 16-byte copies
+};
+
+__global__ void __launch_bounds__(256) commit_state_kernel(const CommitArgs a) {
+  const long long slot = a.slot_bytes == 8 ? *static_cast<const long long*>(a.slot)
+                                           : static_cast<long long>(*static_cast<const int*>(a.slot));
+  const bool ok = slot >= 0 && slot < a.slots;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long t0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const long long n = a.cnt[j];
+    if (n == 0) continue;
+    float* d = a.dst[j];
+    if (!ok) {
+      for (long long e = t0; e < n; e += stride) d[e] = __int_as_float(0x7fc00000);
+      continue;
+    }
+    const float* sp = a.src[j] + slot * n;
+    if (a.vec) {
+      const float4* s4 = reinterpret_cast<const float4*>(sp);
+      float4* d4 = reinterpret_cast<float4*>(d);
+      for (long long e = t0; e < n / 4; e += stride) d4[e] = __ldcs(s4 + e);
+    } else {
+      for (long long e = t0; e < n; e += stride) d[e] = sp[e];
+    }
+  }
+}
+
 // Opts the kernel into `bytes` of dynamic shared memory, once per device.
 template <typename K>
 int allow_dynamic_smem(K kernel, size_t bytes, bool* done) {
@@ -514,4 +555,38 @@ extern "C" int bp_mlstm_accept(const int64_t* ids, const int64_t* tok, int64_t* 
   if (st != BP_OK) return st;
   accept_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ids, tok, out, S, smax);
   return check_launch("accept launch");
+}
+
+// Counterpart of byteprof/optim/draft_core.py:92-111 (commit_state and its Triton commit_kernel,
+// byteprof/optim/draft_kernels.py:7-18).
+extern "C" int bp_mlstm_commit_state(const float* c_hist, const float* n_hist, const float* m_hist, float* c_cur,
+                                     float* n_cur, float* m_cur, long long c_count, long long n_count, long long m_count,
+                                     const void* slot, int slot_bytes, int slots, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (c_count < 0 || n_count < 0 || m_count < 0 || slots <= 0)
+    return fail(BP_ERR_INVALID_ARGUMENT, "negative count or no history slots");
+  if (slot_bytes != 4 && slot_bytes != 8) return fail(BP_ERR_INVALID_ARGUMENT, "slot must be int32 or int64");
+  if (slot == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "slot is NULL");
+  if ((c_count > 0 && (c_hist == nullptr || c_cur == nullptr)) || (n_count > 0 && (n_hist == nullptr || n_cur == nullptr)) ||
+      (m_count > 0 && (m_hist == nullptr || m_cur == nullptr)))
+    return fail(BP_ERR_INVALID_ARGUMENT, "NULL state pointer");
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  CommitArgs a;
+  a.src[0] = c_hist; a.src[1] = n_hist; a.src[2] = m_hist;
+  a.dst[0] = c_cur; a.dst[1] = n_cur; a.dst[2] = m_cur;
+  a.cnt[0] = c_count; a.cnt[1] = n_count; a.cnt[2] = m_count;
+  a.slot = slot;
+  a.slot_bytes = slot_bytes;
+  a.slots = slots;
+  a.vec = 1;
+  for (int j = 0; j < 3; ++j)
+    if (a.cnt[j] % 4 != 0 || !al16(a.src[j]) || !al16(a.dst[j])) a.vec = 0;
+  long long most = c_count > n_count ? c_count : n_count;
+  most = most > m_count ? most : m_count;
+  long long blocks = (most / (a.vec ? 4 : 1) + 255) / 256;
+  blocks = blocks < 1 ? 1 : (blocks > 4 * 148 ? 4 * 148 : blocks);
+  commit_state_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("commit state launch");
 }

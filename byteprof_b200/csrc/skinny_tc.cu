@@ -612,15 +612,18 @@ extern "C" int bp_skinny_mm_static_scratch(const void* x, long long ldx, const v
   if (M > 0 && N > 0 && K > 0 && (w_dtype == BP_DTYPE_BF16 || w_dtype == BP_DTYPE_INT8)) {
     int st = require_sm100();
     if (st != BP_OK) return st;
+    // The address is resolved on every such call, whatever the shape, before the size checks: then the
+    // first call on a device does the lookup (which may load the module) even when its own shape needs no
+    // scratch, and a later call made during stream capture never does.
+    void* scratch = nullptr;
+    st = static_scratch_ptr(&scratch);
+    if (st != BP_OK) return st;
     const size_t need = skinny_tc_workspace_bytes(N, K, w_dtype == BP_DTYPE_INT8);
     if ((N + kBM - 1) / kBM > kTcMaxTiles || need > kStaticScratchBytes)
       return fail(BP_ERR_UNSUPPORTED,
                   "N=%d K=%d needs %zu bytes of scratch; the static scratch holds %zu (N <= %d rows, <= %d SMs)", N, K,
                   need, kStaticScratchBytes, kTcMaxTiles * kBM, kStaticMaxCtas);
     if (need > 0) {
-      void* scratch = nullptr;
-      st = static_scratch_ptr(&scratch);
-      if (st != BP_OK) return st;
       // The tile counters must start at zero. Every call leaves them at zero, but a call that stopped
       // early (device error) would not, so they are cleared on the stream before each call.
       const size_t tiles = static_cast<size_t>((N + kBM - 1) / kBM);

@@ -17,6 +17,7 @@
  *                       byteprof/optim/mlstm_multistep.py:89-133 lazy_commit_kernel
  *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
  *   bp_mlstm_accept     byteprof/optim/mlstm_multistep.py:136-146 accept_kernel
+ *   bp_mlstm_commit_state byteprof/optim/draft_core.py:92-111  commit_state (+ draft_kernels.py commit_kernel)
  *   bp_rmsnorm_ex, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish, bp_glob_step,
  *   bp_loc_enc_step, bp_loc_dec_step
  *                       the per-byte pieces of the minimal Bolmo loop: byteprof/optim/bolmo.py:32-136
@@ -310,6 +311,19 @@ int bp_mlstm_scan(const float* c_in, const float* n_in, const float* m_in, const
  * Replaces accept_kernel (byteprof/optim/mlstm_multistep.py:136-146).
  */
 int bp_mlstm_accept(const int64_t* ids, const int64_t* tok, int64_t* out, int S, int smax, void* stream);
+
+/*
+ * State commit of the drafting loop: cur <- hist[slot] for one layer's state, slot = *slot read on the
+ * device (int32 when slot_bytes = 4, int64 when 8), so a captured graph commits whatever length a round
+ * accepted. c_hist / n_hist / m_hist hold `slots` consecutive copies of c_count / n_count / m_count fp32
+ * values (history slots [slots, 1, NH, DQ, DV], [slots, 1, NH, DQ], [slots, 1, NH, 1]); c_cur / n_cur /
+ * m_cur receive slot `slot`. A slot outside [0, slots) fills cur with NaN and reads no history.
+ * Replaces commit_state and its commit_kernel (byteprof/optim/draft_core.py:92-111,
+ * byteprof/optim/draft_kernels.py:7-18).
+ */
+int bp_mlstm_commit_state(const float* c_hist, const float* n_hist, const float* m_hist, float* c_cur, float* n_cur,
+                          float* m_cur, long long c_count, long long n_count, long long m_count, const void* slot,
+                          int slot_bytes, int slots, void* stream);
 
 /*
  * Device error flags raised by the kernels since the last call, then cleared (synchronises the current

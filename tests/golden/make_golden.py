@@ -1,8 +1,8 @@
 """Generates the golden vectors in tests/golden/golden.npz by running the reference's own code.
 
-Run in a container where the byteprof project is checked out (default path below, or $BYTEPROF_REF):
+Run where the byteprof project is checked out, naming its root with --ref or $BYTEPROF_REF:
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    TRITON_INTERPRET=1 python tests/golden/make_golden.py --ref <path to byteprof checkout>
 
 What it runs (paths inside the byteprof project):
   * byteprof/quant/triton_int8.py:50-55  quantize_rowwise_int8 on seeded bf16 weights (torch, CPU)
@@ -32,16 +32,30 @@ os.environ.setdefault("TRITON_INTERPRET", "1")
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = Path(os.environ.get("BYTEPROF_REF", "/root/reference"))
 OUT = Path(__file__).resolve().parent / "golden.npz"
+
+
+def reference_root(argv: list[str]) -> Path:
+    """The byteprof checkout: --ref PATH, else $BYTEPROF_REF; there is no default."""
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("BYTEPROF_REF"))
+    a = ap.parse_args(argv)
+    if not a.ref:
+        ap.error("name the byteprof checkout with --ref or $BYTEPROF_REF")
+    root = Path(a.ref)
+    if not (root / "byteprof").is_dir():
+        ap.error(f"{root} holds no byteprof package")
+    return root
 
 
 def bits(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().view(torch.int16).numpy().view(np.uint16).copy()
 
 
-def main() -> None:
-    sys.path.insert(0, str(REF))
+def main(argv: list[str] | None = None) -> None:
+    sys.path.insert(0, str(reference_root(sys.argv[1:] if argv is None else argv)))
     import triton
     import triton.language as tl
 

@@ -48,6 +48,38 @@ def test_static_scratch_matches_the_workspace_entry_point_twice_in_a_row(kind, n
     assert _lib.device_errors() == 0
 
 
+def test_static_scratch_entry_runs_inside_a_global_mode_graph_capture():
+    """The use case it exists for: a stream captured in global mode, where allocation is refused. One call
+    with a small shape (which needs no scratch) before the capture is the documented warm-up; the large bf16
+    and int8 calls captured afterwards use the array and must not look anything up or allocate. Replayed
+    twice, the graph gives the results of skinny_mm with a caller workspace."""
+    dev = torch.device("cuda", torch.cuda.current_device())
+    xs = torch.randn(3, 256, device=dev).to(torch.bfloat16)
+    ws_small = torch.randn(37, 256, device=dev).to(torch.bfloat16)
+    _static_scratch_mm(xs, ws_small, torch.empty(3, 37, device=dev, dtype=torch.bfloat16))
+    cases = []
+    for kind, n, k, m in (("bf16", 100352, 2048, 4), ("int8", 100352, 2048, 16)):
+        _, args = make_weights(kind, n, k, seed=41)
+        x = torch.randn(m, k, generator=torch.Generator(device=dev).manual_seed(9), device=dev).to(torch.bfloat16)
+        want = skinny_mm(x, *args)  # loads the kernels this shape runs, outside the capture
+        cases.append((x, args, torch.empty(m, n, device=dev, dtype=torch.bfloat16), want, kind))
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(dev)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side, capture_error_mode="global"):
+        for x, args, out, _, kind in cases:
+            _static_scratch_mm(x, args[0], out, args[1] if kind == "int8" else None)
+    for _ in range(2):
+        for _, _, out, _, _ in cases:
+            out.fill_(float("nan"))
+        g.replay()
+        torch.cuda.synchronize()
+        for _, _, out, want, kind in cases:
+            assert torch.equal(out, want), kind
+    del g
+    assert _lib.device_errors() == 0
+
+
 def test_static_scratch_rejects_problems_beyond_its_limit():
     x = torch.zeros(1, 64, device="cuda", dtype=torch.bfloat16)
     w = torch.zeros(8, 64, device="cuda", dtype=torch.bfloat16)
