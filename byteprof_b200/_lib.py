@@ -30,18 +30,20 @@ _SIGNATURES = {
     "bp_skinny_workspace_bytes": (c_size_t, [c_int, c_int, c_int, c_int]),
     "bp_skinny_mm_static_scratch": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_void_p, c_longlong,
                                             c_int, c_int, c_int, c_int, c_void_p]),
+    "bp_skinny_mm_xf32": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_void_p, c_longlong, c_int,
+                                  c_int, c_int, c_int, c_void_p]),
     "bp_gemv_int8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p, c_size_t,
                              c_void_p]),
     "bp_skinny_mm_int4": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_void_p, c_void_p, c_longlong, c_int,
                                   c_int, c_int, c_int, c_int, c_void_p, c_size_t, c_void_p]),
     "bp_rmsnorm": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_longlong, c_int, c_int, c_float, c_void_p]),
     "bp_rmsnorm_ex": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_longlong, c_void_p, c_longlong,
-                              c_void_p, c_longlong, c_int, c_int, c_float, c_int, c_void_p]),
-    "bp_swiglu": (c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int, c_void_p]),
+                              c_void_p, c_longlong, c_int, c_int, c_float, c_int, c_int, c_void_p]),
+    "bp_swiglu": (c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int, c_int, c_void_p]),
     "bp_gate_softcap": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_longlong, c_int, c_int, c_float,
                                 c_void_p]),
     "bp_decode_attention": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
-                                    c_void_p, c_int, c_int, c_int, c_float, c_float, c_void_p]),
+                                    c_void_p, c_int, c_int, c_int, c_float, c_float, c_int, c_void_p]),
     "bp_decode_finish": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "bp_glob_step_workspace_bytes": (c_size_t, []),
     "bp_loc_step_workspace_bytes": (c_size_t, []),

@@ -14,8 +14,10 @@
 //
 // All kernels let the next kernel launch at once (programmatic dependent launch) and wait for the
 // previous one before reading anything, so a following skinny GEMM streams its weights while these
-// run. Rounding points are those of the same steps written with bf16 torch tensors: every bf16
-// intermediate is rounded where a bf16 tensor would hold it; arithmetic in between is fp32.
+// run. Activations (and the attention's KV cache) are bf16 or fp32 (`Act<T>`); weights are bf16.
+// With bf16 activations the rounding points are those of the same steps written with bf16 torch
+// tensors: every bf16 intermediate is rounded where a bf16 tensor would hold it, arithmetic in between
+// is fp32. With fp32 activations nothing is rounded to bf16 (the decoder's exactness mode).
 #include <math.h>
 
 #include "bp_common.cuh"
@@ -31,6 +33,43 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   const __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<const uint32_t*>(&p);
 }
+
+__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
+  f[0] = bf16lo(v.x); f[1] = bf16hi(v.x); f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
+  f[4] = bf16lo(v.z); f[5] = bf16hi(v.z); f[6] = bf16lo(v.w); f[7] = bf16hi(v.w);
+}
+
+// Activation element type: loads and stores of 8 consecutive values (16-byte aligned), single values,
+// and the rounding a value of that type holds.
+template <typename T>
+struct Act;
+template <>
+struct Act<__nv_bfloat16> {
+  static constexpr int kDtype = BP_DTYPE_BF16;
+  __device__ static __forceinline__ void load8(const __nv_bfloat16* p, float (&f)[8]) { unpack8(ldg16(p), f); }
+  __device__ static __forceinline__ void store8(__nv_bfloat16* p, const float (&f)[8]) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                              pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  }
+  __device__ static __forceinline__ float load1(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+  __device__ static __forceinline__ void store1(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+  __device__ static __forceinline__ float rnd(float v) { return round_bf16(v); }
+};
+template <>
+struct Act<float> {
+  static constexpr int kDtype = BP_DTYPE_F32;
+  __device__ static __forceinline__ void load8(const float* p, float (&f)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+  __device__ static __forceinline__ void store8(float* p, const float (&f)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+  __device__ static __forceinline__ float load1(const float* p) { return *p; }
+  __device__ static __forceinline__ void store1(float* p, float v) { *p = v; }
+  __device__ static __forceinline__ float rnd(float v) { return v; }
+};
 
 template <typename Kern, typename... Args>
 cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, cudaStream_t stream, Args... args) {
@@ -60,16 +99,17 @@ cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, cudaStream_t stream, Ar
 constexpr int kNormThreads = 256;
 constexpr int kNormCache = 4;
 
+template <typename T>
 struct NormArgs {
-  const __nv_bfloat16* x;
+  const T* x;
   long long ldx;
   const __nv_bfloat16* w;
   int w_rows;
-  const __nv_bfloat16* res;
+  const T* res;
   long long ldres;
-  __nv_bfloat16* s_out;
+  T* s_out;
   long long lds;
-  __nv_bfloat16* y;
+  T* y;
   long long ldy;
   int rows, cols;
   float eps;
@@ -81,19 +121,14 @@ __device__ __forceinline__ long long row_off(int r, int w_rows, int cols, long l
   return static_cast<long long>(r / w_rows) * ld + static_cast<long long>(r % w_rows) * cols;
 }
 
-__device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
-  f[0] = bf16lo(v.x); f[1] = bf16hi(v.x); f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
-  f[4] = bf16lo(v.z); f[5] = bf16hi(v.z); f[6] = bf16lo(v.w); f[7] = bf16hi(v.w);
-}
-
-template <int MODE>
-__device__ __forceinline__ void norm_in8(const __nv_bfloat16* xr, const __nv_bfloat16* rr, int c, float (&f)[8]) {
-  unpack8(ldg16(xr + c), f);
-  if (MODE == BP_NORM_ADD_FIRST) {  // the normalised value is the bf16 sum
+template <int MODE, typename T>
+__device__ __forceinline__ void norm_in8(const T* xr, const T* rr, int c, float (&f)[8]) {
+  Act<T>::load8(xr + c, f);
+  if (MODE == BP_NORM_ADD_FIRST) {  // the normalised value is the sum as the activation type holds it
     float g[8];
-    unpack8(ldg16(rr + c), g);
+    Act<T>::load8(rr + c, g);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) f[j] = round_bf16(__fadd_rn(f[j], g[j]));
+    for (int j = 0; j < 8; ++j) f[j] = Act<T>::rnd(__fadd_rn(f[j], g[j]));
   }
 }
 
@@ -101,31 +136,28 @@ __device__ __forceinline__ void norm_in8(const __nv_bfloat16* xr, const __nv_bfl
 // but rare cases), so that every implementation that does the same gets the same bits.
 __device__ __forceinline__ float sigmoid_d(float v) { return static_cast<float>(1.0 / (1.0 + exp(-static_cast<double>(v)))); }
 
-template <int MODE>
-__device__ __forceinline__ void norm_out8(const float (&f)[8], float inv, const __nv_bfloat16* wr,
-                                          const __nv_bfloat16* rr, __nv_bfloat16* sr, __nv_bfloat16* yr, int c) {
+template <int MODE, typename T>
+__device__ __forceinline__ void norm_out8(const float (&f)[8], float inv, const __nv_bfloat16* wr, const T* rr, T* sr,
+                                          T* yr, int c) {
   float wv[8], o[8];
   unpack8(ldg16(wr + c), wv);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], inv), wv[j]);  // bf16(x * inv * w) below
+  for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], inv), wv[j]);  // rounded to T by the store
   if (MODE == BP_NORM_ADD_AFTER || MODE == BP_NORM_GATE) {
     float e[8];
-    unpack8(ldg16(rr + c), e);
+    Act<T>::load8(rr + c, e);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float nb = round_bf16(o[j]);
-      o[j] = MODE == BP_NORM_ADD_AFTER ? __fadd_rn(e[j], nb) : __fmul_rn(round_bf16(sigmoid_d(e[j])), nb);
+      const float nb = Act<T>::rnd(o[j]);
+      o[j] = MODE == BP_NORM_ADD_AFTER ? __fadd_rn(e[j], nb) : __fmul_rn(Act<T>::rnd(sigmoid_d(e[j])), nb);
     }
   }
-  if (sr != nullptr)
-    *reinterpret_cast<uint4*>(sr + c) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                                   pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
-  *reinterpret_cast<uint4*>(yr + c) = make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]),
-                                                 pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  if (sr != nullptr) Act<T>::store8(sr + c, f);
+  Act<T>::store8(yr + c, o);
 }
 
-template <int MODE, bool kCached>
-__global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs a) {
+template <int MODE, bool kCached, typename T>
+__global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs<T> a) {
   __shared__ float red[kNormThreads / 32];
   pdl_launch_dependents();
   pdl_wait_prior_grids();
@@ -135,8 +167,8 @@ __global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs a) {
   const bool live = r < a.rows;
   const int rc = live ? r : a.rows - 1;  // rows past the end read the last row and store nothing
   const __nv_bfloat16* wr = a.w + static_cast<long long>(rc % a.w_rows) * a.cols;
-  const __nv_bfloat16* xr = a.x + row_off(rc, a.w_rows, a.cols, a.ldx);
-  const __nv_bfloat16* rr = MODE == BP_NORM_PLAIN ? nullptr : a.res + row_off(rc, a.w_rows, a.cols, a.ldres);
+  const T* xr = a.x + row_off(rc, a.w_rows, a.cols, a.ldx);
+  const T* rr = MODE == BP_NORM_PLAIN ? nullptr : a.res + row_off(rc, a.w_rows, a.cols, a.ldres);
   float f[kCached ? kNormCache : 1][8];
   float ss = 0.0f;
   if (kCached) {
@@ -144,14 +176,14 @@ __global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs a) {
     for (int i = 0; i < kNormCache; ++i) {
       const int c = (t + i * team) * 8;
       if (i < a.iters && c < a.cols) {
-        norm_in8<MODE>(xr, rr, c, f[i]);
+        norm_in8<MODE, T>(xr, rr, c, f[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) ss = fmaf(f[i][j], f[i][j], ss);
       }
     }
   } else {
     for (int c = t * 8; c < a.cols; c += team * 8) {
-      norm_in8<MODE>(xr, rr, c, f[0]);
+      norm_in8<MODE, T>(xr, rr, c, f[0]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss = fmaf(f[0][j], f[0][j], ss);
     }
@@ -164,43 +196,42 @@ __global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs a) {
   for (int w = 0; w < warps; ++w) tot += red[slot * warps + w];
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(a.cols)), a.eps)));
   if (!live) return;
-  __nv_bfloat16* yr = a.y + row_off(r, a.w_rows, a.cols, a.ldy);
-  __nv_bfloat16* sr = (MODE == BP_NORM_ADD_FIRST && a.s_out != nullptr) ? a.s_out + row_off(r, a.w_rows, a.cols, a.lds)
-                                                                        : nullptr;
+  T* yr = a.y + row_off(r, a.w_rows, a.cols, a.ldy);
+  T* sr = (MODE == BP_NORM_ADD_FIRST && a.s_out != nullptr) ? a.s_out + row_off(r, a.w_rows, a.cols, a.lds) : nullptr;
   if (kCached) {
 #pragma unroll
     for (int i = 0; i < kNormCache; ++i) {
       const int c = (t + i * team) * 8;
-      if (i < a.iters && c < a.cols) norm_out8<MODE>(f[i], inv, wr, rr, sr, yr, c);
+      if (i < a.iters && c < a.cols) norm_out8<MODE, T>(f[i], inv, wr, rr, sr, yr, c);
     }
   } else {
     for (int c = t * 8; c < a.cols; c += team * 8) {
-      norm_in8<MODE>(xr, rr, c, f[0]);
-      norm_out8<MODE>(f[0], inv, wr, rr, sr, yr, c);
+      norm_in8<MODE, T>(xr, rr, c, f[0]);
+      norm_out8<MODE, T>(f[0], inv, wr, rr, sr, yr, c);
     }
   }
 }
 
 // ---- SwiGLU ---------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) swiglu_kernel(const __nv_bfloat16* __restrict__ gu, long long ldgu,
-                                                     __nv_bfloat16* __restrict__ out, long long ldo, int ffn) {
+// silu in double precision, rounded once to fp32, then to T; the product rounded to T by the store.
+template <typename T>
+__global__ void __launch_bounds__(256) swiglu_kernel(const T* __restrict__ gu, long long ldgu, T* __restrict__ out,
+                                                     long long ldo, int ffn) {
   pdl_launch_dependents();
   pdl_wait_prior_grids();
   const int j = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
   const int r = blockIdx.y;
   if (j >= ffn) return;
-  const __nv_bfloat16* row = gu + static_cast<long long>(r) * ldgu;
-  const uint4 g = ldg16(row + j), u = ldg16(row + ffn + j);
-  const uint32_t gv[4] = {g.x, g.y, g.z, g.w}, uv[4] = {u.x, u.y, u.z, u.w};
-  uint32_t o[4];
+  const T* row = gu + static_cast<long long>(r) * ldgu;
+  float g[8], u[8], o[8];
+  Act<T>::load8(row + j, g);
+  Act<T>::load8(row + ffn + j, u);
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const float g0 = bf16lo(gv[q]), g1 = bf16hi(gv[q]);
-    const float s0 = round_bf16(static_cast<float>(g0 / (1.0 + exp(-static_cast<double>(g0)))));
-    const float s1 = round_bf16(static_cast<float>(g1 / (1.0 + exp(-static_cast<double>(g1)))));
-    o[q] = pack_bf16x2(__fmul_rn(s0, bf16lo(uv[q])), __fmul_rn(s1, bf16hi(uv[q])));
+  for (int q = 0; q < 8; ++q) {
+    const float sl = Act<T>::rnd(static_cast<float>(g[q] / (1.0 + exp(-static_cast<double>(g[q])))));
+    o[q] = __fmul_rn(sl, u[q]);
   }
-  *reinterpret_cast<uint4*>(out + static_cast<long long>(r) * ldo + j) = make_uint4(o[0], o[1], o[2], o[3]);
+  Act<T>::store8(out + static_cast<long long>(r) * ldo + j, o);
 }
 
 // ---- gate soft cap ----------------------------------------------------------------------------------
@@ -229,18 +260,39 @@ constexpr int kCtaSpan = kAttnWarps * kPerWarp;   // 128 positions per CTA and r
 constexpr int kAttnCluster = 8;                    // CTAs per head
 constexpr int kRound = kAttnCluster * kCtaSpan;    // 1024 positions per round
 
+template <typename T>
 struct AttnArgs {
-  const __nv_bfloat16* qkv;  // [3 * nh * kHd]: q | k | v of the current position
+  const T* qkv;              // [3 * nh * kHd]: q | k | v of the current position
   const __nv_bfloat16* qw;   // q RMSNorm weight [nh * kHd]
   const __nv_bfloat16* kw;   // k RMSNorm weight [nh * kHd]
   const float* cos_t;        // [max_pos, kHd / 2]
   const float* sin_t;
   const long long* pos;      // device: the position of this query
-  __nv_bfloat16* kc;         // [max_pos, nh, kHd]
-  __nv_bfloat16* vc;
-  __nv_bfloat16* out;        // [nh * kHd]
+  T* kc;                     // [max_pos, nh, kHd]
+  T* vc;
+  T* out;                    // [nh * kHd]
   int nh, max_pos;
   float eps, scale;
+};
+
+// Four consecutive cache values of one row as a lane holds them (8 bytes of bf16, 16 bytes of fp32).
+template <typename T>
+struct Row4;
+template <>
+struct Row4<__nv_bfloat16> {
+  uint2 v;
+  __device__ __forceinline__ void zero() { v = make_uint2(0u, 0u); }
+  __device__ __forceinline__ void load(const __nv_bfloat16* p) { v = __ldg(reinterpret_cast<const uint2*>(p)); }
+  __device__ __forceinline__ void get(float (&f)[4]) const {
+    f[0] = bf16lo(v.x); f[1] = bf16hi(v.x); f[2] = bf16lo(v.y); f[3] = bf16hi(v.y);
+  }
+};
+template <>
+struct Row4<float> {
+  float4 v;
+  __device__ __forceinline__ void zero() { v = make_float4(0.f, 0.f, 0.f, 0.f); }
+  __device__ __forceinline__ void load(const float* p) { v = __ldg(reinterpret_cast<const float4*>(p)); }
+  __device__ __forceinline__ void get(float (&f)[4]) const { f[0] = v.x; f[1] = v.y; f[2] = v.z; f[3] = v.w; }
 };
 
 
@@ -248,22 +300,24 @@ __device__ __forceinline__ float inv_rms(float sum_sq, int n, float eps) {
   return __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(sum_sq, static_cast<float>(n)), eps)));
 }
 
-__device__ __forceinline__ void load_rows(const AttnArgs& a, long long base, long long p, int h, int lane,
-                                          uint2 (&kk)[kPerWarp], uint2 (&vv)[kPerWarp]) {
+template <typename T>
+__device__ __forceinline__ void load_rows(const AttnArgs<T>& a, long long base, long long p, int h, int lane,
+                                          Row4<T> (&kk)[kPerWarp], Row4<T> (&vv)[kPerWarp]) {
 #pragma unroll
   for (int j = 0; j < kPerWarp; ++j) {
-    kk[j] = make_uint2(0u, 0u);
-    vv[j] = make_uint2(0u, 0u);
+    kk[j].zero();
+    vv[j].zero();
     if (base + j < p) {  // rows below p were written by earlier launches; row p comes from this CTA
       const long long off = ((base + j) * a.nh + h) * kHd + lane * 4;
-      kk[j] = __ldg(reinterpret_cast<const uint2*>(a.kc + off));
-      vv[j] = __ldg(reinterpret_cast<const uint2*>(a.vc + off));
+      kk[j].load(a.kc + off);
+      vv[j].load(a.vc + off);
     }
   }
 }
 
+template <typename T>
 __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThreads)
-    decode_attention_kernel(AttnArgs a) {
+    decode_attention_kernel(AttnArgs<T> a) {
   constexpr int kHalf = kHd / 2;
   __shared__ __align__(16) float qs[kHd];
   __shared__ __align__(16) float ks[kHd];  // position p's rotated k (bf16 values) and v, owner CTA only
@@ -279,19 +333,19 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
   const int rank = static_cast<int>(cluster_ctarank()), h = blockIdx.y;
   const long long p = *a.pos;
   if (p < 0 || p >= a.max_pos) {  // the same p for the whole cluster: every CTA leaves here together
-    if (rank == 0 && tid < kHd) a.out[h * kHd + tid] = __float2bfloat16_rn(__int_as_float(0x7fc00000));
+    if (rank == 0 && tid < kHd) Act<T>::store1(a.out + h * kHd + tid, __int_as_float(0x7fc00000));
     return;
   }
   const int rounds = static_cast<int>(p / kRound) + 1;
   const bool own = static_cast<int>((p % kRound) / kCtaSpan) == rank;  // this CTA's range holds p
   const int d = a.nh * kHd;
-  const __nv_bfloat16* q = a.qkv;
-  const __nv_bfloat16* k = a.qkv + d;
-  const __nv_bfloat16* v = a.qkv + 2 * d;
+  const T* q = a.qkv;
+  const T* k = a.qkv + d;
+  const T* v = a.qkv + 2 * d;
 
   // Everything that depends only on p is requested first: round 0's cached rows of this warp, the
   // rotary factors, this head's q / k / v values and norm weights, the q and k vectors for the norms.
-  uint2 kk[kPerWarp], vv[kPerWarp];
+  Row4<T> kk[kPerWarp], vv[kPerWarp];
   load_rows(a, static_cast<long long>(rank) * kCtaSpan + warp * kPerWarp, p, h, lane, kk, vv);
   const int hi = h * kHd + (tid % kHalf);
   float cs = 0.0f, sn = 0.0f, qa = 0.0f, qb = 0.0f, qwa = 0.0f, qwb = 0.0f, ka = 0.0f, kb = 0.0f, kwa = 0.0f, kwb = 0.0f;
@@ -299,26 +353,26 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
   if (tid < kHalf) {
     cs = a.cos_t[p * kHalf + tid];
     sn = a.sin_t[p * kHalf + tid];
-    qa = __bfloat162float(q[hi]);
-    qb = __bfloat162float(q[hi + kHalf]);
+    qa = Act<T>::load1(q + hi);
+    qb = Act<T>::load1(q + hi + kHalf);
     qwa = __bfloat162float(a.qw[hi]);
     qwb = __bfloat162float(a.qw[hi + kHalf]);
     if (own) {
-      ka = __bfloat162float(k[hi]);
-      kb = __bfloat162float(k[hi + kHalf]);
+      ka = Act<T>::load1(k + hi);
+      kb = Act<T>::load1(k + hi + kHalf);
       kwa = __bfloat162float(a.kw[hi]);
       kwb = __bfloat162float(a.kw[hi + kHalf]);
     }
   } else if (own && tid < kHd) {
     const int j = (tid - kHalf) * 2;
-    va = __bfloat162float(v[h * kHd + j]);
-    vb = __bfloat162float(v[h * kHd + j + 1]);
+    va = Act<T>::load1(v + h * kHd + j);
+    vb = Act<T>::load1(v + h * kHd + j + 1);
   }
   float sq = 0.0f, sk = 0.0f;
   for (int c = tid * 8; c < d; c += kAttnThreads * 8) {
     float fq[8], fk[8];
-    unpack8(ldg16(q + c), fq);
-    unpack8(ldg16(k + c), fk);
+    Act<T>::load8(q + c, fq);
+    Act<T>::load8(k + c, fk);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       sq = fmaf(fq[j], fq[j], sq);
@@ -344,24 +398,24 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
   const float inv_q = inv_rms(tq, d, a.eps), inv_k = inv_rms(tk, d, a.eps);
   const long long slot = p * a.nh + h;  // cache row of (p, h)
   if (tid < kHalf) {
-    const float q0 = round_bf16(__fmul_rn(__fmul_rn(qa, inv_q), qwa));
-    const float q1 = round_bf16(__fmul_rn(__fmul_rn(qb, inv_q), qwb));
+    const float q0 = Act<T>::rnd(__fmul_rn(__fmul_rn(qa, inv_q), qwa));
+    const float q1 = Act<T>::rnd(__fmul_rn(__fmul_rn(qb, inv_q), qwb));
     qs[tid] = __fsub_rn(__fmul_rn(q0, cs), __fmul_rn(q1, sn));
     qs[tid + kHalf] = __fadd_rn(__fmul_rn(q1, cs), __fmul_rn(q0, sn));
     if (own) {
-      const float k0 = round_bf16(__fmul_rn(__fmul_rn(ka, inv_k), kwa));
-      const float k1 = round_bf16(__fmul_rn(__fmul_rn(kb, inv_k), kwb));
-      const __nv_bfloat16 r0 = __float2bfloat16_rn(__fsub_rn(__fmul_rn(k0, cs), __fmul_rn(k1, sn)));
-      const __nv_bfloat16 r1 = __float2bfloat16_rn(__fadd_rn(__fmul_rn(k1, cs), __fmul_rn(k0, sn)));
-      a.kc[slot * kHd + tid] = r0;
-      a.kc[slot * kHd + tid + kHalf] = r1;
-      ks[tid] = __bfloat162float(r0);
-      ks[tid + kHalf] = __bfloat162float(r1);
+      const float k0 = Act<T>::rnd(__fmul_rn(__fmul_rn(ka, inv_k), kwa));
+      const float k1 = Act<T>::rnd(__fmul_rn(__fmul_rn(kb, inv_k), kwb));
+      const float r0 = Act<T>::rnd(__fsub_rn(__fmul_rn(k0, cs), __fmul_rn(k1, sn)));
+      const float r1 = Act<T>::rnd(__fadd_rn(__fmul_rn(k1, cs), __fmul_rn(k0, sn)));
+      Act<T>::store1(a.kc + slot * kHd + tid, r0);
+      Act<T>::store1(a.kc + slot * kHd + tid + kHalf, r1);
+      ks[tid] = r0;
+      ks[tid + kHalf] = r1;
     }
   } else if (own && tid < kHd) {
     const int j = (tid - kHalf) * 2;
-    a.vc[slot * kHd + j] = __float2bfloat16_rn(va);
-    a.vc[slot * kHd + j + 1] = __float2bfloat16_rn(vb);
+    Act<T>::store1(a.vc + slot * kHd + j, va);
+    Act<T>::store1(a.vc + slot * kHd + j + 1, vb);
     vs[j] = va;
     vs[j + 1] = vb;
   }
@@ -380,7 +434,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
         const float4 t = *reinterpret_cast<const float4*>(&ks[lane * 4]);
         k4[0] = t.x; k4[1] = t.y; k4[2] = t.z; k4[3] = t.w;
       } else {
-        k4[0] = bf16lo(kk[j].x); k4[1] = bf16hi(kk[j].x); k4[2] = bf16lo(kk[j].y); k4[3] = bf16hi(kk[j].y);
+        kk[j].get(k4);
       }
       float dot = __fmul_rn(qv.x, k4[0]);
       dot = fmaf(qv.y, k4[1], dot);
@@ -419,7 +473,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
         const float4 t = *reinterpret_cast<const float4*>(&vs[lane * 4]);
         v4[0] = t.x; v4[1] = t.y; v4[2] = t.z; v4[3] = t.w;
       } else {
-        v4[0] = bf16lo(vv[j].x); v4[1] = bf16hi(vv[j].x); v4[2] = bf16lo(vv[j].y); v4[3] = bf16hi(vv[j].y);
+        vv[j].get(v4);
       }
 #pragma unroll
       for (int c = 0; c < 4; ++c) o4[c] = fmaf(e[j], v4[c], o4[c]);
@@ -464,7 +518,7 @@ __global__ void __cluster_dims__(kAttnCluster, 1, 1) __launch_bounds__(kAttnThre
     lg = fmaf(cl[c], f, lg);
     og = fmaf(co[c][tid], f, og);
   }
-  a.out[h * kHd + tid] = __float2bfloat16_rn(__fdiv_rn(og, lg));
+  Act<T>::store1(a.out + h * kHd + tid, __fdiv_rn(og, lg));
 }
 
 // ---- argmax + boundary flag --------------------------------------------------------------------------
@@ -528,15 +582,35 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 namespace bp {
 namespace {
 
-template <int MODE>
-cudaError_t launch_norm(NormArgs a, cudaStream_t s) {
+template <int MODE, typename T>
+cudaError_t launch_norm(NormArgs<T> a, cudaStream_t s) {
   int team = 32;  // threads per row: the power of two (32 to 256) covering cols / 8 chunks
   while (team < kNormThreads && team * 8 < a.cols) team *= 2;
   a.team = team;
   a.iters = (a.cols + team * 8 - 1) / (team * 8);
   const dim3 grid((a.rows + kNormThreads / team - 1) / (kNormThreads / team)), block(kNormThreads);
-  return a.iters <= kNormCache ? launch_pdl(norm_ex_kernel<MODE, true>, grid, block, s, a)
-                               : launch_pdl(norm_ex_kernel<MODE, false>, grid, block, s, a);
+  return a.iters <= kNormCache ? launch_pdl(norm_ex_kernel<MODE, true, T>, grid, block, s, a)
+                               : launch_pdl(norm_ex_kernel<MODE, false, T>, grid, block, s, a);
+}
+
+template <typename T>
+cudaError_t launch_norm_mode(const void* x, long long ldx, const void* w, int w_rows, const void* res, long long ldres,
+                             void* s_out, long long lds, void* y, long long ldy, int rows, int cols, float eps, int mode,
+                             cudaStream_t s) {
+  NormArgs<T> a{static_cast<const T*>(x), ldx, static_cast<const __nv_bfloat16*>(w), w_rows, static_cast<const T*>(res),
+                ldres, static_cast<T*>(s_out), lds, static_cast<T*>(y), ldy, rows, cols, eps, 0, 0};
+  switch (mode) {
+    case BP_NORM_PLAIN: return launch_norm<BP_NORM_PLAIN, T>(a, s);
+    case BP_NORM_ADD_FIRST: return launch_norm<BP_NORM_ADD_FIRST, T>(a, s);
+    case BP_NORM_ADD_AFTER: return launch_norm<BP_NORM_ADD_AFTER, T>(a, s);
+    default: return launch_norm<BP_NORM_GATE, T>(a, s);
+  }
+}
+
+int check_act_dtype(int dtype) {
+  if (dtype != BP_DTYPE_BF16 && dtype != BP_DTYPE_F32)
+    return fail(BP_ERR_INVALID_ARGUMENT, "activation dtype %d is not bf16 or fp32", dtype);
+  return BP_OK;
 }
 
 }  // namespace
@@ -544,9 +618,10 @@ cudaError_t launch_norm(NormArgs a, cudaStream_t s) {
 
 extern "C" int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_rows, const void* res, long long ldres,
                              void* s_out, long long lds, void* y, long long ldy, int rows, int cols, float eps, int mode,
-                             void* stream) {
+                             int dtype, void* stream) {
   using namespace bp;
   clear_error();
+  if (check_act_dtype(dtype) != BP_OK) return BP_ERR_INVALID_ARGUMENT;
   if (rows < 0 || cols < 0 || w_rows < 1)
     return fail(BP_ERR_INVALID_ARGUMENT, "bad size (rows=%d cols=%d w_rows=%d)", rows, cols, w_rows);
   if (mode < BP_NORM_PLAIN || mode > BP_NORM_GATE) return fail(BP_ERR_INVALID_ARGUMENT, "unknown norm mode %d", mode);
@@ -564,29 +639,26 @@ extern "C" int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_
     return fail(BP_ERR_MISALIGNED, "rmsnorm_ex needs 16-byte aligned rows, cols and strides multiples of 8");
   int st = require_sm100();
   if (st != BP_OK) return st;
-  NormArgs a{static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(w), w_rows,
-             static_cast<const __nv_bfloat16*>(res), ldres, static_cast<__nv_bfloat16*>(s_out), lds,
-             static_cast<__nv_bfloat16*>(y), ldy, rows, cols, eps, 0, 0};
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e;
-  switch (mode) {
-    case BP_NORM_PLAIN: e = launch_norm<BP_NORM_PLAIN>(a, s); break;
-    case BP_NORM_ADD_FIRST: e = launch_norm<BP_NORM_ADD_FIRST>(a, s); break;
-    case BP_NORM_ADD_AFTER: e = launch_norm<BP_NORM_ADD_AFTER>(a, s); break;
-    default: e = launch_norm<BP_NORM_GATE>(a, s); break;
-  }
+  const cudaError_t e =
+      dtype == BP_DTYPE_BF16
+          ? launch_norm_mode<__nv_bfloat16>(x, ldx, w, w_rows, res, ldres, s_out, lds, y, ldy, rows, cols, eps, mode, s)
+          : launch_norm_mode<float>(x, ldx, w, w_rows, res, ldres, s_out, lds, y, ldy, rows, cols, eps, mode, s);
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "rmsnorm_ex launch: %s", cudaGetErrorString(e));
   return check_launch("rmsnorm_ex");
 }
 
 extern "C" int bp_rmsnorm(const void* x, long long ldx, const void* w, void* y, long long ldy, int rows, int cols,
                           float eps, void* stream) {
-  return bp_rmsnorm_ex(x, ldx, w, 1, nullptr, 0, nullptr, 0, y, ldy, rows, cols, eps, BP_NORM_PLAIN, stream);
+  return bp_rmsnorm_ex(x, ldx, w, 1, nullptr, 0, nullptr, 0, y, ldy, rows, cols, eps, BP_NORM_PLAIN, BP_DTYPE_BF16,
+                       stream);
 }
 
-extern "C" int bp_swiglu(const void* gu, long long ldgu, void* out, long long ldo, int rows, int ffn, void* stream) {
+extern "C" int bp_swiglu(const void* gu, long long ldgu, void* out, long long ldo, int rows, int ffn, int dtype,
+                         void* stream) {
   using namespace bp;
   clear_error();
+  if (check_act_dtype(dtype) != BP_OK) return BP_ERR_INVALID_ARGUMENT;
   if (rows < 0 || ffn < 0) return fail(BP_ERR_INVALID_ARGUMENT, "negative size (rows=%d ffn=%d)", rows, ffn);
   if (rows == 0 || ffn == 0) return BP_OK;
   if (gu == nullptr || out == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "gu or out is NULL");
@@ -597,8 +669,13 @@ extern "C" int bp_swiglu(const void* gu, long long ldgu, void* out, long long ld
   int st = require_sm100();
   if (st != BP_OK) return st;
   const dim3 grid((ffn / 8 + 255) / 256, rows);
-  const cudaError_t e = launch_pdl(swiglu_kernel, grid, dim3(256), static_cast<cudaStream_t>(stream),
-                                   static_cast<const __nv_bfloat16*>(gu), ldgu, static_cast<__nv_bfloat16*>(out), ldo, ffn);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      dtype == BP_DTYPE_BF16
+          ? launch_pdl(swiglu_kernel<__nv_bfloat16>, grid, dim3(256), s, static_cast<const __nv_bfloat16*>(gu), ldgu,
+                       static_cast<__nv_bfloat16*>(out), ldo, ffn)
+          : launch_pdl(swiglu_kernel<float>, grid, dim3(256), s, static_cast<const float*>(gu), ldgu,
+                       static_cast<float*>(out), ldo, ffn);
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "swiglu launch: %s", cudaGetErrorString(e));
   return check_launch("swiglu");
 }
@@ -622,11 +699,28 @@ extern "C" int bp_gate_softcap(const float* g, long long ldg, const float* bias,
   return check_launch("gate_softcap");
 }
 
+namespace bp {
+namespace {
+
+template <typename T>
+cudaError_t launch_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos_t,
+                             const float* sin_t, const int64_t* pos, void* k_cache, void* v_cache, void* out, int nh,
+                             int max_pos, float eps, float scale, cudaStream_t s) {
+  AttnArgs<T> a{static_cast<const T*>(qkv), static_cast<const __nv_bfloat16*>(q_norm_w),
+                static_cast<const __nv_bfloat16*>(k_norm_w), cos_t, sin_t, reinterpret_cast<const long long*>(pos),
+                static_cast<T*>(k_cache), static_cast<T*>(v_cache), static_cast<T*>(out), nh, max_pos, eps, scale};
+  return launch_pdl(decode_attention_kernel<T>, dim3(kAttnCluster, nh), dim3(kAttnThreads), s, a);
+}
+
+}  // namespace
+}  // namespace bp
+
 extern "C" int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos_t,
                                    const float* sin_t, const int64_t* pos, void* k_cache, void* v_cache, void* out,
-                                   int nh, int head_dim, int max_pos, float eps, float scale, void* stream) {
+                                   int nh, int head_dim, int max_pos, float eps, float scale, int dtype, void* stream) {
   using namespace bp;
   clear_error();
+  if (check_act_dtype(dtype) != BP_OK) return BP_ERR_INVALID_ARGUMENT;
   if (head_dim != kHd) return fail(BP_ERR_UNSUPPORTED, "decode attention supports head_dim 128 (got %d)", head_dim);
   if (nh < 1 || nh > 65535 || max_pos < 1) return fail(BP_ERR_INVALID_ARGUMENT, "bad nh=%d or max_pos=%d", nh, max_pos);
   if (qkv == nullptr || q_norm_w == nullptr || k_norm_w == nullptr || cos_t == nullptr || sin_t == nullptr ||
@@ -636,12 +730,13 @@ extern "C" int bp_decode_attention(const void* qkv, const void* q_norm_w, const 
     return fail(BP_ERR_MISALIGNED, "qkv and the caches must be 16-byte aligned");
   int st = require_sm100();
   if (st != BP_OK) return st;
-  AttnArgs a{static_cast<const __nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(q_norm_w),
-             static_cast<const __nv_bfloat16*>(k_norm_w), cos_t, sin_t, reinterpret_cast<const long long*>(pos),
-             static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache),
-             static_cast<__nv_bfloat16*>(out), nh, max_pos, eps, scale};
-  const cudaError_t e = launch_pdl(decode_attention_kernel, dim3(kAttnCluster, nh), dim3(kAttnThreads),
-                                   static_cast<cudaStream_t>(stream), a);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const cudaError_t e =
+      dtype == BP_DTYPE_BF16
+          ? launch_attention<__nv_bfloat16>(qkv, q_norm_w, k_norm_w, cos_t, sin_t, pos, k_cache, v_cache, out, nh,
+                                            max_pos, eps, scale, s)
+          : launch_attention<float>(qkv, q_norm_w, k_norm_w, cos_t, sin_t, pos, k_cache, v_cache, out, nh, max_pos,
+                                    eps, scale, s);
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "decode_attention launch: %s", cudaGetErrorString(e));
   return check_launch("decode_attention");
 }

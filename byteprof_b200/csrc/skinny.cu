@@ -31,7 +31,7 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 
 struct SkinnyArgs {
-  const __nv_bfloat16* x;
+  const void* x;  // bf16 or fp32 (the kernel's XT)
   long long ldx;
   const void* w;
   const __nv_bfloat16* scale;  // int8 only: [N]
@@ -74,6 +74,15 @@ __device__ __forceinline__ void unpack_w(const uint4& v, float (&f)[16]) {
 }
 
 template <int EPL>
+__device__ __forceinline__ void load_x(const float* p, float (&f)[EPL]) {
+#pragma unroll
+  for (int h = 0; h < EPL / 4; ++h) {
+    const float4 v = __ldg(reinterpret_cast<const float4*>(p) + h);
+    f[4 * h + 0] = v.x; f[4 * h + 1] = v.y; f[4 * h + 2] = v.z; f[4 * h + 3] = v.w;
+  }
+}
+
+template <int EPL>
 __device__ __forceinline__ void load_x(const __nv_bfloat16* p, float (&f)[EPL]) {
 #pragma unroll
   for (int h = 0; h < EPL / 8; ++h) {
@@ -86,6 +95,7 @@ __device__ __forceinline__ void load_x(const __nv_bfloat16* p, float (&f)[EPL]) 
 }
 
 __device__ __forceinline__ float load_w1(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float load_w1(const float* p) { return *p; }
 __device__ __forceinline__ float load_w1(const int8_t* p) { return static_cast<float>(*p); }
 
 template <typename WT>
@@ -101,7 +111,7 @@ __device__ __forceinline__ void store_y(const SkinnyArgs& a, int m, int row, flo
     static_cast<__nv_bfloat16*>(a.y)[m * a.ldy + row] = __float2bfloat16_rn(v);
 }
 
-template <typename WT, int M, int R, int U, bool VEC>
+template <typename WT, int M, int R, int U, bool VEC, typename XT>
 __global__ void __launch_bounds__(kThreads) skinny_fma_kernel(const SkinnyArgs a) {
   constexpr int EPL = WTraits<WT>::EPL;
   constexpr int KW = VEC ? 32 * EPL : 32;  // K elements covered by one warp step
@@ -112,6 +122,7 @@ __global__ void __launch_bounds__(kThreads) skinny_fma_kernel(const SkinnyArgs a
   const int kb = blockIdx.y * a.k_chunk;
   const int ke = min(a.K, kb + a.k_chunk);
   const WT* __restrict__ w = static_cast<const WT*>(a.w);
+  const XT* __restrict__ x = static_cast<const XT*>(a.x);
 
   float acc[R][M];
 #pragma unroll
@@ -150,7 +161,7 @@ __global__ void __launch_bounds__(kThreads) skinny_fma_kernel(const SkinnyArgs a
         if (k < ke) {
           float xf[M][EPL];
 #pragma unroll
-          for (int m = 0; m < M; ++m) load_x<EPL>(a.x + m * a.ldx + k, xf[m]);
+          for (int m = 0; m < M; ++m) load_x<EPL>(x + m * a.ldx + k, xf[m]);
 #pragma unroll
           for (int r = 0; r < R; ++r) {
             float wf[EPL];
@@ -168,7 +179,7 @@ __global__ void __launch_bounds__(kThreads) skinny_fma_kernel(const SkinnyArgs a
     for (int k = kb + lane; k < ke; k += 32) {
       float xf[M];
 #pragma unroll
-      for (int m = 0; m < M; ++m) xf[m] = __bfloat162float(a.x[m * a.ldx + k]);
+      for (int m = 0; m < M; ++m) xf[m] = load_w1(x + m * a.ldx + k);
 #pragma unroll
       for (int r = 0; r < R; ++r) {
         const float wv = rv[r] ? load_w1(wr[r] + k) : 0.0f;
@@ -250,7 +261,7 @@ struct Tile<int8_t, M> {
   static constexpr int U = M <= 4 ? 3 : 2;
 };
 
-template <typename WT, int M>
+template <typename WT, int M, typename XT>
 int launch_rows(SkinnyArgs a, bool vec, cudaStream_t st) {
   constexpr int R = Tile<WT, M>::R;
   constexpr int U = Tile<WT, M>::U;
@@ -289,9 +300,9 @@ int launch_rows(SkinnyArgs a, bool vec, cudaStream_t st) {
   }
   cudaError_t e;
   if (vec)
-    e = cudaLaunchKernelEx(&cfg, skinny_fma_kernel<WT, M, R, U, true>, a);
+    e = cudaLaunchKernelEx(&cfg, skinny_fma_kernel<WT, M, R, U, true, XT>, a);
   else
-    e = cudaLaunchKernelEx(&cfg, skinny_fma_kernel<WT, M, R, U, false>, a);
+    e = cudaLaunchKernelEx(&cfg, skinny_fma_kernel<WT, M, R, U, false, XT>, a);
   if (e != cudaSuccess)
     return fail(BP_ERR_CUDA, "skinny launch (M=%d N=%d K=%d split=%d): %s", M, a.N, a.K, S, cudaGetErrorString(e));
   return BP_OK;
@@ -301,11 +312,25 @@ template <typename WT>
 int dispatch_m(const SkinnyArgs& a, int m, bool vec, cudaStream_t st) {
   switch (m) {
 #define BP_CASE(MM) \
-  case MM: return launch_rows<WT, MM>(a, vec, st);
+  case MM: return launch_rows<WT, MM, __nv_bfloat16>(a, vec, st);
     BP_CASE(1) BP_CASE(2) BP_CASE(3) BP_CASE(4) BP_CASE(5) BP_CASE(6) BP_CASE(7) BP_CASE(8)
     BP_CASE(9) BP_CASE(10) BP_CASE(11) BP_CASE(12) BP_CASE(13) BP_CASE(14) BP_CASE(15) BP_CASE(16)
 #undef BP_CASE
     default: return fail(BP_ERR_INVALID_ARGUMENT, "rows per launch must be 1..16, got %d", m);
+  }
+}
+
+// fp32 activations: up to 4 rows per launch (the decoder's exactness mode runs one).
+constexpr int kF32MaxRows = 4;
+
+template <typename WT>
+int dispatch_m_f32(const SkinnyArgs& a, int m, bool vec, cudaStream_t st) {
+  switch (m) {
+    case 1: return launch_rows<WT, 1, float>(a, vec, st);
+    case 2: return launch_rows<WT, 2, float>(a, vec, st);
+    case 3: return launch_rows<WT, 3, float>(a, vec, st);
+    case 4: return launch_rows<WT, 4, float>(a, vec, st);
+    default: return fail(BP_ERR_INVALID_ARGUMENT, "fp32 rows per launch must be 1..%d, got %d", kF32MaxRows, m);
   }
 }
 
@@ -414,4 +439,53 @@ extern "C" int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale,
                             void* workspace, size_t workspace_bytes, void* stream) {
   return bp::skinny_entry(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, workspace, workspace_bytes, stream,
                           N <= kGemvCudaCoreMaxN);
+}
+
+// Skinny linear with fp32 activations on the CUDA-core kernel (the decoder's exactness mode): the same
+// weights, K partition and summation order as the bf16-activation kernel, with x read as fp32.
+extern "C" int bp_skinny_mm_xf32(const float* x, long long ldx, const void* w, int w_dtype, const void* w_scale,
+                                 void* y, long long ldy, int y_dtype, int M, int N, int K, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (M < 0 || N < 0 || K < 0) return fail(BP_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d K=%d)", M, N, K);
+  if (w_dtype != BP_DTYPE_BF16 && w_dtype != BP_DTYPE_INT8)
+    return fail(BP_ERR_INVALID_ARGUMENT, "weight dtype %d is not bf16 or int8", w_dtype);
+  if (y_dtype != BP_DTYPE_BF16 && y_dtype != BP_DTYPE_F32)
+    return fail(BP_ERR_INVALID_ARGUMENT, "output dtype %d is not bf16 or fp32", y_dtype);
+  if (M == 0 || N == 0) return BP_OK;
+  if (y == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "y is NULL");
+  if (ldy < N) return fail(BP_ERR_INVALID_ARGUMENT, "ldy (%lld) < N (%d)", ldy, N);
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const size_t ysz = y_dtype == BP_DTYPE_F32 ? 4 : 2;
+  if (K == 0) {
+    cudaError_t e = cudaMemset2DAsync(y, static_cast<size_t>(ldy) * ysz, 0, static_cast<size_t>(N) * ysz, M, s);
+    if (e != cudaSuccess) return fail(BP_ERR_CUDA, "zero fill for K = 0: %s", cudaGetErrorString(e));
+    return BP_OK;
+  }
+  if (x == nullptr || w == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "x or w is NULL");
+  if (ldx < K) return fail(BP_ERR_INVALID_ARGUMENT, "ldx (%lld) < K (%d)", ldx, K);
+  if (w_dtype == BP_DTYPE_INT8 && w_scale == nullptr)
+    return fail(BP_ERR_INVALID_ARGUMENT, "int8 weights need a scale [N]");
+  const bool is8 = w_dtype == BP_DTYPE_INT8;
+  const int epl = is8 ? 16 : 8;
+  const bool vec = aligned16(x) && aligned16(w) && (ldx % 4 == 0) && (K % epl == 0);
+  SkinnyArgs a;
+  a.ldx = ldx;
+  a.w = w;
+  a.scale = static_cast<const __nv_bfloat16*>(w_scale);
+  a.ldy = ldy;
+  a.y_f32 = y_dtype == BP_DTYPE_F32;
+  a.N = N;
+  a.K = K;
+  a.k_chunk = K;
+  for (int r0 = 0; r0 < M; r0 += kF32MaxRows) {
+    const int m = M - r0 < kF32MaxRows ? M - r0 : kF32MaxRows;
+    a.x = x + static_cast<long long>(r0) * ldx;
+    a.y = static_cast<char*>(y) + static_cast<long long>(r0) * ldy * static_cast<long long>(ysz);
+    st = is8 ? dispatch_m_f32<int8_t>(a, m, vec, s) : dispatch_m_f32<__nv_bfloat16>(a, m, vec, s);
+    if (st != BP_OK) return st;
+  }
+  return BP_OK;
 }

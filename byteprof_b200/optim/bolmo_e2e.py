@@ -20,6 +20,11 @@ by kernel (GlobalBlock.step). fused_local=True runs each local step as one persi
 (decode_ops.LocStep, csrc/loc_step.cu); it is off by default because on B200 it measures slower than the
 kernel-by-kernel local step (a persistent kernel cannot start streaming its weights before the previous
 piece has left the GPU, while each skinny GEMM starts under its predecessor).
+
+precision="fp32" is the exactness mode: the same weights (bf16) with fp32 activations, fp32 KV caches
+and no rounding of any intermediate to bf16, kernel by kernel (skinny GEMMs read x as fp32, the glue
+kernels and the scan run their fp32 forms). It decodes the bytes that exact arithmetic on the same
+weights decodes, so it pins the whole model end to end; the default "bf16" mode is the fast one.
 """
 
 from __future__ import annotations
@@ -44,7 +49,8 @@ def _norm_w(gen, device, *shape):
 class GlobalBlock:
     """One OLMo-2 block for single-position decoding with a static KV cache."""
 
-    def __init__(self, d: int, nh: int, ffn: int, max_pos: int, gen: torch.Generator, device: torch.device):
+    def __init__(self, d: int, nh: int, ffn: int, max_pos: int, gen: torch.Generator, device: torch.device,
+                 act_dtype: torch.dtype = torch.bfloat16):
         self.d, self.nh, self.ffn = d, nh, ffn
         self.w_qkv = _rnd(gen, device, 3 * d, d)
         self.q_norm = _norm_w(gen, device, d)
@@ -54,10 +60,10 @@ class GlobalBlock:
         self.w_gu = _rnd(gen, device, 2 * ffn, d)
         self.w_down = _rnd(gen, device, d, ffn)
         self.mlp_norm = _norm_w(gen, device, d)
-        self.attn = DecodeAttention(nh, d // nh, max_pos, device)
+        self.attn = DecodeAttention(nh, d // nh, max_pos, device, dtype=act_dtype)
 
     def step(self, x: torch.Tensor, pos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
-        """x [1, d] bf16 at patch position `pos` (device int64) -> the block's output [1, d]."""
+        """x [1, d] (the activation dtype) at patch position `pos` (device int64) -> the block's output [1, d]."""
         att = self.attn(skinny_mm(x, self.w_qkv), self.q_norm, self.k_norm, cos, sin, pos, EPS)
         h = add_norm(skinny_mm(att, self.w_o), x, self.attn_norm, EPS)
         dn = skinny_mm(swiglu(skinny_mm(h, self.w_gu)), self.w_down)
@@ -70,29 +76,36 @@ class BolmoDecoder:
     def __init__(self, device: torch.device | str = "cuda", seed: int = 0, d: int = 2048, vocab: int = 512,
                  local_heads: int = 4, local_dh: int = 512, local_ffn: int = 2816, global_layers: int = 16,
                  global_heads: int = 16, global_ffn: int = 8192, max_patches: int = 1024,
-                 rope_theta: float = 500000.0, fused_glob: bool = True, fused_local: bool = False):
+                 rope_theta: float = 500000.0, fused_glob: bool = True, fused_local: bool = False,
+                 precision: str = "bf16"):
+        if precision not in ("bf16", "fp32"):
+            raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
+        act = torch.bfloat16 if precision == "bf16" else torch.float32
+        if act == torch.float32:  # the persistent kernels run bf16 activations only
+            fused_glob = fused_local = False
+        self.precision, self.act = precision, act
         device = torch.device(device)
         gen = torch.Generator(device=device).manual_seed(seed)
         self.device, self.d, self.vocab, self.max_patches = device, d, vocab, max_patches
         self.embed = _rnd(gen, device, vocab, d)
-        self.enc = LocalLayer(d, local_heads, local_dh, local_ffn, gen, device, smax=1)
+        self.enc = LocalLayer(d, local_heads, local_dh, local_ffn, gen, device, smax=1, act_dtype=act)
         self.enc_norm = _norm_w(gen, device, d)
         self.w_boundary = _rnd(gen, device, 1, d)
         self.w_patch = _rnd(gen, device, d, d)
-        self.blocks = [GlobalBlock(d, global_heads, global_ffn, max_patches, gen, device)
+        self.blocks = [GlobalBlock(d, global_heads, global_ffn, max_patches, gen, device, act_dtype=act)
                        for _ in range(global_layers)]
         self.dec_in_norm = _norm_w(gen, device, d)
         self.w_in = _rnd(gen, device, d, d)
-        self.dec = LocalLayer(d, local_heads, local_dh, local_ffn, gen, device, smax=1)
+        self.dec = LocalLayer(d, local_heads, local_dh, local_ffn, gen, device, smax=1, act_dtype=act)
         self.final_norm = _norm_w(gen, device, d)
         self.lm_head = _rnd(gen, device, vocab, d)
         self.cos, self.sin = rope_tables(max_patches, d // global_heads, rope_theta, device)
         # per-byte device buffers (graph inputs and outputs)
         self.byte = torch.zeros(1, dtype=torch.long, device=device)
         self.pos = torch.zeros(1, dtype=torch.long, device=device)  # the next patch position
-        self.e = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
-        self.patch = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
-        self.value = torch.zeros(1, d, dtype=torch.bfloat16, device=device)
+        self.e = torch.zeros(1, d, dtype=act, device=device)
+        self.patch = torch.zeros(1, d, dtype=act, device=device)
+        self.value = torch.zeros(1, d, dtype=act, device=device)
         self.boundary_logit = torch.zeros(1, 1, dtype=torch.float32, device=device)
         self.logits = torch.zeros(1, vocab, dtype=torch.float32, device=device)
         self.out = torch.zeros(2, dtype=torch.long, device=device)  # [token, boundary flag]
@@ -129,6 +142,8 @@ class BolmoDecoder:
                                 self.patch, self.boundary_logit)
             return
         h = self.embed.index_select(0, self.byte)
+        if self.act != h.dtype:
+            h = h.to(self.act)
         _, e = self.enc.step(h, rmsnorm(h, self.enc.norm1, EPS), parity, out_norm=self.enc_norm, want_sum=False)
         self.e.copy_(e)
         skinny_mm(e, self.w_patch, out=self.patch)

@@ -29,13 +29,16 @@ import torch
 
 from .. import _lib
 from . import draft_fused
-from .decode_ops import gate_softcap, norm_add, norm_gate, swiglu
+from .decode_ops import NORM_PLAIN, gate_softcap, norm_add, norm_gate, rmsnorm_ex, swiglu
 from .draft_core import mlstm_scan
 from .skinny import skinny_mm
 
 
 def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Row-wise RMSNorm of a bf16 [rows, cols] tensor (rows may be strided) on the sm_100a kernel."""
+    """Row-wise RMSNorm of a bf16 [rows, cols] tensor (rows may be strided) on the sm_100a kernel; an fp32 x
+    (the exactness mode) gives an fp32 result through the same kernel family."""
+    if x.dtype == torch.float32:
+        return rmsnorm_ex(x, w, eps, NORM_PLAIN, out=out)
     rows, cols = x.shape
     y = out if out is not None else torch.empty(rows, cols, dtype=torch.bfloat16, device=x.device)
     if x.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or y.dtype != torch.bfloat16:
@@ -60,11 +63,11 @@ class LocalLayer:
 
     def __init__(self, d: int, nh: int, dh: int, ffn: int, gen: torch.Generator, device: torch.device,
                  smax: int, std: float = 0.02, gate_cap: float = 15.0, norm_eps: float = 1e-6,
-                 mlstm_eps: float = 1e-6):
+                 mlstm_eps: float = 1e-6, act_dtype: torch.dtype = torch.bfloat16):
         def rnd(*shape, scale=std):
             return (torch.randn(*shape, generator=gen, device=device) * scale).to(torch.bfloat16)
 
-        self.d, self.nh, self.dh, self.ffn = d, nh, dh, ffn
+        self.d, self.nh, self.dh, self.ffn, self.act = d, nh, dh, ffn, act_dtype
         self.gate_cap, self.norm_eps, self.mlstm_eps = gate_cap, norm_eps, mlstm_eps
         self.norm1 = (1.0 + rnd(d)).to(torch.bfloat16)
         self.w_qkvo = rnd(4 * d, d)
@@ -80,7 +83,7 @@ class LocalLayer:
         self.nm = ((self.state[1], self.state[2]), (torch.zeros(1, nh, dh, **f32), torch.zeros(1, nh, 1, **f32)))
         self.nstart = torch.zeros(nh, dh, **f32)
         self.mstart = torch.zeros(nh, **f32)
-        self.hbuf = torch.zeros(smax, nh, dh, dtype=torch.bfloat16, device=device)
+        self.hbuf = torch.zeros(smax, nh, dh, dtype=act_dtype, device=device)
         self.saved: dict[int, tuple[torch.Tensor, ...]] = {}
 
     def reset(self) -> None:
@@ -101,7 +104,7 @@ class LocalLayer:
     def _tail(self, h: torch.Tensor, y: torch.Tensor, s: int, out_norm: torch.Tensor | None, want_sum: bool):
         d, eps = self.d, self.norm_eps
         z = norm_gate(self.hbuf[:s], y[:, 3 * d:], self.mh_norm, eps,
-                      out=torch.empty(s, d, dtype=torch.bfloat16, device=h.device))
+                      out=torch.empty(s, d, dtype=self.act, device=h.device))
         h2, x2 = norm_add(skinny_mm(z, self.w_out), h, self.norm2, eps)
         dn = skinny_mm(swiglu(skinny_mm(x2, self.w_gu)), self.w_down)
         if out_norm is None:

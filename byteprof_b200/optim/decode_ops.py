@@ -13,8 +13,9 @@ GEMMs (byteprof/optim/bolmo.py:32-136, bolmo_loop.py:36-64):
   * GlobStep                 the whole global-model step (all OLMo-2 blocks) as one persistent kernel
   * LocStep                  the local encoder or decoder step (one mLSTM layer and its heads) as one
                              persistent kernel
-Every bf16 intermediate is rounded where a bf16 torch tensor would hold it. CUDA tensors only; a
-missing library raises.
+Activations are bf16 or fp32 (one dtype per call; weights bf16). With bf16 every intermediate is rounded
+where a bf16 torch tensor would hold it; with fp32 (the decoder's exactness mode) nothing is rounded to
+bf16. CUDA tensors only; a missing library raises.
 """
 
 from __future__ import annotations
@@ -34,6 +35,16 @@ def _bf16(*ts: torch.Tensor) -> None:
             raise ValueError("bf16 tensors expected")
 
 
+def _act(dtype: torch.dtype, *ts: torch.Tensor) -> int:
+    """The C ABI code of the activation dtype (bf16 or fp32), which every given tensor must have."""
+    if dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"activations must be bf16 or fp32, got {dtype}")
+    for t in ts:
+        if t is not None and t.dtype != dtype:
+            raise ValueError(f"all activations of one call must be {dtype}")
+    return _lib.dtype_code(dtype)
+
+
 def _rows(t: torch.Tensor) -> tuple[int, int]:
     if t.dim() != 2 or t.stride(1) != 1:
         raise ValueError("2-D tensors with unit column stride expected")
@@ -42,35 +53,36 @@ def _rows(t: torch.Tensor) -> tuple[int, int]:
 
 def rmsnorm_ex(x: torch.Tensor, w: torch.Tensor, eps: float, mode: int = NORM_PLAIN, res: torch.Tensor | None = None,
                s_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """The general form on [rows, cols] bf16 tensors with one weight row (w [cols])."""
+    """The general form on [rows, cols] bf16 or fp32 tensors with one bf16 weight row (w [cols])."""
     rows, ldx = _rows(x)
     cols = x.shape[1]
-    y = out if out is not None else torch.empty(rows, cols, dtype=torch.bfloat16, device=x.device)
+    y = out if out is not None else torch.empty(rows, cols, dtype=x.dtype, device=x.device)
     ldres = 0
     if res is not None:
         if res.shape[-1] != cols:
             raise ValueError("res must have cols columns")
         ldres = 0 if res.dim() == 1 or res.shape[0] == 1 else _rows(res)[1]
     lds = _rows(s_out)[1] if s_out is not None else 0
-    _bf16(x, w, res, s_out, y)
+    _bf16(w)
+    code = _act(x.dtype, res, s_out, y)
     if w.numel() != cols:
         raise ValueError("w must hold cols values")
     _lib.require_cuda(x, w, res, s_out, y)
     with _lib.on_device(x):
         _lib.call("bp_rmsnorm_ex", x.data_ptr(), ldx, w.data_ptr(), 1, _lib.ptr(res), ldres, _lib.ptr(s_out), lds,
-                  y.data_ptr(), _rows(y)[1], rows, cols, eps, mode, _lib.stream_of(x))
+                  y.data_ptr(), _rows(y)[1], rows, cols, eps, mode, code, _lib.stream_of(x))
     return y
 
 
 def norm_add(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float,
              want_sum: bool = True) -> tuple[torch.Tensor | None, torch.Tensor]:
-    """(h, n) with h = bf16(x + res) and n = rmsnorm(h) * w; res may be one row (broadcast)."""
+    """(h, n) with h = x + res (rounded to x's dtype) and n = rmsnorm(h) * w; res may be one row (broadcast)."""
     s = torch.empty_like(x) if want_sum else None
     return s, rmsnorm_ex(x, w, eps, NORM_ADD_FIRST, res=res, s_out=s)
 
 
 def add_norm(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
-    """res + rmsnorm(x) * w (both roundings to bf16 as torch would do them)."""
+    """res + rmsnorm(x) * w (with bf16: both roundings to bf16 as torch would do them)."""
     return rmsnorm_ex(x, w, eps, NORM_ADD_AFTER, res=res)
 
 
@@ -83,23 +95,24 @@ def norm_gate(h: torch.Tensor, o: torch.Tensor, w: torch.Tensor, eps: float, out
         raise ValueError("h needs contiguous (NH, DH) rows and w must be a contiguous [NH, DH]")
     if o.stride(1) != 1 or out.stride(1) != 1 or o.shape[0] < s or out.shape[0] < s:
         raise ValueError("o and out need unit column strides and S rows")
-    _bf16(h, o, w, out)
+    _bf16(w)
+    code = _act(h.dtype, o, out)
     _lib.require_cuda(h, o, w, out)
     with _lib.on_device(h):
         _lib.call("bp_rmsnorm_ex", h.data_ptr(), h.stride(0), w.data_ptr(), nh, o.data_ptr(), o.stride(0), None, 0,
-                  out.data_ptr(), out.stride(0), s * nh, dh, eps, NORM_GATE, _lib.stream_of(h))
+                  out.data_ptr(), out.stride(0), s * nh, dh, eps, NORM_GATE, code, _lib.stream_of(h))
     return out
 
 
 def swiglu(gu: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
-    """gu [rows, 2 * ffn] bf16 (gate | up) -> bf16(bf16(silu(gate)) * up) [rows, ffn]."""
+    """gu [rows, 2 * ffn] (gate | up) -> silu(gate) * up [rows, ffn] (bf16: bf16(bf16(silu(gate)) * up))."""
     rows, ld = _rows(gu)
     ffn = gu.shape[1] // 2
-    y = out if out is not None else torch.empty(rows, ffn, dtype=torch.bfloat16, device=gu.device)
-    _bf16(gu, y)
+    y = out if out is not None else torch.empty(rows, ffn, dtype=gu.dtype, device=gu.device)
+    code = _act(gu.dtype, y)
     _lib.require_cuda(gu, y)
     with _lib.on_device(gu):
-        _lib.call("bp_swiglu", gu.data_ptr(), ld, y.data_ptr(), _rows(y)[1], rows, ffn, _lib.stream_of(gu))
+        _lib.call("bp_swiglu", gu.data_ptr(), ld, y.data_ptr(), _rows(y)[1], rows, ffn, code, _lib.stream_of(gu))
     return y
 
 
@@ -137,12 +150,14 @@ def rope_tables(max_pos: int, head_dim: int, theta: float, device: torch.device)
 
 
 class DecodeAttention:
-    """Static KV caches of one layer and its single-position attention."""
+    """Static KV caches of one layer and its single-position attention; activations and caches of `dtype`
+    (bf16, or fp32 for the exactness mode)."""
 
-    def __init__(self, nh: int, head_dim: int, max_pos: int, device: torch.device):
-        self.nh, self.hd, self.max_pos = nh, head_dim, max_pos
-        self.k_cache = torch.zeros(max_pos, nh, head_dim, dtype=torch.bfloat16, device=device)
-        self.v_cache = torch.zeros(max_pos, nh, head_dim, dtype=torch.bfloat16, device=device)
+    def __init__(self, nh: int, head_dim: int, max_pos: int, device: torch.device,
+                 dtype: torch.dtype = torch.bfloat16):
+        self.nh, self.hd, self.max_pos, self.dtype = nh, head_dim, max_pos, dtype
+        self.k_cache = torch.zeros(max_pos, nh, head_dim, dtype=dtype, device=device)
+        self.v_cache = torch.zeros(max_pos, nh, head_dim, dtype=dtype, device=device)
 
     def reset(self) -> None:
         self.k_cache.zero_()
@@ -151,17 +166,18 @@ class DecodeAttention:
     def __call__(self, qkv: torch.Tensor, q_norm: torch.Tensor, k_norm: torch.Tensor, cos: torch.Tensor,
                  sin: torch.Tensor, pos: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
         d = self.nh * self.hd
-        if qkv.dtype != torch.bfloat16 or qkv.numel() != 3 * d or not qkv.is_contiguous():
-            raise ValueError("qkv must be a contiguous bf16 [1, 3 * nh * head_dim]")
+        if qkv.dtype != self.dtype or qkv.numel() != 3 * d or not qkv.is_contiguous():
+            raise ValueError(f"qkv must be a contiguous {self.dtype} [1, 3 * nh * head_dim]")
         if pos.dtype != torch.int64 or cos.shape != (self.max_pos, self.hd // 2) or sin.shape != cos.shape:
             raise ValueError("int64 pos and cos / sin tables [max_pos, head_dim / 2] expected")
-        y = out if out is not None else torch.empty(1, d, dtype=torch.bfloat16, device=qkv.device)
-        _bf16(q_norm, k_norm, y)
+        y = out if out is not None else torch.empty(1, d, dtype=self.dtype, device=qkv.device)
+        _bf16(q_norm, k_norm)
+        code = _act(self.dtype, y)
         _lib.require_cuda(qkv, q_norm, k_norm, cos, sin, pos, y)
         with _lib.on_device(qkv):
             _lib.call("bp_decode_attention", qkv.data_ptr(), q_norm.data_ptr(), k_norm.data_ptr(), cos.data_ptr(),
                       sin.data_ptr(), pos.data_ptr(), self.k_cache.data_ptr(), self.v_cache.data_ptr(), y.data_ptr(),
-                      self.nh, self.hd, self.max_pos, eps, self.hd ** -0.5, _lib.stream_of(qkv))
+                      self.nh, self.hd, self.max_pos, eps, self.hd ** -0.5, code, _lib.stream_of(qkv))
         return y
 
 

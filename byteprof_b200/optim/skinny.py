@@ -8,8 +8,9 @@ weight preparation) and 209-217 (`dequantize`). Weight formats:
         w ~ scale[g, n] * (q - zero[g, n]), q in 0..15, groups of 128 along K; inside a group, byte j of
         a row holds code j in its low nibble and code j + 64 in its high nibble, and the R rows of one
         group are one contiguous block (the reference's tile-major format, R = 32 by default).
-fp32 accumulation; the output has the dtype of `out` (bf16 by default, fp32 gives the unrounded
-accumulator).
+fp32 accumulation; the output has the dtype of `out` (x's dtype by default; fp32 gives the unrounded
+accumulator). Activations are bf16 (the reference's kernel input) or, beyond the reference, fp32 with bf16 or
+int8 weights (the byte decoder's exactness mode; the CUDA-core kernel reads x as fp32).
 """
 
 from __future__ import annotations
@@ -41,8 +42,8 @@ def _kind(w: torch.Tensor) -> str:
 def skinny_mm(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = None,
               zero: torch.Tensor | None = None, out: torch.Tensor | None = None,
               cfg: tuple[int, ...] | None = None) -> torch.Tensor:
-    """x: [M, K] bf16 (contiguous); w: bf16 [N, K] | int8 [N, K] + scale [N] | int4 tile-major uint8 + scale,
-    zero [K/128, N]. `cfg` is accepted and ignored."""
+    """x: [M, K] bf16 (or fp32 with bf16 / int8 weights), contiguous; w: bf16 [N, K] | int8 [N, K] + scale [N] |
+    int4 tile-major uint8 + scale, zero [K/128, N]. `cfg` is accepted and ignored."""
     if x.dim() != 2 or not x.is_contiguous():
         raise ValueError("x must be a contiguous [M, K] tensor")
     m, k = x.shape
@@ -64,8 +65,8 @@ def skinny_mm(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = Non
         n = scale.shape[1]
         if zero.shape != scale.shape:
             raise ValueError("int4 zero must have the shape of scale [K/128, N]")
-    if x.dtype != torch.bfloat16:
-        raise ValueError(f"x must be bf16, got {x.dtype}")
+    if x.dtype != torch.bfloat16 and not (x.dtype == torch.float32 and kind != "int4"):
+        raise ValueError(f"x must be bf16 (or fp32 with bf16 / int8 weights), got {x.dtype}")
     y = out if out is not None else torch.empty(m, n, dtype=x.dtype, device=x.device)
     if y.shape != (m, n) or (m > 0 and n > 0 and y.stride(1) != 1):
         raise ValueError(f"out must be [M, N] = [{m}, {n}] with unit column stride")
@@ -90,6 +91,12 @@ def skinny_mm(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor | None = Non
     if scale is not None and kind == "int8" and scale.dtype != torch.bfloat16:
         scale = scale.to(torch.bfloat16)
     wcode = _lib.dtype_code(w.dtype)
+    if x.dtype == torch.float32:
+        with _lib.on_device(x):
+            _lib.call("bp_skinny_mm_xf32", x.data_ptr(), k, w.data_ptr(), wcode,
+                      _lib.ptr(scale if kind == "int8" else None), y.data_ptr(), y.stride(0), _lib.dtype_code(y.dtype),
+                      m, n, k, _lib.stream_of(x))
+        return y
     with _lib.on_device(x):
         ws, ws_bytes = _lib.skinny_workspace(x.device, m, n, k, wcode)
         _lib.call("bp_skinny_mm", x.data_ptr(), k, w.data_ptr(), wcode, _lib.ptr(scale if kind == "int8" else None),

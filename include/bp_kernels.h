@@ -108,6 +108,16 @@ int bp_skinny_mm_static_scratch(const void* x, long long ldx, const void* w, int
                                 void* y, long long ldy, int y_dtype, int M, int N, int K, void* stream);
 
 /*
+ * Skinny linear with fp32 activations: bp_skinny_mm's arithmetic (the CUDA-core kernel: the K partition
+ * depends on N and K only, fp32 accumulation) with x read as fp32 [M, K] (16-byte aligned and ldx a
+ * multiple of 4 for the vector path). Weights bf16 or int8 + bf16 scale, y bf16 or fp32, no workspace.
+ * No counterpart in the reference, whose fp32 activations go to F.linear on dequantized fp32 weights
+ * (byteprof/optim/skinny_linear.py:67-68): it serves the byte decoder's fp32-activation exactness mode.
+ */
+int bp_skinny_mm_xf32(const float* x, long long ldx, const void* w, int w_dtype, const void* w_scale, void* y,
+                      long long ldy, int y_dtype, int M, int N, int K, void* stream);
+
+/*
  * int8 weight-only GEMV for one activation row: y[1, N] = scale[n] * sum_k x[k] * q[n, k].
  * bp_skinny_mm with M = 1 and int8 weights, including its workspace rule, except that with N <= 4096 it
  * always takes the CUDA-core kernel (one launch; faster than the tensor-core kernel's two at that size)
@@ -149,8 +159,10 @@ int bp_rmsnorm(const void* x, long long ldx, const void* w, void* y, long long l
                void* stream);
 
 /*
- * RMSNorm fused with the step around it; bf16 in and out, fp32 arithmetic, one warp per row with
- * bp_rmsnorm's summation order. n(v) = bf16(v * rsqrt(mean(v^2) + eps) * w):
+ * RMSNorm fused with the step around it, one warp per row with bp_rmsnorm's summation order. x, res,
+ * s_out and y hold `dtype` values (BP_DTYPE_BF16 or BP_DTYPE_F32), w is bf16, arithmetic fp32. With bf16
+ * every step rounds where a bf16 tensor would hold the value (as written below); with fp32 nothing is
+ * rounded to bf16. n(v) = bf16(v * rsqrt(mean(v^2) + eps) * w):
  *   BP_NORM_PLAIN      y = n(x)
  *   BP_NORM_ADD_FIRST  s = bf16(x + res); y = n(s)     (s_out receives s when not NULL)
  *   BP_NORM_ADD_AFTER  y = bf16(res + n(x))
@@ -164,14 +176,15 @@ int bp_rmsnorm(const void* x, long long ldx, const void* w, void* y, long long l
 enum { BP_NORM_PLAIN = 0, BP_NORM_ADD_FIRST = 1, BP_NORM_ADD_AFTER = 2, BP_NORM_GATE = 3 };
 int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_rows, const void* res, long long ldres,
                   void* s_out, long long lds, void* y, long long ldy, int rows, int cols, float eps, int mode,
-                  void* stream);
+                  int dtype, void* stream);
 
 /*
  * SwiGLU: out[r, j] = bf16(bf16(silu(gu[r, j])) * gu[r, ffn + j]) for j < ffn (gate | up halves of one
- * GEMM output, bf16). ffn and strides multiples of 8, 16-byte aligned. Replaces act_fn(gate) * up of
- * the MLPs in the Bolmo layers (byteprof/optim/bolmo.py:32-44).
+ * GEMM output) with dtype BP_DTYPE_BF16; with BP_DTYPE_F32 gu and out are fp32 and nothing is rounded to
+ * bf16. ffn and strides multiples of 8, 16-byte aligned. Replaces act_fn(gate) * up of the MLPs in the
+ * Bolmo layers (byteprof/optim/bolmo.py:32-44).
  */
-int bp_swiglu(const void* gu, long long ldgu, void* out, long long ldo, int rows, int ffn, void* stream);
+int bp_swiglu(const void* gu, long long ldgu, void* out, long long ldo, int rows, int ffn, int dtype, void* stream);
 
 /*
  * mLSTM gate pre-activations: out[r, c] = cap * tanh((g[r, c] + bias[c]) / cap), fp32 (bias may be
@@ -189,12 +202,13 @@ int bp_gate_softcap(const float* g, long long ldg, const float* bias, float* out
  *   out [nh * head_dim] bf16 = softmax(q . k_j * scale) over j <= p, times v_j.
  * Work per head is one thread-block cluster of 8 CTAs (128 positions each per 1024-position round),
  * merged in the leader CTA in a fixed order (deterministic). head_dim 128. A position outside
- * [0, max_pos) writes NaN and touches no cache row.
+ * [0, max_pos) writes NaN and touches no cache row. dtype BP_DTYPE_BF16 as above; BP_DTYPE_F32: qkv,
+ * the caches and out hold fp32 values and nothing is rounded to bf16.
  * Replaces GlobalStep.step's attention over the StaticCache (byteprof/optim/bolmo.py:100-136).
  */
 int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_norm_w, const float* cos_t,
                         const float* sin_t, const int64_t* pos, void* k_cache, void* v_cache, void* out, int nh,
-                        int head_dim, int max_pos, float eps, float scale, void* stream);
+                        int head_dim, int max_pos, float eps, float scale, int dtype, void* stream);
 
 /*
  * One global-model step of a Bolmo-1B-shaped byte decoder in a single persistent (cooperative) kernel:

@@ -13,7 +13,7 @@ whole model is checked statistically: the logits of every step strongly correlat
 their deviation a small fraction of their RMS, and the greedy byte and boundary decision agreeing at
 most steps, every disagreement at a small top-2 gap. The first divergence of the free-running greedy
 sequences is reported. CUDA-graph decoding gives exactly the bits of eager decoding, and decoding is
-deterministic."""
+deterministic. The exactness mode (fp32 activations) is checked byte for byte in tests/test_bolmo_exact_gpu.py."""
 
 import numpy as np
 import pytest
@@ -24,10 +24,12 @@ from helpers import to_np
 from oracle import bolmo_ref
 
 pytestmark = pytest.mark.gpu
-MIN_CORR = 0.9        # per-step correlation of the logits with the oracle's
-MAX_MEDIAN_DEV = 0.1  # median over steps of max |logit - oracle| / RMS(oracle logits)
-MIN_TOKEN_AGREE = 0.75
-MIN_BOUNDARY_AGREE = 0.9
+# Bars set just under what this build measures (correlation >= 0.975, median deviation 0.06, 96-97 % of the
+# greedy bytes, every boundary decision), so that losing a layer's contribution or a rounding point fails.
+MIN_CORR = 0.97       # per-step correlation of the logits with the oracle's
+MAX_MEDIAN_DEV = 0.08  # median over steps of max |logit - oracle| / RMS(oracle logits)
+MIN_TOKEN_AGREE = 0.93
+MIN_BOUNDARY_AGREE = 0.98
 
 
 @pytest.fixture(scope="module")
@@ -64,7 +66,7 @@ def _teacher_forced(model, ref, prompt, n_new):
     return fed, rows
 
 
-def _check(rows):
+def _check(rows, min_agree=MIN_TOKEN_AGREE):
     """Statistics of a teacher-forced run; asserts the bars and returns them."""
     devs, corrs, tok_ok, bnd_ok, gaps, first = [], [], 0, 0, [], None
     for t, (tok, bnd, lg, rl, rb, rbl, opened) in enumerate(rows):
@@ -84,7 +86,7 @@ def _check(rows):
     print(stats)
     assert stats["min_corr"] >= MIN_CORR, stats
     assert stats["median_dev"] <= MAX_MEDIAN_DEV, stats
-    assert stats["token_agree"] >= MIN_TOKEN_AGREE and stats["boundary_agree"] >= MIN_BOUNDARY_AGREE, stats
+    assert stats["token_agree"] >= min_agree and stats["boundary_agree"] >= MIN_BOUNDARY_AGREE, stats
     assert not gaps or max(gaps) <= 2 * stats["max_dev"], stats  # disagreements only at near-ties
     return stats
 
@@ -108,7 +110,7 @@ def test_graphs_give_the_bits_of_eager_decoding(model):
 
 def test_short_decode_tracks_the_oracle(model, ref):
     fed, rows = _teacher_forced(model, ref, _prompt(32, 2), 32)
-    stats = _check(rows)
+    stats = _check(rows, min_agree=0.85)  # 63 steps: a few near-ties weigh more
     assert 0 < stats["patches"] <= len(rows)
 
 

@@ -1,0 +1,96 @@
+"""End-to-end parity of the byte decoder's exactness mode (BolmoDecoder(precision="fp32")) against the float64
+oracle of the same model (oracle/bolmo_exact.py): identical greedy bytes and patch decisions.
+
+The bf16 mode cannot be checked that way: with random weights the model amplifies single bf16 rounding
+steps (tests/test_bolmo_e2e_gpu.py bounds it statistically). With fp32 activations every rounding is
+2^16 times finer, the logits follow exact arithmetic to about 1e-5 of their spread, and the greedy bytes
+of the benchmark configuration (256-byte prompt, 512 generated) must be exactly those of the float64
+oracle, as the north star of this path asks ("an identical greedy byte sequence end to end"). The margin
+is reported: the smallest top-2 logit gap of the oracle's run against the largest deviation of the GPU's
+logits seen in the teacher-forced check."""
+
+import numpy as np
+import pytest
+import torch
+
+from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+from helpers import to_np
+from oracle import bolmo_exact
+
+pytestmark = pytest.mark.gpu
+MAX_DEV = 1e-4  # max |logit - oracle| / RMS(oracle logits) over the teacher-forced steps
+
+
+@pytest.fixture(scope="module")
+def model():
+    m = BolmoDecoder(seed=11, precision="fp32")
+    m.capture()
+    return m
+
+
+@pytest.fixture(scope="module")
+def oracle(model):
+    return bolmo_exact.BolmoExact({k: to_np(v) for k, v in model.weights().items()})
+
+
+def _prompt(n, seed):
+    return np.random.default_rng(seed).integers(0, 256, size=n).tolist()
+
+
+def first_divergence(a, b):
+    for i, (x, y) in enumerate(zip(a, b)):
+        if x != y:
+            return i
+    return None if len(a) == len(b) else min(len(a), len(b))
+
+
+def test_fp32_logits_follow_the_float64_model(model, oracle):
+    """Teacher forced on the GPU's own bytes: every step's logits within MAX_DEV of the oracle's spread, the
+    same greedy byte and the same boundary decision at every step."""
+    model.reset()
+    oracle.reset()
+    prompt = _prompt(48, 2)
+    new_patch, devs, fed = True, [], list(prompt)
+    for i in range(len(prompt) + 48):
+        b = fed[i]
+        tok, bnd = model.feed(b, new_patch)
+        lg = to_np(model.logits)[0].astype(np.float64)
+        rl, rb, _ = oracle.feed(b, new_patch)
+        devs.append(float(np.abs(lg - rl).max() / np.sqrt(np.mean(rl ** 2))))
+        assert tok == int(np.argmax(rl)) and bnd == rb, (i, tok, int(np.argmax(rl)), bnd, rb)
+        if i + 1 >= len(prompt):
+            fed.append(tok)
+        new_patch = bnd
+    print({"steps": len(devs), "max_dev": max(devs), "median_dev": float(np.median(devs))})
+    assert max(devs) <= MAX_DEV, max(devs)
+
+
+def test_benchmark_configuration_greedy_bytes_are_identical(model, oracle):
+    """The benchmark's decode (prompt of 256 uniform-random bytes, 512 generated), free running on both
+    sides: the same 512 bytes and the same patch starts."""
+    prompt = _prompt(256, 3)
+    model.reset()
+    gen, opened = model.generate(prompt, 512)
+    oracle.reset()
+    ref, ref_opened, gaps = bolmo_exact.greedy(oracle, prompt, 512)
+    first = first_divergence(gen, ref)
+    rms_gap = float(np.min(gaps))
+    print({"first_divergence": first, "min_top2_gap": rms_gap, "median_top2_gap": float(np.median(gaps)),
+           "patches": sum(opened)})
+    assert first is None, (first, gen[first] if first is not None else None, ref[first] if first is not None else None)
+    assert gen == ref and opened == ref_opened
+
+
+def test_fp32_mode_runs_the_graphs_bit_for_bit_like_eager(model):
+    prompt = _prompt(12, 1)
+    model.reset()
+    tg, og = model.generate(prompt, 16)
+    lg = model.logits.clone()
+    graphs, model.graphs = model.graphs, {}
+    try:
+        model.reset()
+        te, oe = model.generate(prompt, 16)
+        assert (tg, og) == (te, oe)
+        assert torch.equal(lg, model.logits)
+    finally:
+        model.graphs = graphs

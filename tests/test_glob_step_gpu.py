@@ -12,7 +12,9 @@ import torch
 
 from byteprof_b200.optim.bolmo_e2e import EPS, BolmoDecoder
 from byteprof_b200.optim.bolmo_local import rmsnorm
+from byteprof_b200.optim.decode_ops import GlobStep
 from helpers import to_np
+from oracle import bolmo_ref
 
 pytestmark = pytest.mark.gpu
 
@@ -102,3 +104,37 @@ def test_a_position_outside_the_cache_writes_nan_and_nothing_else():
     m.glob_kernel(m.patch, m.value, m.pos)
     assert torch.isnan(m.value.float()).all() and int(m.pos) == m.max_patches
     assert torch.equal(m.blocks[0].attn.k_cache, caches[0][0]) and torch.equal(m.blocks[0].attn.v_cache, caches[0][1])
+
+
+def test_each_block_of_the_persistent_kernel_against_the_oracle():
+    """Block by block on the default (persistent) path: block i alone in the kernel, fed the oracle's input of
+    block i, against the oracle's output of that block (both through the final RMSNorm the kernel applies),
+    with the same caches holding 300 earlier positions. Every block within one bf16 step normwise and most
+    outputs bit-equal: a per-block check that the statistical bar of the whole model cannot give."""
+    pos = 300
+    m, caches = _setup(16, pos, seed=9)
+    w = {k: to_np(v) for k, v in m.weights().items()}
+    ref = bolmo_ref.BolmoRef(w)
+    for i, b in enumerate(m.blocks):
+        ref.attn[i].k[:] = to_np(b.attn.k_cache)
+        ref.attn[i].v[:] = to_np(b.attn.v_cache)
+    ref.pos = pos
+    x = to_np(m.patch)
+    errs = []
+    for i, b in enumerate(m.blocks):
+        one = GlobStep([b], m.dec_in_norm, m.cos, m.sin, m.max_patches, EPS)
+        xin = torch.from_numpy(x).to(device="cuda", dtype=torch.bfloat16)
+        assert np.array_equal(to_np(xin), x)  # the oracle's bf16 activations go in exactly
+        m.pos.fill_(pos)
+        one(xin, m.value, m.pos)
+        g = f"glob{i}."
+        att = ref.attn[i](bolmo_ref.linear(x, w[g + "w_qkv"]), w[g + "q_norm"], w[g + "k_norm"], ref.cos, ref.sin, pos,
+                          EPS)
+        h = bolmo_ref.add_norm(bolmo_ref.linear(att, w[g + "w_o"]), x, w[g + "attn_norm"], EPS)
+        dn = bolmo_ref.linear(bolmo_ref.swiglu(bolmo_ref.linear(h, w[g + "w_gu"])), w[g + "w_down"])
+        x = bolmo_ref.add_norm(dn, h, w[g + "mlp_norm"], EPS)
+        want = bolmo_ref.rmsnorm(x, w["dec_in_norm"], EPS)
+        err, exact = _compare(m.value, torch.from_numpy(want))
+        errs.append((i, round(err, 5), round(exact, 3)))
+        assert err <= 2.0**-6 and exact >= 0.75, errs
+    print(errs)
