@@ -530,6 +530,41 @@ def _time_decode(m, seed: int, reps: int, replay: list | None = None) -> dict:
             "device_us": per, "tokens": gen, "fed": fed}
 
 
+def _divergence_from_exact(m, ours: dict, seed: int, device: torch.device) -> dict:
+    """The timed bf16 decode against the same model in the exactness mode (fp32 activations, whose greedy bytes
+    are those of float64 arithmetic on the same weights, tests/test_bolmo_exact_gpu.py), as the reference
+    reports its bf16 runs against its exact ones (byteprof FINDINGS.md section 5, byteprof/counting.py:56-65):
+    the exact model is fed the bytes and patch decisions the bf16 run fed, and at every generated step its
+    greedy choice is compared with the bf16 run's. Reports the first generated step where they differ, the
+    exact model's top-2 logit gap there and the median gap over the earlier steps."""
+    from byteprof_b200.optim.bolmo_e2e import BolmoDecoder
+
+    ex = BolmoDecoder(device=device, seed=seed, precision="fp32")
+    ex.capture()
+    ex.reset()
+    fed, gen = ours["fed"], ours["tokens"]
+    gaps, first, first_gap, agree = [], None, None, 0
+    for i, (b, new_patch) in enumerate(fed):
+        tok, _ = ex.feed(b, new_patch)
+        j = i - (DECODE_PROMPT - 1)  # the step that chose generated byte j
+        if j < 0:
+            continue
+        top = torch.topk(ex.logits[0], 2).values
+        gap = float(top[0] - top[1])
+        if tok == gen[j]:
+            agree += 1
+        elif first is None:
+            first, first_gap = j, gap
+        if first is None:
+            gaps.append(gap)
+    del ex
+    torch.cuda.empty_cache()
+    return {"against": "the same model in the exactness mode (fp32 activations), teacher forced on the bf16 run's bytes",
+            "greedy_agreement": f"{agree}/{len(gen)}", "first_divergence": first,
+            "top2_gap_at_first_divergence": None if first_gap is None else round(first_gap, 5),
+            "median_top2_gap_before": round(float(statistics.median(gaps)), 5) if gaps else None}
+
+
 def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 20) -> dict:
     """greedy decoding of the random-init Bolmo-1B-shaped byte model, batch 1, on this
     repository's kernels, and the same model and loop on stock PyTorch ops (TorchDecoder) beside it."""
@@ -553,6 +588,10 @@ def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 2
         "frac": round(streamed / ours["wall"] / 1e9 / peak, 4),
         "graphs_per_byte": "enc + dec, + glob on a patch start; one host sync per byte",
     }
+    try:
+        out["exactness"] = _divergence_from_exact(m, ours, seed, device)
+    except Exception as exc:  # noqa: BLE001 - a failed comparison must not hide our own number
+        out["exactness"] = {"error": f"{type(exc).__name__}: {exc}"[:300]}
     try:
         t = TorchDecoder(m)
         t.capture()

@@ -18,7 +18,7 @@ from helpers import to_np
 from oracle import bolmo_exact
 
 pytestmark = pytest.mark.gpu
-MAX_DEV = 1e-4  # max |logit - oracle| / RMS(oracle logits) over the teacher-forced steps
+MAX_DEV = 5e-5  # max |logit - oracle| / RMS(oracle logits) over the teacher-forced steps (measured 8.3e-6)
 
 
 @pytest.fixture(scope="module")
@@ -74,8 +74,7 @@ def test_benchmark_configuration_greedy_bytes_are_identical(model, oracle):
     oracle.reset()
     ref, ref_opened, gaps = bolmo_exact.greedy(oracle, prompt, 512)
     first = first_divergence(gen, ref)
-    rms_gap = float(np.min(gaps))
-    print({"first_divergence": first, "min_top2_gap": rms_gap, "median_top2_gap": float(np.median(gaps)),
+    print({"first_divergence": first, "min_top2_gap": float(np.min(gaps)), "median_top2_gap": float(np.median(gaps)),
            "patches": sum(opened)})
     assert first is None, (first, gen[first] if first is not None else None, ref[first] if first is not None else None)
     assert gen == ref and opened == ref_opened
