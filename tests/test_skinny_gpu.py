@@ -39,6 +39,22 @@ def test_matches_oracle_for_every_m(kind, n, k):
     assert worst < TOL, worst
 
 
+@pytest.mark.parametrize("n,k", [(12288, 2048), (20480, 4096), (100352, 2048), (256, 16384), (1024, 64), (300, 5056)])
+def test_activation_window_shapes(n, k):
+    """The bf16 kernel's activation window: stream-K CTAs whose units wrap from the last k-block to the first
+    (12288 x 2048, 20480 x 4096), CTAs covering whole tiles (the LM head), large cluster windows (256 x 16384),
+    one k-block (K = 64) and an odd tile count; M on both sides of 8 (8-row window blocks up to M = 8). Rows
+    must also be bit-identical whatever M is."""
+    _, args = make_weights("bf16", n, k, seed=3)
+    wd = deq_np("bf16", args)
+    x = x_rows(16, k, seed=4)
+    full = S.skinny_mm(x, *args)
+    assert skinny_ref.nerr(to_np(full), to_np(x), wd) < TOL
+    for m in (1, 5, 8, 9, 12):
+        y = S.skinny_mm(x[:m].contiguous(), *args)
+        assert torch.equal(y, full[:m]), m
+
+
 @pytest.mark.parametrize("kind", ["bf16", "int8"])
 @pytest.mark.parametrize("n,k", [(37, 1000), (3, 129), (16, 2047), (7, 5000), (1025, 2049)])
 def test_unaligned_k_takes_the_elementwise_path(kind, n, k):
