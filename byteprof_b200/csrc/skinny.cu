@@ -336,10 +336,27 @@ int dispatch_m_f32(const SkinnyArgs& a, int m, bool vec, cudaStream_t st) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// BP_SKINNY_PATH=fma forces the CUDA-core kernel for bf16 too (read at every call; for comparisons).
-bool tc_path_enabled() {
+// BP_SKINNY_PATH (read at every call; for comparisons): "fma" forces the CUDA-core kernels for bf16 and int8,
+// "tc" keeps int8 on the tensor cores at every M, "exact" takes the exact int8 CUDA-core kernel wherever it
+// applies.
+char path_override() {
   const char* e = getenv("BP_SKINNY_PATH");
-  return !(e != nullptr && e[0] == 'f');
+  return e == nullptr ? 0 : e[0];
+}
+bool tc_path_enabled() { return path_override() != 'f'; }
+
+// int8 weights go to the exact CUDA-core kernel for one activation row and at most this many output rows
+// (only where both exact kernels take the shape, so the choice never changes a bit of the result). Measured,
+// graph of a cold weight ring: 2048 x 2048 5.9 us against 6.5 on the tensor cores (two launches: digit prep
+// and the main kernel), 2048 x 8192 8.8 against 11.2; the tensor cores win from 8192 rows (8192 x 2048 8.2
+// against 12.9) and at M = 4 (2048 x 2048 6.8 against 13.5: dp4a work grows with every row).
+constexpr int kI8xMaxN = 4096;
+
+bool use_i8x(const void* x, long long ldx, const void* w, int m, int N, int K) {
+  const char o = path_override();
+  if (o == 't' || o == 'f') return false;
+  if (!skinny_i8x_supported(x, ldx, w, m, N, K) || !skinny_tc_supported(x, ldx, w, m, N, K, true)) return false;
+  return o == 'e' || (m == 1 && N <= kI8xMaxN);
 }
 
 }  // namespace
@@ -365,11 +382,12 @@ extern "C" int bp_device_errors(unsigned int* flags) {
 namespace bp {
 namespace {
 
-// The body of bp_skinny_mm. `cuda_cores` keeps every row chunk on the CUDA-core kernel (bp_gemv_int8's
-// rule below); otherwise the tensor-core kernel takes every shape it supports.
+// The body of bp_skinny_mm: per chunk of up to 16 rows, int8 weights at M <= 4 go to the exact CUDA-core
+// kernel (use_i8x), otherwise the tensor-core kernel takes every shape it supports, and the CUDA-core
+// streaming kernel the rest.
 int skinny_entry(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale, void* y,
                  long long ldy, int y_dtype, int M, int N, int K, void* workspace, size_t workspace_bytes,
-                 void* stream, bool cuda_cores) {
+                 void* stream) {
   clear_error();
   if (M < 0 || N < 0 || K < 0) return fail(BP_ERR_INVALID_ARGUMENT, "negative size (M=%d N=%d K=%d)", M, N, K);
   if (w_dtype != BP_DTYPE_BF16 && w_dtype != BP_DTYPE_INT8)
@@ -409,7 +427,9 @@ int skinny_entry(const void* x, long long ldx, const void* w, int w_dtype, const
     const int m = M - r0 < 16 ? M - r0 : 16;
     a.x = static_cast<const __nv_bfloat16*>(x) + static_cast<long long>(r0) * ldx;
     a.y = static_cast<char*>(y) + static_cast<long long>(r0) * ldy * static_cast<long long>(ysz);
-    if (!cuda_cores && tc_path_enabled() && skinny_tc_supported(a.x, ldx, w, m, N, K, is8))
+    if (is8 && use_i8x(a.x, ldx, w, m, N, K))
+      st = launch_skinny_i8x(a.x, ldx, w, w_scale, a.y, ldy, a.y_f32, m, N, K, s);
+    else if (tc_path_enabled() && skinny_tc_supported(a.x, ldx, w, m, N, K, is8))
       st = launch_skinny_tc(a.x, ldx, w, w_scale, a.y, ldy, a.y_f32, m, N, K, is8, workspace, workspace_bytes, s);
     else
       st = is8 ? dispatch_m<int8_t>(a, m, vec, s) : dispatch_m<__nv_bfloat16>(a, m, vec, s);
@@ -424,21 +444,14 @@ int skinny_entry(const void* x, long long ldx, const void* w, int w_dtype, const
 extern "C" int bp_skinny_mm(const void* x, long long ldx, const void* w, int w_dtype, const void* w_scale, void* y,
                             long long ldy, int y_dtype, int M, int N, int K, void* workspace, size_t workspace_bytes,
                             void* stream) {
-  return bp::skinny_entry(x, ldx, w, w_dtype, w_scale, y, ldy, y_dtype, M, N, K, workspace, workspace_bytes, stream,
-                          false);
+  return bp::skinny_entry(x, ldx, w, w_dtype, w_scale, y, ldy, y_dtype, M, N, K, workspace, workspace_bytes, stream);
 }
 
-// One activation row only, so the kernel may depend on the shape and M = 1 together: with N <= 4096 output
-// rows the tensor-core kernel has at most 32 weight tiles and two launches (digit prep + main) of fixed
-// latency, and the CUDA-core kernel's single launch is faster (measured, cold L2: 2048 x 2048 4.4 us
-// against 6.6, 2048 x 8192 7.9 against 11.0); from 8192 rows the tensor-core kernel is (8192 x 2048 8.2
-// against 9.6 us).
-constexpr int kGemvCudaCoreMaxN = 4096;
-
+// The int8 GEMV is bp_skinny_mm at M = 1: aligned shapes take one of the two exact kernels (the same bits
+// either way), others the CUDA-core kernel.
 extern "C" int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,
                             void* workspace, size_t workspace_bytes, void* stream) {
-  return bp::skinny_entry(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, workspace, workspace_bytes, stream,
-                          N <= kGemvCudaCoreMaxN);
+  return bp::skinny_entry(x, K, w, BP_DTYPE_INT8, w_scale, y, N, y_dtype, 1, N, K, workspace, workspace_bytes, stream);
 }
 
 // Skinny linear with fp32 activations on the CUDA-core kernel (the decoder's exactness mode): the same

@@ -32,6 +32,15 @@ bool skinny_i8_supported(const void* x, long long ldx, const void* w, int M, int
 int launch_skinny_i8(const void* x, long long ldx, const void* w, const void* w_scale, void* y, long long ldy, int y_f32,
                      int M, int N, int K, void* ws, size_t ws_bytes, cudaStream_t stream);
 
+// Exact int8 weights on the CUDA cores for 1..4 activation rows (skinny_i8x.cu): bit-identical to the int8
+// tensor-core kernel (the same fixed-point digits and exact integer sums), one launch, no workspace. Needs
+// 16-byte aligned x and w, ldx a multiple of 8, K a multiple of 16 up to 131072, and at most
+// kI8xMaxDigitBytes of digit planes per CTA.
+constexpr size_t kI8xMaxDigitBytes = 64 * 1024;
+bool skinny_i8x_supported(const void* x, long long ldx, const void* w, int M, int N, int K);
+int launch_skinny_i8x(const void* x, long long ldx, const void* w, const void* w_scale, void* y, long long ldy, int y_f32,
+                      int M, int N, int K, cudaStream_t stream);
+
 // int4 group-128 weights on the tensor cores (skinny_i4tc.cu): workspace bytes for an N x K weight, whether
 // the problem fits (16-byte aligned x, w, scale, zero; ldx a multiple of 8; N a multiple of 8; K a
 // multiple of 128 up to 131072; 1 <= M <= 16), and the launch (prep kernel + main kernel).

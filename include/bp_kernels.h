@@ -66,9 +66,11 @@ const char* bp_last_error(void);
  *   x      bf16, row stride ldx elements (ldx >= K); rows beyond M are never read
  *   w      w_dtype = BP_DTYPE_BF16: bf16 [N, K] contiguous
  *          w_dtype = BP_DTYPE_INT8: int8 [N, K] contiguous, w_scale = bf16 [N]; y = scale[n] * sum_k x*q.
- *          The int8 tensor-core path sums exactly over x written in fixed point (29 bits below each
- *          row's largest exponent: every x within 2^-22 of the row maximum is exact) and rounds
- *          scale * sum once; a row of x holding Inf or NaN gives a NaN row of y
+ *          Aligned int8 problems (x and w 16-byte aligned, ldx a multiple of 8, K a multiple of 16) sum
+ *          exactly over x written in fixed point (29 bits below each row's largest exponent: every x within
+ *          2^-22 of the row maximum is exact) and round scale * sum once, on the tensor cores or, for up to
+ *          1 row and at most 4096 output rows, on the CUDA cores in one launch: the two give the same
+ *          bits, so a row's result never depends on M. A row of x holding Inf or NaN gives a NaN row of y
  *   y      y_dtype BP_DTYPE_BF16 or BP_DTYPE_F32 (the fp32 store is the un-rounded accumulator), row
  *          stride ldy elements; exactly the M x N block is written
  *   workspace, workspace_bytes  caller-owned device scratch of at least
@@ -119,8 +121,7 @@ int bp_skinny_mm_xf32(const float* x, long long ldx, const void* w, int w_dtype,
 
 /*
  * int8 weight-only GEMV for one activation row: y[1, N] = scale[n] * sum_k x[k] * q[n, k].
- * bp_skinny_mm with M = 1 and int8 weights, including its workspace rule, except that with N <= 4096 it
- * always takes the CUDA-core kernel (one launch; faster than the tensor-core kernel's two at that size)
+ * bp_skinny_mm with M = 1 and int8 weights, including its workspace rule and its results, bit for bit
  * (byteprof/quant/triton_int8.py:15-47).
  */
 int bp_gemv_int8(const void* x, const int8_t* w, const void* w_scale, void* y, int y_dtype, int N, int K,

@@ -34,12 +34,10 @@ def test_gemv_real_shapes_batch_one(n, k):
     _close(gemv_int8(x, q, s), _ref(x, q, s))
 
 
-@pytest.mark.parametrize("n,k,cuda_cores", [(2048, 2048, True), (4096, 2048, True), (2048, 8192, True),
-                                            (4104, 2048, False), (8192, 2048, False)])
-def test_gemv_kernel_choice_by_output_rows(n, k, cuda_cores, monkeypatch):
-    """gemv_int8 takes the CUDA-core kernel up to 4096 output rows and the tensor-core kernel above: its
-    output is bit-identical to skinny_mm at M = 1 forced onto that kernel (BP_SKINNY_PATH=fma) or left on
-    its default (the tensor-core kernel for these aligned shapes)."""
+@pytest.mark.parametrize("n,k", [(2048, 2048), (4096, 2048), (2048, 8192), (4104, 2048), (8192, 2048)])
+def test_gemv_is_skinny_mm_at_one_row_bit_for_bit(n, k, monkeypatch):
+    """gemv_int8 is skinny_mm at M = 1: bit-identical to it on its default route and with the tensor-core
+    kernel forced (BP_SKINNY_PATH=tc), since both int8 kernels it can take sum exactly."""
     from byteprof_b200.optim.skinny import skinny_mm
 
     g = torch.Generator().manual_seed(n + k)
@@ -47,8 +45,8 @@ def test_gemv_kernel_choice_by_output_rows(n, k, cuda_cores, monkeypatch):
     x = torch.randn(1, k, generator=g).to("cuda", torch.bfloat16)
     y = gemv_int8(x, q, s)
     _close(y, _ref(x, q, s))
-    if cuda_cores:
-        monkeypatch.setenv("BP_SKINNY_PATH", "fma")
+    assert torch.equal(y, skinny_mm(x, q, s))
+    monkeypatch.setenv("BP_SKINNY_PATH", "tc")
     want = skinny_mm(x, q, s)
     monkeypatch.delenv("BP_SKINNY_PATH", raising=False)
     assert torch.equal(y, want)

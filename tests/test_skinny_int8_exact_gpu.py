@@ -118,3 +118,50 @@ def test_int8_stream_k_leaves_the_workspace_clean_and_repeats_bitwise():
     torch.cuda.synchronize()
     ws = _lib._workspaces[torch.cuda.current_device()]
     assert int(ws[:4 * 8192].view(torch.int32).abs().sum()) == 0
+
+
+def _with_path(path, fn):
+    import os
+
+    old = os.environ.get("BP_SKINNY_PATH")
+    os.environ["BP_SKINNY_PATH"] = path
+    try:
+        out = fn()
+        torch.cuda.synchronize()
+        return out
+    finally:
+        if old is None:
+            del os.environ["BP_SKINNY_PATH"]
+        else:
+            os.environ["BP_SKINNY_PATH"] = old
+
+
+@pytest.mark.parametrize("n,k", [(2048, 2048), (8192, 2048), (2048, 8192), (100352, 2048), (300, 2064), (50, 144),
+                                 (1000, 16), (37, 65536)])
+@pytest.mark.parametrize("m", [1, 2, 3, 4])
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16])
+def test_cuda_core_exact_kernel_gives_the_tensor_core_bits(n, k, m, out_dtype):
+    """The exact CUDA-core int8 kernel (M <= 4) and the tensor-core kernel form the same integer sums from
+    the same fixed-point digits and round once the same way: their outputs are bit-identical, so routing
+    between them by M never changes a row's result."""
+    _, (q, s) = make_weights("int8", n, k, seed=n + k)
+    x = x_rows(m, k, seed=m, scale=3.0)
+    x[0, 5] = 1e-30  # tiny values far below the row maximum round in the fixed point, the same in both
+    run = lambda: S.skinny_mm(x, q, s, out=torch.empty(m, n, device="cuda", dtype=out_dtype))  # noqa: E731
+    tc = _with_path("tc", run)
+    ex = _with_path("exact", run)
+    assert torch.equal(tc, ex)
+    assert torch.equal(S.skinny_mm(x, q, s, out=torch.empty(m, n, device="cuda", dtype=out_dtype)), ex)  # default route
+
+
+def test_cuda_core_exact_kernel_nan_rows_and_zero_rows():
+    _, (q, s) = make_weights("int8", 2048, 2048, seed=1)
+    x = x_rows(4, 2048, seed=2)
+    x[1, 7] = float("inf")
+    x[2].zero_()
+    x[3, 100] = float("nan")
+    y = _with_path("exact", lambda: S.skinny_mm(x, q, s, out=torch.empty(4, 2048, device="cuda")))
+    assert torch.isnan(y[1]).all() and torch.isnan(y[3]).all()
+    assert (y[2] == 0).all() and torch.isfinite(y[0]).all()
+    tc = _with_path("tc", lambda: S.skinny_mm(x, q, s, out=torch.empty(4, 2048, device="cuda")))
+    assert torch.equal(torch.nan_to_num(tc, nan=7.0), torch.nan_to_num(y, nan=7.0))
