@@ -679,6 +679,12 @@ def scan_cells(device: torch.device, peak: float, reps: int = 5) -> dict:
         out[f"T{t}"] = {"us": round(us, 2), "us_per_step": round(us / t, 4),
                         "gbs": round(scan_bytes(t) / (us * 1e-6) / 1e9, 1), "problems_in_rotation": len(probs),
                         "torch_us": round(lib_us, 2), "vs_torch": round(lib_us / us, 2)}
+        if t == 1:  # the decode loop's use: one state advanced in place byte after byte (C stays in L2)
+            st_in, q, k, v, i, f, h, st_out = probs[0]
+            st_b = (st_in[0], st_out[1], st_out[2])  # C in place; n and m alternate between two buffers
+            warm = _graph_us_per_call(lambda: [mlstm_scan(st_in, q, k, v, i, f, h, st_b, 1e-6),
+                                               mlstm_scan(st_b, q, k, v, i, f, h, st_in, 1e-6)] * 8, 16, reps)
+            out["T1"]["warm_state_us"] = round(warm, 2)
         del probs, sub
         torch.cuda.empty_cache()
     return out

@@ -45,6 +45,21 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return p;
 }
 
+// L2 policy for data that should stay resident across kernels (the recurrent state of the decode loop,
+// re-read at every byte while the weights stream through L2 evict-first).
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t p;
+  asm("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// 16-byte store with an L2 cache policy.
+__device__ __forceinline__ void st_global16_hint(void* ptr, const float4& v, uint64_t policy) {
+  asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(ptr), "f"(v.x), "f"(v.y), "f"(v.z),
+               "f"(v.w), "l"(policy)
+               : "memory");
+}
+
 // 16-byte read-only streaming load: not allocated in L1, evict-first in L2.
 __device__ __forceinline__ uint4 ldg_stream16(const void* ptr, uint64_t policy) {
   uint4 r;
@@ -68,6 +83,11 @@ __device__ __forceinline__ uint32_t smem_addr(const void* p) {
 // Ampere-style asynchronous global -> shared copies (16 bytes), grouped with commit/wait.
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async16_hint(void* smem, const void* gmem, uint64_t policy) {
+  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(smem_addr(smem)), "l"(gmem),
+               "l"(policy)
+               : "memory");
 }
 __device__ __forceinline__ void cp_async4(void* smem, const void* gmem) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(smem)), "l"(gmem) : "memory");

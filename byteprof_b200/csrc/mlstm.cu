@@ -265,9 +265,13 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
     for (int s = 0; s < kDepth - 1; ++s) issue(s);
     gate_chunk<T>(a, head, 0, n_steps, m_run, g_f, g_i, g_mx);
   } else if (a.stage_c) {
-    // 16-byte chunk i = (row i / 4, columns 4 (i % 4) ..): a warp copies 8 whole rows per instruction
+    // 16-byte chunk i = (row i / 4, columns 4 (i % 4) ..): a warp copies 8 whole rows per instruction. The
+    // state is read and written with an L2 evict-last policy: in the decode loop it is re-read at the next
+    // byte while every weight in between streams through L2 evict-first.
+    const uint64_t keep = l2_evict_last_policy();
     for (int i = tid; i < DQ * 4; i += Cfg::NCOMP)
-      cp_async16(cst + stage_word(i >> 2, 4 * (i & 3)), cbase + static_cast<long long>(i >> 2) * a.DV + 4 * (i & 3));
+      cp_async16_hint(cst + stage_word(i >> 2, 4 * (i & 3)), cbase + static_cast<long long>(i >> 2) * a.DV + 4 * (i & 3),
+                      keep);
     cp_async_commit();
     cp_async_wait<0>();
     compute_sync(Cfg::NCOMP);
@@ -384,9 +388,10 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
 #pragma unroll
         for (int e = 0; e < 8; ++e) cst[stage_word((l + Cfg::TPC * ch) * 8 + e, col)] = creg[ch * 8 + e];
       compute_sync(Cfg::NCOMP);
+      const uint64_t keep = l2_evict_last_policy();
       for (int i = tid; i < DQ * 4; i += Cfg::NCOMP)
-        *reinterpret_cast<float4*>(obase + static_cast<long long>(i >> 2) * a.DV + 4 * (i & 3)) =
-            *reinterpret_cast<const float4*>(cst + stage_word(i >> 2, 4 * (i & 3)));
+        st_global16_hint(obase + static_cast<long long>(i >> 2) * a.DV + 4 * (i & 3),
+                         *reinterpret_cast<const float4*>(cst + stage_word(i >> 2, 4 * (i & 3))), keep);
     } else {
 #pragma unroll
       for (int ch = 0; ch < Cfg::CH; ++ch)

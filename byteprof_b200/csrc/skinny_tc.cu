@@ -11,15 +11,8 @@
 //    One kernel serves every M = 1..16, so a row's sum does not depend on the number of rows. (An MMA
 //    costs about the same for N = 16 as for N = 128, but four bf16 MMAs per 16 KB stage still run far
 //    faster than HBM delivers the stage.)
-//  * TMA streams 128-row weight tiles (16 KB per stage, 128-byte swizzle, L2 evict-first) into a
-//    shared-memory ring. The activations of every k-block the CTA touches arrive once, right after the
-//    dependency wait, as a window of [rows][64] tiles in a few power-of-two copies (a 3-D view of x), so the
-//    ring carries weights only and the MMAs of the stages loaded before the wait start as soon as the window
-//    lands. Up to M = 8 a window block holds 8 rows and the MMA's rows 8-15 read rows 0-7 again (their
-//    outputs are not stored). When the window does not fit beside a 3-stage ring (the LM head at M > 8),
-//    or K is not a whole number of 64-column blocks, each stage carries its own 16-row activation tile
-//    instead (rows beyond M zero-filled by TMA). Measured (graph of a cold weight ring): LM head M = 1
-//    66.8 us against 68.5 with per-stage tiles, M = 8 66.7 against 69.5.
+//  * TMA streams 128-row weight tiles (16 KB per stage, 128-byte swizzle, L2 evict-first) and the
+//    matching activation tile (rows beyond M zero-filled by TMA) into a shared-memory ring.
 //  * Two work partitions, chosen from (N, K) only (never from M):
 //     - stream-K (many tiles): a persistent grid of two CTAs per SM; CTA c owns the contiguous unit range
 //       [c U / P, (c + 1) U / P) of the U = tiles x k-blocks units, so every SM streams the same number
@@ -47,39 +40,13 @@ constexpr int kBM = 128;  // weight rows per tile (MMA M)
 constexpr int kNP = 16;   // activation rows per launch (MMA N)
 constexpr int kEpiThreads = 128;
 constexpr int kBK = 64;   // K elements per stage (one 128-byte swizzle row)
-constexpr int kMaxClusterSplit = 8;  // portable cluster size (clusters of 16 measured slower: 2048 x 2048 at M = 1
-                                     // 8.3 us against 4.4, 2048 x 8192 14.9 against 10.4)
-constexpr int kABytes = kBM * kBK * 2;  // 16 KB of weights per stage
-constexpr int kBBytes = kNP * kBK * 2;  // one activation tile of a k-block (16 rows)
-constexpr int kXRowBytes = kBK * 2;     // one activation row of a k-block
+constexpr int kMaxClusterSplit = 8;  // portable cluster size
+constexpr int kABytes = kBM * kBK * 2;
+constexpr int kBBytes = kNP * kBK * 2;
 constexpr int kThreads = 192;  // TMA, MMA, 4 epilogue warps
 constexpr int kEpiWarp0 = 2;
 constexpr uint32_t kTmemCols = 32;  // two 16-column accumulators
 constexpr int kEpiBatch = 4;        // stream-K partials loaded at once by the finishing CTA
-constexpr int kMaxStages = 6;
-constexpr int kMinWindowStages = 3;  // fewer weight stages than this: activations per stage instead
-constexpr int kRedElems = kNP * (kBM + kMaxClusterSplit);
-constexpr size_t kSmemPerCta = 115712;  // two CTAs per SM: 228 KB per SM, 1 KB of it reserved per CTA
-constexpr size_t kSmemSlack = 1024;     // the dynamic base is aligned up to 1024 bytes
-constexpr int kXBoxes = 6;              // activation-window copies of 32, 16, 8, 4, 2 or 1 k-blocks
-
-struct TcCtl {
-  uint64_t full[kMaxStages];
-  uint64_t empty[kMaxStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
-  uint64_t mma_done;
-  uint64_t xfull;
-  uint32_t tmem_base;
-  int abort;
-  int last_flag;
-};
-
-// Tensor maps of the activation window: the same [K / 64 blocks][M rows][64 columns] view of x with boxes of
-// 32 >> j k-blocks (j = 0 .. 5), so that any run of blocks is loaded in at most six copies.
-struct XMaps {
-  CUtensorMap m[kXBoxes];
-};
 
 struct TcArgs {
   void* y;
@@ -92,12 +59,39 @@ struct TcArgs {
   int S;            // cluster mode: CTAs per tile; 0: stream-K mode
   int* counters;    // stream-K: [tiles], zero between launches
   float* partials;  // stream-K: [P][2][kNP][kBM]
-  // shared-memory plan, offsets from the 1024-byte aligned base
-  int stages;       // weight ring depth
-  int xwin;         // 1: the CTA's activations arrive once, as a window of k-blocks; 0: one tile per stage
-  int xrows;        // rows per window block: 8 (M <= 8; the MMA's rows 8-15 read rows 0-7 again) or 16
-  uint32_t off_b, off_red, off_ctl;
 };
+
+// Stream-K: a 6-stage ring. Cluster split-K: 5 stages and the slots where the cluster's CTAs store their
+// partials of this CTA's rows ([source rank][activation row][row of this CTA's share]), so that two CTAs
+// still fit per SM.
+template <bool kCluster>
+struct TcCfg {
+  static constexpr int kStages = kCluster ? 5 : 6;
+  static constexpr int kRedElems = kCluster ? kNP * (kBM + kMaxClusterSplit) : 4;
+};
+
+template <bool kCluster>
+struct __align__(1024) TcSmem {
+  uint8_t a[TcCfg<kCluster>::kStages][kABytes];
+  uint8_t b[TcCfg<kCluster>::kStages][kBBytes];
+  float red[TcCfg<kCluster>::kRedElems];
+  uint64_t full[TcCfg<kCluster>::kStages];
+  uint64_t empty[TcCfg<kCluster>::kStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+  int last_flag;
+};
+
+template <bool kCluster>
+constexpr size_t smem_bytes() {
+  return sizeof(TcSmem<kCluster>) + 1024;  // + slack to align the base to 1024 bytes
+}
+// Two CTAs per SM (so that the next kernel's CTAs start under this one's tail): 228 KB per SM, 1 KB of
+// it reserved per CTA.
+static_assert(smem_bytes<false>() <= 115712 && smem_bytes<true>() <= 115712, "two CTAs per SM must fit");
 
 __host__ __device__ __forceinline__ long long unit_start(int c, long long U, int P) {
   return static_cast<long long>(c) * U / P;
@@ -132,39 +126,16 @@ __device__ __forceinline__ void store_rows(const TcArgs& a, int row, const float
     if (m < a.M) store_value(a, m, row, v[m]);
 }
 
-// Copies k-blocks [kb, kb + len) of the activations into window slots [slot, slot + len) in power-of-two
-// pieces (each piece lies inside the run, so no two copies write the same bytes).
-__device__ __forceinline__ void load_window_run(const XMaps& xm, uint8_t* win, uint32_t blk_bytes, uint64_t* bar,
-                                                int kb, int slot, int len) {
-#pragma unroll 1
-  for (int j = 0; j < kXBoxes; ++j) {
-    const int b = 32 >> j;
-    while (len >= b) {
-      tma_load_3d(win + static_cast<size_t>(slot) * blk_bytes, &xm.m[j], bar, 0, 0, kb);
-      kb += b;
-      slot += b;
-      len -= b;
-    }
-  }
-}
-
 // kCluster = false: stream-K over (tile, k-block) units, split tiles finished through the workspace.
 // kCluster = true: grid = tiles x S, the S CTAs of a cluster split one tile's K range evenly and add
 // their partials through distributed shared memory (used when there are few tiles).
 template <bool kCluster>
 __global__ void __launch_bounds__(kThreads, 2)
-    skinny_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
-                     const __grid_constant__ XMaps xm, const TcArgs a) {
+    skinny_tc_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx, const TcArgs a) {
+  constexpr int kStages = TcCfg<kCluster>::kStages;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* const base =
-      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-  TcCtl& s = *reinterpret_cast<TcCtl*>(base + a.off_ctl);
-  uint8_t* const ring = base;               // stages x 16 KB of weights
-  uint8_t* const bsm = base + a.off_b;      // the activation window, or one activation tile per stage
-  float* const red = reinterpret_cast<float*>(base + a.off_red);
-  const int stages = a.stages;
-  const bool xwin = a.xwin != 0;
-  const uint32_t xblk = static_cast<uint32_t>(a.xrows * kXRowBytes);  // bytes of one window block
+  TcSmem<kCluster>& s =
+      *reinterpret_cast<TcSmem<kCluster>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int c = blockIdx.x;
   const long long U = a.units;
@@ -183,12 +154,9 @@ __global__ void __launch_bounds__(kThreads, 2)
   const int n_units = static_cast<int>(u1 - u0);
   const int t_first = static_cast<int>(u0 / KB);
   const int t_last = n_units > 0 ? static_cast<int>((u1 - 1) / KB) : t_first - 1;
-  // The activation window: all K blocks when the CTA's units cover a whole tile (slot = k-block), else the
-  // n_units consecutive blocks from u0 (slot = u - u0, the run wrapping past the last block to block 0).
-  const bool all_blocks = n_units >= KB;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) {
+    for (int i = 0; i < kStages; ++i) {
       mbar_init(&s.full[i], 1);
       mbar_init(&s.empty[i], 1);
     }
@@ -197,15 +165,11 @@ __global__ void __launch_bounds__(kThreads, 2)
       mbar_init(&s.tempty[b], kEpiThreads);
     }
     mbar_init(&s.mma_done, 1);
-    mbar_init(&s.xfull, 1);
     s.abort = 0;
     s.last_flag = 0;
     mbar_fence_init();
     tma_prefetch_desc(&tw);
-    if (xwin)
-      for (int j = 0; j < kXBoxes; ++j) tma_prefetch_desc(&xm.m[j]);
-    else
-      tma_prefetch_desc(&tx);
+    tma_prefetch_desc(&tx);
   }
   if (warp == 1) {
     tmem_alloc(&s.tmem_base, kTmemCols);
@@ -222,57 +186,38 @@ __global__ void __launch_bounds__(kThreads, 2)
     if (lane == 0) {
       // ---- TMA producer ----
       const uint64_t pol = l2_evict_first_policy();
-      const uint32_t stage_tx = xwin ? kABytes : kABytes + kBBytes;
-      const int npre = n_units < stages ? n_units : stages;
+      const int npre = n_units < kStages ? n_units : kStages;
       for (int i = 0; i < npre; ++i) {  // weights only: they do not depend on the previous kernel
         const long long u = u0 + i;
         const int t = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
-        mbar_arrive_expect_tx(&s.full[i], stage_tx);
-        tma_load_2d_hint(ring + static_cast<size_t>(i) * kABytes, &tw, &s.full[i], kb * kBK, t * kBM, pol);
+        mbar_arrive_expect_tx(&s.full[i], kABytes + kBBytes);
+        tma_load_2d_hint(s.a[i], &tw, &s.full[i], kb * kBK, t * kBM, pol);
       }
       pdl_wait_prior_grids();
-      if (xwin) {
-        if (n_units > 0) {  // the whole window in a few copies, on its own barrier
-          const int xn = all_blocks ? KB : n_units;
-          mbar_arrive_expect_tx(&s.xfull, static_cast<uint32_t>(xn) * xblk);
-          const int kb0 = all_blocks ? 0 : static_cast<int>(u0 % KB);
-          const int first = xn < KB - kb0 ? xn : KB - kb0;
-          load_window_run(xm, bsm, xblk, &s.xfull, kb0, 0, first);
-          if (xn > first) load_window_run(xm, bsm, xblk, &s.xfull, 0, first, xn - first);
-        }
-      } else {
-        for (int i = 0; i < npre; ++i)
-          tma_load_2d(bsm + static_cast<size_t>(i) * kBBytes, &tx, &s.full[i], static_cast<int>((u0 + i) % KB) * kBK, 0);
-      }
+      for (int i = 0; i < npre; ++i) tma_load_2d(s.b[i], &tx, &s.full[i], static_cast<int>((u0 + i) % KB) * kBK, 0);
       int issued = npre;
-      int st = npre % stages, ph = (npre / stages) & 1;  // stage and ring pass of unit i
       for (int i = npre; i < n_units; ++i) {
-        if (!mbar_wait(&s.empty[st], static_cast<uint32_t>(ph ^ 1), abort)) break;
+        const int st = i % kStages;
+        if (!mbar_wait(&s.empty[st], static_cast<uint32_t>((i / kStages) + 1) & 1u, abort)) break;
         const long long u = u0 + i;
         const int t = static_cast<int>(u / KB), kb = static_cast<int>(u % KB);
-        mbar_arrive_expect_tx(&s.full[st], stage_tx);
-        tma_load_2d_hint(ring + static_cast<size_t>(st) * kABytes, &tw, &s.full[st], kb * kBK, t * kBM, pol);
-        if (!xwin) tma_load_2d(bsm + static_cast<size_t>(st) * kBBytes, &tx, &s.full[st], kb * kBK, 0);
+        mbar_arrive_expect_tx(&s.full[st], kABytes + kBBytes);
+        tma_load_2d_hint(s.a[st], &tw, &s.full[st], kb * kBK, t * kBM, pol);
+        tma_load_2d(s.b[st], &tx, &s.full[st], kb * kBK, 0);
         issued = i + 1;
-        if (++st == stages) {
-          st = 0;
-          ph ^= 1;
-        }
       }
-      // drain: the last copy issued into each stage (and the window) has landed
-      for (int j = 0; j < stages && j < issued; ++j) {
-        const int i_last = j + stages * ((issued - 1 - j) / stages);
-        mbar_wait_drain(&s.full[j], static_cast<uint32_t>(i_last / stages) & 1u);
+      // drain: the last copy issued into each stage has landed
+      for (int st = 0; st < kStages && st < issued; ++st) {
+        const int i_last = st + kStages * ((issued - 1 - st) / kStages);
+        mbar_wait_drain(&s.full[st], static_cast<uint32_t>(i_last / kStages) & 1u);
       }
-      if (xwin && n_units > 0) mbar_wait_drain(&s.xfull, 0);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---- MMA issuer ----
       constexpr uint32_t idesc = umma_idesc_bf16(kBM, kNP);
-      const uint32_t bsbo = (xwin && a.xrows == 8) ? 0u : 1024u;  // 8-row window blocks: rows 8-15 repeat 0-7
-      int it = 0, st = 0, ph = 0;
-      bool ok = !xwin || n_units == 0 || mbar_wait(&s.xfull, 0, abort);
+      int i = 0, it = 0;
+      bool ok = true;
       for (int t = t_first; t <= t_last && ok; ++t, ++it) {
         const long long lo = u0 > static_cast<long long>(t) * KB ? u0 : static_cast<long long>(t) * KB;
         const long long hi = u1 < static_cast<long long>(t + 1) * KB ? u1 : static_cast<long long>(t + 1) * KB;
@@ -280,25 +225,19 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (!mbar_wait(&s.tempty[buf], static_cast<uint32_t>((it >> 1) + 1) & 1u, abort)) break;
         tc_fence_after_sync();
         const uint32_t dacc = tmem + static_cast<uint32_t>(buf * kNP);
-        for (long long u = lo; u < hi; ++u) {
-          if (!mbar_wait(&s.full[st], static_cast<uint32_t>(ph), abort)) {
+        for (long long u = lo; u < hi; ++u, ++i) {
+          const int st = i % kStages;
+          if (!mbar_wait(&s.full[st], static_cast<uint32_t>(i / kStages) & 1u, abort)) {
             ok = false;
             break;
           }
           tc_fence_after_sync();
-          const uint32_t ab = smem_addr(ring + static_cast<size_t>(st) * kABytes);
-          const int slot = all_blocks ? static_cast<int>(u % KB) : static_cast<int>(u - u0);
-          const uint32_t bb = xwin ? smem_addr(bsm + static_cast<size_t>(slot) * xblk)
-                                   : smem_addr(bsm + static_cast<size_t>(st) * kBBytes);
+          const uint32_t ab = smem_addr(s.a[st]), bb = smem_addr(s.b[st]);
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk)
-            umma_f16(dacc, umma_desc_sw128(ab + 32 * kk), umma_desc_sw128_sbo(bb + 32 * kk, bsbo), idesc,
+            umma_f16(dacc, umma_desc_sw128(ab + 32 * kk), umma_desc_sw128(bb + 32 * kk), idesc,
                      (u > lo || kk > 0) ? 1u : 0u);
           umma_commit(&s.empty[st]);  // frees the stage once these MMAs have read it
-          if (++st == stages) {
-            st = 0;
-            ph ^= 1;
-          }
         }
         if (ok) umma_commit(&s.tfull[buf]);
       }
@@ -326,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 2)
         // one tile per CTA: row r's partial goes to the slot for this rank in the CTA that owns row r
         const int R = (kBM + a.S - 1) / a.S;
         const int own = r / R;
-        const uint32_t dst = mapa_shared(smem_addr(&red[rank * kNP * R + (r - own * R)]), static_cast<uint32_t>(own));
+        const uint32_t dst = mapa_shared(smem_addr(&s.red[rank * kNP * R + (r - own * R)]), static_cast<uint32_t>(own));
 #pragma unroll
         for (int m = 0; m < kNP; ++m)
           if (m < a.M)
@@ -408,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 2)
       for (int item = threadIdx.x; item < nrows * a.M; item += kThreads) {
         const int m = item / nrows, lr = item - m * nrows;
         float v = 0.0f;
-        for (int src = 0; src < S; ++src) v += red[(src * kNP + m) * R + lr];
+        for (int src = 0; src < S; ++src) v += s.red[(src * kNP + m) * R + lr];
         const int row = t * kBM + r0 + lr;
         if (row < a.N) store_value(a, m, row, v);
       }
@@ -435,91 +374,6 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Work partition; depends on (N, K) and the SM count only, never on M.
-struct Partition {
-  int tiles, kblocks, P, S;  // S > 0: cluster mode with S CTAs per tile; S == 0: stream-K over P CTAs
-  long long units;
-  int K;
-};
-
-// Shared-memory plan of one launch (depends on M through the window's rows; never changes the partition).
-struct Plan {
-  int stages, xwin, xrows;
-  uint32_t off_b, off_red, off_ctl;
-  size_t dyn_bytes;
-};
-
-// BP_TC_XWINDOW=off loads an activation tile with every weight stage instead of the window (for comparisons).
-bool xwindow_enabled() {
-  static int v = -1;
-  if (v < 0) {
-    const char* e = getenv("BP_TC_XWINDOW");
-    v = (e != nullptr && e[0] == 'o' && e[1] == 'f') ? 0 : 1;
-  }
-  return v == 1;
-}
-
-Partition partition(int N, int K) {
-  Partition p;
-  p.tiles = (N + kBM - 1) / kBM;
-  p.kblocks = (K + kBK - 1) / kBK;
-  p.units = static_cast<long long>(p.tiles) * p.kblocks;
-  p.K = K;
-  const int sms = tc_sm_count();
-  if (2 * p.tiles <= sms) {
-    // few tiles: split each tile's K range over a cluster of S CTAs (no workspace, no global fix-up). Two
-    // CTAs fit per SM, so S = 2 SMs / tiles: every SM then runs two producers (measured on 8192 x 2048:
-    // 9.9 us with S = 2, 8.5 us with S = 4)
-    int S = 2 * sms / p.tiles;
-    if (S > kMaxClusterSplit) S = kMaxClusterSplit;
-    if (S > p.kblocks) S = p.kblocks;
-    p.S = S < 1 ? 1 : S;
-    p.P = p.tiles * p.S;
-  } else {
-    // two CTAs per SM, each with its own ring: twice the weight bytes in flight per SM
-    p.S = 0;
-    p.P = static_cast<int>(p.units < 2 * sms ? p.units : 2 * sms);
-  }
-  return p;
-}
-
-Plan plan_smem(const Partition& p, int M) {
-  Plan q;
-  const size_t budget = kSmemPerCta - kSmemSlack;
-  const size_t ctl = (sizeof(TcCtl) + 15) & ~static_cast<size_t>(15);
-  const size_t red = p.S > 0 ? kRedElems * sizeof(float) : 0;
-  q.xrows = M <= 8 ? 8 : kNP;
-  // the largest window of any CTA: its K range in cluster mode, else min(units per CTA, k-blocks)
-  long long most;
-  if (p.S > 0) {
-    most = (p.kblocks + p.S - 1) / p.S;
-  } else {
-    const long long per = (p.units + p.P - 1) / p.P;
-    most = per < p.kblocks ? per : p.kblocks;
-  }
-  const size_t win = (static_cast<size_t>(most) * q.xrows * kXRowBytes + 1023) & ~static_cast<size_t>(1023);
-  const long long room = static_cast<long long>(budget) - static_cast<long long>(red + ctl + win);
-  const long long wstages = room > 0 ? room / kABytes : 0;
-  // The window's view of x has no K bound inside a block (its innermost extent is the block's 64 columns), so
-  // it is used only when K is a whole number of blocks; otherwise the per-stage tiles, whose 2-D view fills
-  // the columns past K with zeros.
-  if (xwindow_enabled() && p.kblocks * kBK == p.K && wstages >= kMinWindowStages) {
-    q.xwin = 1;
-    q.stages = static_cast<int>(wstages < kMaxStages ? wstages : kMaxStages);
-    q.off_b = static_cast<uint32_t>(q.stages) * kABytes;
-    q.off_red = q.off_b + static_cast<uint32_t>(win);
-  } else {
-    q.xwin = 0;
-    const long long ps = static_cast<long long>(budget - red - ctl) / (kABytes + kBBytes);
-    q.stages = static_cast<int>(ps < kMaxStages ? ps : kMaxStages);
-    q.off_b = static_cast<uint32_t>(q.stages) * kABytes;
-    q.off_red = q.off_b + static_cast<uint32_t>(q.stages) * kBBytes;
-  }
-  q.off_ctl = q.off_red + static_cast<uint32_t>(red);
-  q.dyn_bytes = q.off_ctl + ctl + kSmemSlack;
-  return q;
-}
-
 template <bool kCluster>
 int ensure_attrs() {
   static bool done[64] = {false};
@@ -527,16 +381,46 @@ int ensure_attrs() {
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && done[dev]) return BP_OK;
   cudaError_t e = cudaFuncSetAttribute(skinny_tc_kernel<kCluster>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(kSmemPerCta));
-  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+                                       static_cast<int>(smem_bytes<kCluster>()));
+  if (e != cudaSuccess)
+    return fail(BP_ERR_CUDA, "cudaFuncSetAttribute(smem %zu): %s", smem_bytes<kCluster>(), cudaGetErrorString(e));
   if (dev >= 0 && dev < 64) done[dev] = true;
   return BP_OK;
 }
 
+// Work partition; depends on (N, K) and the SM count only, never on M.
+struct Partition {
+  int tiles, kblocks, P, S;  // S > 0: cluster mode with S CTAs per tile; S == 0: stream-K over P CTAs
+  long long units;
+};
+
+Partition partition(int N, int K) {
+  Partition p;
+  p.tiles = (N + kBM - 1) / kBM;
+  p.kblocks = (K + kBK - 1) / kBK;
+  p.units = static_cast<long long>(p.tiles) * p.kblocks;
+  const int sms = tc_sm_count();
+  if (2 * p.tiles <= sms) {
+    // few tiles: split each tile's K range over a cluster of S CTAs (no workspace, no global fix-up). Two
+    // CTAs fit per SM, so S = 2 SMs / tiles: every SM then runs two producers, and a single producer issuing
+    // a weight and an activation copy per stage streams well below the SM's share of HBM (measured on
+    // 8192 x 2048: 9.9 us with S = 2, 8.5 us with S = 4)
+    int S = 2 * sms / p.tiles;
+    if (S > kMaxClusterSplit) S = kMaxClusterSplit;
+    if (S > p.kblocks) S = p.kblocks;
+    p.S = S < 1 ? 1 : S;
+    p.P = p.tiles * p.S;
+  } else {
+    // two CTAs per SM, each with its own 6-stage ring: twice the weight bytes in flight per SM
+    p.S = 0;
+    p.P = static_cast<int>(p.units < 2 * sms ? p.units : 2 * sms);
+  }
+  return p;
+}
+
 template <bool kCluster>
-cudaError_t launch_kernel(cudaLaunchConfig_t* cfg, const CUtensorMap& tw, const CUtensorMap& tx, const XMaps& xm,
-                          const TcArgs& a) {
-  return cudaLaunchKernelEx(cfg, skinny_tc_kernel<kCluster>, tw, tx, xm, a);
+cudaError_t launch_kernel(cudaLaunchConfig_t* cfg, const CUtensorMap& tw, const CUtensorMap& tx, const TcArgs& a) {
+  return cudaLaunchKernelEx(cfg, skinny_tc_kernel<kCluster>, tw, tx, a);
 }
 
 size_t skinny_bf16_workspace_bytes(int N, int K) {
@@ -549,7 +433,6 @@ size_t skinny_bf16_workspace_bytes(int N, int K) {
 int launch_skinny_bf16(const void* x, long long ldx, const void* w, void* y, long long ldy, int y_f32, int M, int N,
                        int K, void* ws, size_t ws_bytes, cudaStream_t stream) {
   const Partition p = partition(N, K);
-  const Plan q = plan_smem(p, M);
   const size_t need = skinny_bf16_workspace_bytes(N, K);
   if (need > 0 && (ws == nullptr || ws_bytes < need))
     return fail(BP_ERR_INVALID_ARGUMENT, "the tensor-core path needs a zero-initialised workspace of %zu bytes (got %zu)",
@@ -559,28 +442,12 @@ int launch_skinny_bf16(const void* x, long long ldx, const void* w, void* y, lon
   int st = p.S > 0 ? ensure_attrs<true>() : ensure_attrs<false>();
   if (st != BP_OK) return st;
   CUtensorMap tw, tx;
-  XMaps xm;
   st = tc_encode_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, w, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
                     static_cast<uint64_t>(K) * 2, kBK, kBM, CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
   if (st != BP_OK) return st;
-  if (q.xwin) {
-    // x as [K / 64 blocks][M rows][64 columns]: block stride 128 bytes, row stride ldx elements; a box of b
-    // blocks of xrows rows lands as b consecutive [xrows][64] swizzled tiles (rows >= M zero-filled)
-    const uint64_t dims[3] = {static_cast<uint64_t>(kBK), static_cast<uint64_t>(M), static_cast<uint64_t>(p.kblocks)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(ldx) * 2, static_cast<uint64_t>(kXRowBytes)};
-    for (int j = 0; j < kXBoxes; ++j) {
-      const uint32_t box[3] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(q.xrows), static_cast<uint32_t>(32 >> j)};
-      st = tc_encode(&xm.m[j], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, x, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B,
-                     CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
-      if (st != BP_OK) return st;
-    }
-    tx = xm.m[kXBoxes - 1];  // not read in window mode
-  } else {
-    st = tc_encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
-                      static_cast<uint64_t>(ldx) * 2, kBK, kNP, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
-    if (st != BP_OK) return st;
-    for (int j = 0; j < kXBoxes; ++j) xm.m[j] = tx;  // not read in per-stage mode
-  }
+  st = tc_encode_2d(&tx, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
+                    static_cast<uint64_t>(ldx) * 2, kBK, kNP, CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
+  if (st != BP_OK) return st;
 
   TcArgs a;
   a.y = y;
@@ -596,17 +463,11 @@ int launch_skinny_bf16(const void* x, long long ldx, const void* w, void* y, lon
   a.S = p.S;
   a.counters = need > 0 ? static_cast<int*>(ws) : nullptr;
   a.partials = need > 0 ? reinterpret_cast<float*>(static_cast<char*>(ws) + kTcCountersBytes) : nullptr;
-  a.stages = q.stages;
-  a.xwin = q.xwin;
-  a.xrows = q.xrows;
-  a.off_b = q.off_b;
-  a.off_red = q.off_red;
-  a.off_ctl = q.off_ctl;
 
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.P, 1, 1);
   cfg.blockDim = dim3(kThreads, 1, 1);
-  cfg.dynamicSmemBytes = q.dyn_bytes;
+  cfg.dynamicSmemBytes = p.S > 0 ? smem_bytes<true>() : smem_bytes<false>();
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   int na = 0;
@@ -624,10 +485,10 @@ int launch_skinny_bf16(const void* x, long long ldx, const void* w, void* y, lon
   }
   cfg.attrs = attr;
   cfg.numAttrs = na;
-  const cudaError_t e = p.S > 0 ? launch_kernel<true>(&cfg, tw, tx, xm, a) : launch_kernel<false>(&cfg, tw, tx, xm, a);
+  const cudaError_t e = p.S > 0 ? launch_kernel<true>(&cfg, tw, tx, a) : launch_kernel<false>(&cfg, tw, tx, a);
   if (e != cudaSuccess)
-    return fail(BP_ERR_CUDA, "tensor-core skinny launch (bf16 M=%d N=%d K=%d P=%d S=%d stages=%d window=%d): %s", M, N,
-                K, p.P, p.S, q.stages, q.xwin, cudaGetErrorString(e));
+    return fail(BP_ERR_CUDA, "tensor-core skinny launch (bf16 M=%d N=%d K=%d P=%d S=%d): %s", M, N, K, p.P, p.S,
+                cudaGetErrorString(e));
   return BP_OK;
 }
 

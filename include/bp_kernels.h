@@ -68,8 +68,8 @@ const char* bp_last_error(void);
  *          w_dtype = BP_DTYPE_INT8: int8 [N, K] contiguous, w_scale = bf16 [N]; y = scale[n] * sum_k x*q.
  *          Aligned int8 problems (x and w 16-byte aligned, ldx a multiple of 8, K a multiple of 16) sum
  *          exactly over x written in fixed point (29 bits below each row's largest exponent: every x within
- *          2^-22 of the row maximum is exact) and round scale * sum once, on the tensor cores or, for up to
- *          1 row and at most 4096 output rows, on the CUDA cores in one launch: the two give the same
+ *          2^-22 of the row maximum is exact) and round scale * sum once, on the tensor cores or, for one
+ *          row and at most 4096 output rows, on the CUDA cores in one launch: the two give the same
  *          bits, so a row's result never depends on M. A row of x holding Inf or NaN gives a NaN row of y
  *   y      y_dtype BP_DTYPE_BF16 or BP_DTYPE_F32 (the fp32 store is the un-rounded accumulator), row
  *          stride ldy elements; exactly the M x N block is written

@@ -40,11 +40,11 @@ def test_matches_oracle_for_every_m(kind, n, k):
 
 
 @pytest.mark.parametrize("n,k", [(12288, 2048), (20480, 4096), (100352, 2048), (256, 16384), (1024, 64), (300, 5056)])
-def test_activation_window_shapes(n, k):
-    """The bf16 kernel's activation window: stream-K CTAs whose units wrap from the last k-block to the first
-    (12288 x 2048, 20480 x 4096), CTAs covering whole tiles (the LM head), large cluster windows (256 x 16384),
-    one k-block (K = 64) and an odd tile count; M on both sides of 8 (8-row window blocks up to M = 8). Rows
-    must also be bit-identical whatever M is."""
+def test_stream_k_and_cluster_partitions(n, k):
+    """The bf16 kernel's two partitions at their edges: stream-K CTAs whose units wrap from a tile's last k-block
+    to the next tile's first (12288 x 2048, 20480 x 4096), CTAs covering whole tiles (the LM head), long cluster
+    K ranges (256 x 16384), one k-block (K = 64) and an odd tile count, at M on both sides of 8. Rows must also
+    be bit-identical whatever M is."""
     _, args = make_weights("bf16", n, k, seed=3)
     wd = deq_np("bf16", args)
     x = x_rows(16, k, seed=4)
