@@ -75,10 +75,14 @@ def dist_env() -> tuple[int, int, int]:
 
 
 def init_dist(backend: str, timeout_s: float = 120.0) -> None:
+    """One process group per job (torchrun's environment); NCCL ranks name their GPU explicitly."""
     import torch.distributed as dist
 
     if dist.is_available() and not dist.is_initialized() and int(os.environ.get("WORLD_SIZE", 1)) > 1:
-        dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s))
+        kw = {}
+        if backend == "nccl":
+            kw["device_id"] = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+        dist.init_process_group(backend, timeout=timedelta(seconds=timeout_s), **kw)
 
 
 def barrier() -> None:
