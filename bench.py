@@ -590,7 +590,7 @@ def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 2
         "weight_bytes": {"local_per_byte": local_bytes, "global_per_patch": glob_bytes},
         "weight_gbs": round(streamed / ours["wall"] / 1e9, 1),
         "frac": round(streamed / ours["wall"] / 1e9 / peak, 4),
-        "graphs_per_byte": "enc + dec, + glob on a patch start; one host sync per byte",
+        "graphs_per_byte": "one graph per byte: enc + dec, or enc + glob + dec on a patch start; one host sync per byte",
     }
     try:
         out["exactness"] = _divergence_from_exact(m, ours, seed, device)

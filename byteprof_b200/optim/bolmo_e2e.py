@@ -11,9 +11,9 @@ the shapes of the end-to-end benchmark configuration and weights ~ N(0, 0.02) (n
     gives the patch value (byteprof/optim/bolmo_loop.py:58-61 does the same with dec.initial_norm);
   * local decoder: W_in e + patch value -> one mLSTM layer -> RMSNorm -> LM head 2048 -> 512 -> argmax.
 The loop is byteprof's minimal loop (byteprof/optim/bolmo_loop.py:1-20, 182-207; bolmo.py:47-136): per
-byte the encoder graph, the global graph only when the previous step flagged a boundary (the first
-byte opens a patch), the decoder graph, then one device-to-host read of (token, boundary flag): the
-only synchronisation. Every projection is a skinny GEMM of this library (M = 1), the mLSTM steps are
+byte the encoder, the global step only when the previous step flagged a boundary (the first byte opens a
+patch), the decoder, then one device-to-host read of (token, boundary flag): the only synchronisation.
+Each byte is one CUDA graph launch (encoder + decoder, or encoder + global step + decoder). Every projection is a skinny GEMM of this library (M = 1), the mLSTM steps are
 the fused scan, and the glue between them is the fused kernels of `decode_ops`. By default the global
 step is one persistent kernel (decode_ops.GlobStep, csrc/glob_step.cu); fused_glob=False runs it kernel
 by kernel (GlobalBlock.step). fused_local=True runs each local step as one persistent kernel too
@@ -184,29 +184,35 @@ class BolmoDecoder:
         return (("enc0", lambda: self.enc_step(0)), ("enc1", lambda: self.enc_step(1)), ("glob", self.glob_step),
                 ("dec0", lambda: self.dec_step(0)), ("dec1", lambda: self.dec_step(1)))
 
+    def _bytes(self):
+        """The whole work of one byte as one piece, per state parity: encoder and decoder, or encoder, global
+        step and decoder when the byte opens a patch (one graph launch per byte, no gaps between graphs)."""
+        def one(p: int, patch: bool):
+            def fn():
+                self.enc_step(p)
+                if patch:
+                    self.glob_step()
+                self.dec_step(p)
+            return fn
+        return tuple((f"{'patch' if patch else 'byte'}{p}", one(p, patch)) for p in (0, 1) for patch in (False, True))
+
     def capture(self) -> None:
-        """One CUDA graph per piece and state parity. The warm-up runs go through the same buffers and
-        are undone by `reset` (capture before decoding)."""
+        """One CUDA graph per piece and state parity (the pieces alone, for timing them, and each byte's whole
+        work, which `launch` replays). The warm-up runs go through the same buffers and are undone by `reset`
+        (capture before decoding)."""
         s_ = torch.cuda.Stream()
         s_.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s_):
             for _, fn in self._pieces():
                 fn()
         torch.cuda.current_stream().wait_stream(s_)
-        for name, fn in self._pieces():
+        for name, fn in self._pieces() + self._bytes():
             g = torch.cuda.CUDAGraph()
             with torch.cuda.graph(g):
                 fn()
             self.graphs[name] = g
         torch.cuda.synchronize()
         self.reset()
-
-    def _run(self, name: str, fn) -> None:
-        g = self.graphs.get(name)
-        if g is not None:
-            g.replay()
-        else:
-            fn()
 
     def launch(self, b: int, new_patch: bool) -> None:
         """Queue one byte (encoder, the global model if a patch starts here, decoder); no sync."""
@@ -217,11 +223,16 @@ class BolmoDecoder:
         p = self.parity
         self._pin_byte[0] = b
         self.byte.copy_(self._pin_byte, non_blocking=True)
-        self._run(f"enc{p}", lambda: self.enc_step(p))
+        whole = self.graphs.get(f"{'patch' if new_patch else 'byte'}{p}")
+        if whole is not None:
+            whole.replay()
+        else:
+            self.enc_step(p)
+            if new_patch:
+                self.glob_step()
+            self.dec_step(p)
         if new_patch:
-            self._run("glob", self.glob_step)
             self.patches += 1
-        self._run(f"dec{p}", lambda: self.dec_step(p))
         self._pin_out.copy_(self.out, non_blocking=True)
         self.parity = 1 - p
 
