@@ -29,7 +29,39 @@ int check_launch(const char* what);
 // The current device must be sm_100 (B200 class); cached per device.
 int require_sm100();
 
+// Programmatic dependent launch: kernels launched with it start while the kernel before them in the
+// stream still runs, and wait for it (pdl_wait_prior_grids) before touching anything it may write. On
+// unless BP_DISABLE_PDL=1.
+bool tc_pdl_enabled();
+
+// Fills `attr` (room for two) with the PDL attribute (when enabled) and a cluster of `cluster_y` CTAs
+// along y (when above 1), and points `cfg` at them.
+inline void set_launch_attrs(cudaLaunchConfig_t& cfg, cudaLaunchAttribute* attr, int cluster_y = 1) {
+  unsigned n = 0;
+  if (tc_pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_y > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = 1;
+    attr[n].val.clusterDim.y = static_cast<unsigned>(cluster_y);
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+}
+
 // ---- device helpers -----------------------------------------------------------------------------
+// Counterparts of set_launch_attrs' PDL attribute inside a kernel: let the next kernel's CTAs launch
+// now (they wait on their side), and wait until every kernel before this one has finished and its
+// writes are visible. Every kernel of a PDL chain waits before it reads or writes data another kernel
+// touches, so one kernel's wait also covers all kernels before it.
+__device__ __forceinline__ void pdl_wait_prior_grids() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
 

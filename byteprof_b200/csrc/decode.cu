@@ -114,6 +114,8 @@ struct NormArgs {
   int rows, cols;
   float eps;
   int team, iters;
+  const long long* index;  // gather mode (PLAIN): row r of x is row index[r] of a table of index_rows rows
+  long long index_rows;
 };
 
 // Row r = g * w_rows + j lives at g * ld + j * cols (w_rows = 1: the usual r * ld).
@@ -168,22 +170,34 @@ __global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs<T> a) {
   const int rc = live ? r : a.rows - 1;  // rows past the end read the last row and store nothing
   const __nv_bfloat16* wr = a.w + static_cast<long long>(rc % a.w_rows) * a.cols;
   const T* xr = a.x + row_off(rc, a.w_rows, a.cols, a.ldx);
+  bool poison = false;  // gather mode: an index outside the table gives a NaN row
+  if (MODE == BP_NORM_PLAIN && a.index != nullptr) {
+    const long long id = a.index[rc];
+    poison = id < 0 || id >= a.index_rows;
+    xr = a.x + (poison ? 0 : id) * a.ldx;
+  }
   const T* rr = MODE == BP_NORM_PLAIN ? nullptr : a.res + row_off(rc, a.w_rows, a.cols, a.ldres);
   float f[kCached ? kNormCache : 1][8];
   float ss = 0.0f;
+  auto load = [&](int c, float (&v)[8]) {
+    norm_in8<MODE, T>(xr, rr, c, v);
+    if (poison)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __int_as_float(0x7fc00000);
+  };
   if (kCached) {
 #pragma unroll
     for (int i = 0; i < kNormCache; ++i) {
       const int c = (t + i * team) * 8;
       if (i < a.iters && c < a.cols) {
-        norm_in8<MODE, T>(xr, rr, c, f[i]);
+        load(c, f[i]);
 #pragma unroll
         for (int j = 0; j < 8; ++j) ss = fmaf(f[i][j], f[i][j], ss);
       }
     }
   } else {
     for (int c = t * 8; c < a.cols; c += team * 8) {
-      norm_in8<MODE, T>(xr, rr, c, f[0]);
+      load(c, f[0]);
 #pragma unroll
       for (int j = 0; j < 8; ++j) ss = fmaf(f[0][j], f[0][j], ss);
     }
@@ -197,7 +211,10 @@ __global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs<T> a) {
   const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(a.cols)), a.eps)));
   if (!live) return;
   T* yr = a.y + row_off(r, a.w_rows, a.cols, a.ldy);
-  T* sr = (MODE == BP_NORM_ADD_FIRST && a.s_out != nullptr) ? a.s_out + row_off(r, a.w_rows, a.cols, a.lds) : nullptr;
+  // s_out: the sum (ADD_FIRST) or the gathered row (gather mode)
+  T* sr = a.s_out != nullptr && (MODE == BP_NORM_ADD_FIRST || (MODE == BP_NORM_PLAIN && a.index != nullptr))
+              ? a.s_out + row_off(r, a.w_rows, a.cols, a.lds)
+              : nullptr;
   if (kCached) {
 #pragma unroll
     for (int i = 0; i < kNormCache; ++i) {
@@ -206,7 +223,7 @@ __global__ void __launch_bounds__(kNormThreads) norm_ex_kernel(NormArgs<T> a) {
     }
   } else {
     for (int c = t * 8; c < a.cols; c += team * 8) {
-      norm_in8<MODE, T>(xr, rr, c, f[0]);
+      load(c, f[0]);
       norm_out8<MODE, T>(f[0], inv, wr, rr, sr, yr, c);
     }
   }
@@ -598,7 +615,7 @@ cudaError_t launch_norm_mode(const void* x, long long ldx, const void* w, int w_
                              void* s_out, long long lds, void* y, long long ldy, int rows, int cols, float eps, int mode,
                              cudaStream_t s) {
   NormArgs<T> a{static_cast<const T*>(x), ldx, static_cast<const __nv_bfloat16*>(w), w_rows, static_cast<const T*>(res),
-                ldres, static_cast<T*>(s_out), lds, static_cast<T*>(y), ldy, rows, cols, eps, 0, 0};
+                ldres, static_cast<T*>(s_out), lds, static_cast<T*>(y), ldy, rows, cols, eps, 0, 0, nullptr, 0};
   switch (mode) {
     case BP_NORM_PLAIN: return launch_norm<BP_NORM_PLAIN, T>(a, s);
     case BP_NORM_ADD_FIRST: return launch_norm<BP_NORM_ADD_FIRST, T>(a, s);
@@ -646,6 +663,34 @@ extern "C" int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_
           : launch_norm_mode<float>(x, ldx, w, w_rows, res, ldres, s_out, lds, y, ldy, rows, cols, eps, mode, s);
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "rmsnorm_ex launch: %s", cudaGetErrorString(e));
   return check_launch("rmsnorm_ex");
+}
+
+// Embedding lookup fused with the first norm of the byte encoder: h_out[r] = table[index[r]] and
+// y[r] = rmsnorm(h_out[r]) * w, both bf16 (one launch instead of a gather kernel and a norm; the gather
+// takes part in the PDL chain).
+extern "C" int bp_embed_rmsnorm(const void* table, long long ld_table, long long table_rows, const int64_t* index,
+                                const void* w, void* h_out, long long ldh, void* y, long long ldy, int rows, int cols,
+                                float eps, void* stream) {
+  using namespace bp;
+  clear_error();
+  if (rows < 0 || cols < 0 || table_rows < 0)
+    return fail(BP_ERR_INVALID_ARGUMENT, "bad size (rows=%d cols=%d table_rows=%lld)", rows, cols, table_rows);
+  if (rows == 0 || cols == 0) return BP_OK;
+  if (table == nullptr || index == nullptr || w == nullptr || y == nullptr)
+    return fail(BP_ERR_INVALID_ARGUMENT, "table, index, w or y is NULL");
+  if (ld_table < cols || ldy < cols || (h_out != nullptr && ldh < cols))
+    return fail(BP_ERR_INVALID_ARGUMENT, "row strides must be >= cols");
+  if (cols % 8 != 0 || ld_table % 8 != 0 || ldy % 8 != 0 || ldh % 8 != 0 || !aligned16(table) || !aligned16(w) ||
+      !aligned16(y) || (h_out != nullptr && !aligned16(h_out)) || (reinterpret_cast<uintptr_t>(index) & 7u) != 0)
+    return fail(BP_ERR_MISALIGNED, "embed_rmsnorm needs 16-byte aligned rows, cols and strides multiples of 8");
+  int st = require_sm100();
+  if (st != BP_OK) return st;
+  NormArgs<__nv_bfloat16> a{static_cast<const __nv_bfloat16*>(table), ld_table, static_cast<const __nv_bfloat16*>(w), 1,
+                            nullptr, 0, static_cast<__nv_bfloat16*>(h_out), ldh, static_cast<__nv_bfloat16*>(y), ldy,
+                            rows, cols, eps, 0, 0, reinterpret_cast<const long long*>(index), table_rows};
+  const cudaError_t e = launch_norm<BP_NORM_PLAIN, __nv_bfloat16>(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "embed_rmsnorm launch: %s", cudaGetErrorString(e));
+  return check_launch("embed_rmsnorm");
 }
 
 extern "C" int bp_rmsnorm(const void* x, long long ldx, const void* w, void* y, long long ldy, int rows, int cols,

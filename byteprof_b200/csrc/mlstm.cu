@@ -206,6 +206,12 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
   __shared__ float hb[2][kBV];
   extern __shared__ __align__(16) float cst[];  // [DQ x 16] C staging (stage_word layout) when a.stage_c
 
+  // Everything the scan reads (state, q, k, v, gates, the step count) may come from the kernels before it.
+  // The next kernel launches when the scan exits, not earlier: an early launch_dependents let the next
+  // weight stream start during the scan and made a local decode step 2-5 us slower (measured A/B), as its
+  // loads queue beside the scan's latency-bound state reads.
+  pdl_wait_prior_grids();
+
   const int head = blockIdx.y;
   const int c0 = blockIdx.x * kBV;
   const int tid = threadIdx.x;
@@ -418,6 +424,8 @@ __global__ void __launch_bounds__(ScanCfg<DQ, T>::NTHREADS) mlstm_scan_kernel(co
 }
 
 __global__ void accept_kernel(const int64_t* ids, const int64_t* tok, int64_t* out, int S, int smax) {
+  pdl_launch_dependents();
+  pdl_wait_prior_grids();
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int64_t alive = 1, n = 0;
   for (int j = 0; j < S - 1; ++j) {
@@ -444,6 +452,8 @@ struct CommitArgs {
 };
 
 __global__ void __launch_bounds__(256) commit_state_kernel(const CommitArgs a) {
+  pdl_launch_dependents();
+  pdl_wait_prior_grids();
   const long long slot = a.slot_bytes == 8 ? *static_cast<const long long*>(a.slot)
                                            : static_cast<long long>(*static_cast<const int*>(a.slot));
   const bool ok = slot >= 0 && slot < a.slots;
@@ -491,8 +501,16 @@ int launch_scan(const ScanArgs& a, cudaStream_t s) {
     const int st = allow_dynamic_smem(mlstm_scan_kernel<DQ, T>, smem, attr_done);
     if (st != BP_OK) return st;
   }
-  mlstm_scan_kernel<DQ, T><<<grid, Cfg::NTHREADS, smem, s>>>(a);
-  return check_launch("mlstm scan launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(Cfg::NTHREADS, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  set_launch_attrs(cfg, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, mlstm_scan_kernel<DQ, T>, a);
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "mlstm scan launch: %s", cudaGetErrorString(e));
+  return BP_OK;
 }
 
 template <typename T>
@@ -558,8 +576,15 @@ extern "C" int bp_mlstm_accept(const int64_t* ids, const int64_t* tok, int64_t* 
   if (ids == nullptr || tok == nullptr || out == nullptr) return fail(BP_ERR_INVALID_ARGUMENT, "NULL pointer");
   int st = require_sm100();
   if (st != BP_OK) return st;
-  accept_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(ids, tok, out, S, smax);
-  return check_launch("accept launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(32, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  set_launch_attrs(cfg, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, accept_kernel, ids, tok, out, S, smax);
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "accept launch: %s", cudaGetErrorString(e));
+  return BP_OK;
 }
 
 // Counterpart of byteprof/optim/draft_core.py:92-111 (commit_state and its Triton commit_kernel,
@@ -592,6 +617,13 @@ extern "C" int bp_mlstm_commit_state(const float* c_hist, const float* n_hist, c
   most = most > m_count ? most : m_count;
   long long blocks = (most / (a.vec ? 4 : 1) + 255) / 256;
   blocks = blocks < 1 ? 1 : (blocks > 4 * 148 ? 4 * 148 : blocks);
-  commit_state_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  return check_launch("commit state launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(blocks), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[2];
+  set_launch_attrs(cfg, attr);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, commit_state_kernel, a);
+  if (e != cudaSuccess) return fail(BP_ERR_CUDA, "commit state launch: %s", cudaGetErrorString(e));
+  return BP_OK;
 }

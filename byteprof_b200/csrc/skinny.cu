@@ -124,6 +124,8 @@ __global__ void __launch_bounds__(kThreads) skinny_fma_kernel(const SkinnyArgs a
   const WT* __restrict__ w = static_cast<const WT*>(a.w);
   const XT* __restrict__ x = static_cast<const XT*>(a.x);
 
+  pdl_launch_dependents();
+
   float acc[R][M];
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -148,6 +150,7 @@ __global__ void __launch_bounds__(kThreads) skinny_fma_kernel(const SkinnyArgs a
 #pragma unroll
       for (int r = 0; r < R; ++r) buf[u][r] = (rv[r] && k < ke) ? ldg_stream16(wr[r] + k, pol) : make_uint4(0, 0, 0, 0);
     }
+    pdl_wait_prior_grids();  // the weights above are constants; x may come from the kernel before
     for (int kk = k0; kk < ke; kk += U * KW) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(kThreads) skinny_fma_kernel(const SkinnyArgs a
     }
   } else {
     // Element-wise path for rows that are not 16-byte aligned (odd K): correctness, not speed.
+    pdl_wait_prior_grids();
     for (int k = kb + lane; k < ke; k += 32) {
       float xf[M];
 #pragma unroll
@@ -286,18 +290,8 @@ int launch_rows(SkinnyArgs a, bool vec, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads, 1, 1);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  if (S > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = S;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  } else {
-    cfg.attrs = nullptr;
-    cfg.numAttrs = 0;
-  }
+  cudaLaunchAttribute attr[2];
+  set_launch_attrs(cfg, attr, S);
   cudaError_t e;
   if (vec)
     e = cudaLaunchKernelEx(&cfg, skinny_fma_kernel<WT, M, R, U, true, XT>, a);

@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(kThreads / R) skinny_i4_kernel(const I4Args a)
   const int plen = padded_len(a.gb);
   float* xsum = xs + M * plen;
   const int ntiles = (a.N + kTileRows - 1) / kTileRows;  // row tiles the packed tensor holds
+  pdl_launch_dependents();
 
   // this lane's 16 bytes of group g of row r: ((t G + g) 32 + rr) 64 + 16 c (padding rows of a tile are
   // zero). A row past the last tile reads the last tile instead (valid memory; its scale is 0 and its
@@ -131,6 +132,7 @@ __global__ void __launch_bounds__(kThreads / R) skinny_i4_kernel(const I4Args a)
   };
 #pragma unroll
   for (int u = 0; u < U - 1; ++u) fetch(g0 + u, u);
+  pdl_wait_prior_grids();  // the weights above are constants; x may come from the kernel before
 
   int bb = g0;  // first group of the staged batch
   for (int gg = g0; gg < g1; gg += U) {
@@ -295,16 +297,8 @@ int launch_i4(I4Args a, cudaStream_t st) {
   cfg.blockDim = dim3(kThreads / R, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  cfg.numAttrs = 0;
-  if (S > 1) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 1;
-    attr[0].val.clusterDim.y = S;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-  }
+  cudaLaunchAttribute attr[2];
+  set_launch_attrs(cfg, attr, S);
   const cudaError_t e = cudaLaunchKernelEx(&cfg, skinny_i4_kernel<M, U, R>, a);
   if (e != cudaSuccess)
     return fail(BP_ERR_CUDA, "int4 skinny launch (M=%d N=%d K=%d split=%d): %s", M, a.N, a.K, S, cudaGetErrorString(e));

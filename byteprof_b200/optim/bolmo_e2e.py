@@ -32,7 +32,8 @@ from __future__ import annotations
 import torch
 
 from .bolmo_local import LocalLayer, rmsnorm
-from .decode_ops import DecodeAttention, GlobStep, LocStep, add_norm, decode_finish, norm_add, rope_tables, swiglu
+from .decode_ops import (DecodeAttention, GlobStep, LocStep, add_norm, decode_finish, embed_rmsnorm, norm_add,
+                         rope_tables, swiglu)
 from .skinny import skinny_mm
 
 EPS = 1e-6
@@ -141,13 +142,14 @@ class BolmoDecoder:
             self.enc_kernel.enc(parity, self.embed, self.byte, self.enc_norm, self.w_patch, self.w_boundary, self.e,
                                 self.patch, self.boundary_logit)
             return
-        h = self.embed.index_select(0, self.byte)
-        if self.act != h.dtype:
-            h = h.to(self.act)
-        _, e = self.enc.step(h, rmsnorm(h, self.enc.norm1, EPS), parity, out_norm=self.enc_norm, want_sum=False)
-        self.e.copy_(e)
-        skinny_mm(e, self.w_patch, out=self.patch)
-        skinny_mm(e, self.w_boundary, out=self.boundary_logit)
+        if self.act == torch.bfloat16:
+            h, x = embed_rmsnorm(self.embed, self.byte, self.enc.norm1, EPS)
+        else:
+            h = self.embed.index_select(0, self.byte).to(self.act)
+            x = rmsnorm(h, self.enc.norm1, EPS)
+        self.enc.step(h, x, parity, out_norm=self.enc_norm, want_sum=False, out=self.e)
+        skinny_mm(self.e, self.w_patch, out=self.patch)
+        skinny_mm(self.e, self.w_boundary, out=self.boundary_logit)
 
     def glob_step(self) -> None:
         if self.glob_kernel is not None:

@@ -101,7 +101,8 @@ class LocalLayer:
         q, k, v = (y[:, j * d:(j + 1) * d].view(s, nh, dh) for j in range(3))
         return y, q, k, v, g[:, :nh].reshape(s, nh, 1), g[:, nh:].reshape(s, nh, 1)
 
-    def _tail(self, h: torch.Tensor, y: torch.Tensor, s: int, out_norm: torch.Tensor | None, want_sum: bool):
+    def _tail(self, h: torch.Tensor, y: torch.Tensor, s: int, out_norm: torch.Tensor | None, want_sum: bool,
+              out: torch.Tensor | None = None):
         d, eps = self.d, self.norm_eps
         z = norm_gate(self.hbuf[:s], y[:, 3 * d:], self.mh_norm, eps,
                       out=torch.empty(s, d, dtype=self.act, device=h.device))
@@ -109,7 +110,7 @@ class LocalLayer:
         dn = skinny_mm(swiglu(skinny_mm(x2, self.w_gu)), self.w_down)
         if out_norm is None:
             return h2 + dn, None
-        return norm_add(dn, h2, out_norm, eps, want_sum)
+        return norm_add(dn, h2, out_norm, eps, want_sum, out=out)
 
     def forward(self, h: torch.Tensor, x: torch.Tensor | None = None, out_norm: torch.Tensor | None = None,
                 want_sum: bool = True):
@@ -131,13 +132,13 @@ class LocalLayer:
         draft_fused.lazy_commit(self.state, k, v, i_pre, f_pre, length, self.nstart, self.mstart)
 
     def step(self, h: torch.Tensor, x: torch.Tensor, parity: int, out_norm: torch.Tensor | None = None,
-             want_sum: bool = True):
+             want_sum: bool = True, out: torch.Tensor | None = None):
         """One position ([1, d]) of the decode loop; the state advances (n, m from buffer `parity` to
-        buffer 1 - parity). Returns as `forward`."""
+        buffer 1 - parity). Returns as `forward` (the normalised output into `out` when given)."""
         y, q, k, v, i_pre, f_pre = self._project(x)
         mlstm_scan(self.current_state(parity), q, k, v, i_pre, f_pre, self.hbuf, self.current_state(1 - parity),
                    self.mlstm_eps)
-        return self._tail(h, y, 1, out_norm, want_sum)
+        return self._tail(h, y, 1, out_norm, want_sum, out)
 
 
 class BolmoLocal:

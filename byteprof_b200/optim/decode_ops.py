@@ -2,6 +2,7 @@
 
 They replace the chains of small torch ops that byteprof's minimal Bolmo loop runs between its
 GEMMs (byteprof/optim/bolmo.py:32-136, bolmo_loop.py:36-64):
+  * embed_rmsnorm(t, i, w)   h = t[i], returns (h, rmsnorm(h) * w)             (byte embedding + first norm)
   * norm_add(x, res, w)      h = bf16(x + res), returns (h, rmsnorm(h) * w)   (pre-norm residual add)
   * add_norm(x, res, w)      res + rmsnorm(x) * w                              (OLMo-2 norm-after block)
   * norm_gate(h, o, w)       sigmoid(o) * rmsnorm(h) * w per head              (mLSTM output gate)
@@ -74,11 +75,32 @@ def rmsnorm_ex(x: torch.Tensor, w: torch.Tensor, eps: float, mode: int = NORM_PL
     return y
 
 
+def embed_rmsnorm(table: torch.Tensor, index: torch.Tensor, w: torch.Tensor, eps: float,
+                  h_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(h, n) with h = table[index] (bf16 [rows, cols], index int64 [rows] on the device) and n = rmsnorm(h) * w,
+    in one launch; an index outside the table gives NaN rows."""
+    if index.dtype != torch.int64 or index.dim() != 1 or not index.is_contiguous():
+        raise ValueError("index must be a contiguous int64 vector")
+    rows, cols = index.numel(), table.shape[1]
+    _, ldt = _rows(table)
+    h = h_out if h_out is not None else torch.empty(rows, cols, dtype=table.dtype, device=table.device)
+    y = out if out is not None else torch.empty(rows, cols, dtype=table.dtype, device=table.device)
+    _bf16(table, w, h, y)
+    if w.numel() != cols or h.shape != (rows, cols) or y.shape != (rows, cols):
+        raise ValueError("w must hold cols values and h_out, out must be [rows, cols]")
+    _lib.require_cuda(table, index, w, h, y)
+    with _lib.on_device(table):
+        _lib.call("bp_embed_rmsnorm", table.data_ptr(), ldt, table.shape[0], index.data_ptr(), w.data_ptr(),
+                  h.data_ptr(), _rows(h)[1], y.data_ptr(), _rows(y)[1], rows, cols, eps, _lib.stream_of(table))
+    return h, y
+
+
 def norm_add(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float,
-             want_sum: bool = True) -> tuple[torch.Tensor | None, torch.Tensor]:
-    """(h, n) with h = x + res (rounded to x's dtype) and n = rmsnorm(h) * w; res may be one row (broadcast)."""
+             want_sum: bool = True, out: torch.Tensor | None = None) -> tuple[torch.Tensor | None, torch.Tensor]:
+    """(h, n) with h = x + res (rounded to x's dtype) and n = rmsnorm(h) * w; res may be one row (broadcast).
+    n goes to `out` when given."""
     s = torch.empty_like(x) if want_sum else None
-    return s, rmsnorm_ex(x, w, eps, NORM_ADD_FIRST, res=res, s_out=s)
+    return s, rmsnorm_ex(x, w, eps, NORM_ADD_FIRST, res=res, s_out=s, out=out)
 
 
 def add_norm(x: torch.Tensor, res: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:

@@ -18,7 +18,7 @@
  *                       byteprof/optim/draft_core.py:114-141     mlstm_step_into (library step)
  *   bp_mlstm_accept     byteprof/optim/mlstm_multistep.py:136-146 accept_kernel
  *   bp_mlstm_commit_state byteprof/optim/draft_core.py:92-111  commit_state (+ draft_kernels.py commit_kernel)
- *   bp_rmsnorm_ex, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish, bp_glob_step,
+ *   bp_rmsnorm_ex, bp_embed_rmsnorm, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish, bp_glob_step,
  *   bp_loc_enc_step, bp_loc_dec_step
  *                       the per-byte pieces of the minimal Bolmo loop: byteprof/optim/bolmo.py:32-136
  *                       (_layer_step, LocalLoop.enc_step / dec_step, GlobalStep.step) and
@@ -178,6 +178,17 @@ enum { BP_NORM_PLAIN = 0, BP_NORM_ADD_FIRST = 1, BP_NORM_ADD_AFTER = 2, BP_NORM_
 int bp_rmsnorm_ex(const void* x, long long ldx, const void* w, int w_rows, const void* res, long long ldres,
                   void* s_out, long long lds, void* y, long long ldy, int rows, int cols, float eps, int mode,
                   int dtype, void* stream);
+
+/*
+ * Embedding lookup + RMSNorm, bf16: h_out[r] = table[index[r]] (h_out may be NULL) and
+ * y[r] = bf16(h_out[r] * rsqrt(mean(h_out[r]^2) + eps) * w) for r < rows; index int64 on the device, an
+ * index outside [0, table_rows) gives NaN rows. cols and strides multiples of 8, 16-byte aligned bases.
+ * Replaces the byte embedding of the local encoder and its layer's first norm (byteprof/optim/bolmo.py:
+ * 82-90, LocalLoop.enc_step: enc._embed, then the layer's pre-norm) in one launch. Added with ABI
+ * version 201.
+ */
+int bp_embed_rmsnorm(const void* table, long long ld_table, long long table_rows, const int64_t* index, const void* w,
+                     void* h_out, long long ldh, void* y, long long ldy, int rows, int cols, float eps, void* stream);
 
 /*
  * SwiGLU: out[r, j] = bf16(bf16(silu(gu[r, j])) * gu[r, ffn + j]) for j < ffn (gate | up halves of one

@@ -31,6 +31,28 @@ def test_plain_mode_is_bp_rmsnorm_bit_for_bit(rows, cols):
     _close(y, bolmo_ref.rmsnorm(to_np(x), to_np(w), EPS))
 
 
+@pytest.mark.parametrize("rows,cols", [(1, 2048), (3, 2048), (2, 10240)])
+def test_embed_rmsnorm_is_gather_then_norm(rows, cols):
+    table = randn(512, cols, seed=21)
+    w = randn(cols, seed=22, scale=0.1) + 1
+    idx = torch.tensor([7, 511, 0][:rows], dtype=torch.long, device="cuda")
+    h, y = ops.embed_rmsnorm(table, idx, w, EPS)
+    g = table.index_select(0, idx)
+    assert torch.equal(h, g)
+    assert torch.equal(y, ops.rmsnorm_ex(g, w, EPS))  # the same kernel and order as the plain norm
+    _close(y, bolmo_ref.rmsnorm(to_np(g), to_np(w), EPS))
+
+
+def test_embed_rmsnorm_index_outside_the_table_gives_nan_rows():
+    table = randn(16, 2048, seed=23)
+    w = randn(2048, seed=24, scale=0.1) + 1
+    idx = torch.tensor([3, 16, -1], dtype=torch.long, device="cuda")
+    h, y = ops.embed_rmsnorm(table, idx, w, EPS)
+    assert torch.equal(h[0], table[3])
+    assert torch.isnan(h[1:]).all() and torch.isnan(y[1:]).all()
+    assert not torch.isnan(y[0]).any()
+
+
 @pytest.mark.parametrize("rows", [1, 7])
 def test_norm_add_against_the_oracle(rows):
     x, res = randn(rows, 2048, seed=3), randn(rows, 2048, seed=4, scale=3.0)
