@@ -1,8 +1,8 @@
 // Machinery shared by the persistent decode kernels (glob_step.cu: the global-model step; loc_step.cu:
 // the local encoder and decoder steps): one CTA per SM (cooperative launch), 8 consumer warps and one
 // producer warp; the producer streams this CTA's weight rows in 16 KB 1-D bulk copies through a 12-slot
-// shared-memory ring (each chunk requested into L2 kPrefetchAhead chunks before its copy); the consumers
-// run the phases of the step, separated by grid barriers on one monotonic arrival counter.
+// shared-memory ring; the consumers run the phases of the step, separated by grid barriers on one
+// monotonic arrival counter.
 //
 // Every wait is bounded: a ring wait or a grid barrier that has not completed after kWaitLimitNs sets the
 // CTA's abort flag, the grid's abort word and the device error flag; every CTA then leaves once the bulk
@@ -20,7 +20,6 @@ constexpr int kConsumers = kConsumerWarps * 32;  // 256
 constexpr int kThreads = kConsumers + 32;        // + the producer warp
 constexpr int kSlots = 12;
 constexpr int kSlotBytes = 16384;
-constexpr int kPrefetchAhead = 12;               // chunks requested into L2 ahead of their copy
 constexpr unsigned kFull = 0xffffffffu;
 
 // The ring and the CTA's control words; the first member of a kernel's shared-memory struct.
@@ -68,10 +67,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
       ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
       : "memory");
-}
-
-__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
-  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
 }
 
 __device__ __forceinline__ void unpack8(const uint4 v, float (&f)[8]) {
@@ -182,20 +177,16 @@ __device__ __forceinline__ bool grid_sync(Ring& r, unsigned* sync, unsigned& epo
   return r.bad == 0;
 }
 
-// The producer: chunk k of `src` (src.chunk(k, bytes) -> global address) into the ring, k = 0 .. total-1,
-// each requested into L2 kPrefetchAhead chunks before its copy (requests run no farther ahead while the
-// ring is full: measured, that did not shorten the steps); then waits for every copy in flight.
+// The producer: chunk k of `src` (src.chunk(k, bytes) -> global address) into the ring, k = 0 .. total-1;
+// then waits for every copy in flight. No L2 prefetch ahead of the copies: with one prefetch per chunk the
+// producer issued a chunk every 0.54 us instead of 0.32 (per-CTA stamps), which bounded the global step
+// (682 against 621 us). Copying two contiguous chunks into neighbouring slots as one 32 KB operation did
+// not help either (634 us).
 template <typename Src>
 __device__ void produce(Ring& r, const Src& src, int total) {
   const uint64_t pol = l2_evict_first_policy();
-  int pf = 0;
   uint32_t i = 0;
   for (int k = 0; k < total; ++k) {
-    for (; pf < total && pf < k + kPrefetchAhead; ++pf) {
-      uint32_t nb;
-      const void* p = src.chunk(pf, nb);
-      prefetch_l2(p, nb);
-    }
     const uint32_t s = i % kSlots, use = i / kSlots;
     if (use > 0 && !mbar_wait(&r.empty[s], (use - 1) & 1u, &r.abort)) break;
     uint32_t bytes;

@@ -16,10 +16,12 @@ patch), the decoder, then one device-to-host read of (token, boundary flag): the
 Each byte is one CUDA graph launch (encoder + decoder, or encoder + global step + decoder). Every projection is a skinny GEMM of this library (M = 1), the mLSTM steps are
 the fused scan, and the glue between them is the fused kernels of `decode_ops`. By default the global
 step is one persistent kernel (decode_ops.GlobStep, csrc/glob_step.cu); fused_glob=False runs it kernel
-by kernel (GlobalBlock.step). fused_local=True runs each local step as one persistent kernel too
-(decode_ops.LocStep, csrc/loc_step.cu); it is off by default because on B200 it measures slower than the
-kernel-by-kernel local step (a persistent kernel cannot start streaming its weights before the previous
-piece has left the GPU, while each skinny GEMM starts under its predecessor).
+by kernel (GlobalBlock.step). fused_local chooses which local steps run as one persistent kernel
+(decode_ops.LocStep, csrc/loc_step.cu): "enc" (the default: the encoder step, 52 us against 57 kernel by
+kernel on B200), "dec", True (both) or False (neither). The decoder step stays kernel by kernel by
+default: its persistent form measures slower (62 us against 60), as a persistent kernel cannot start
+streaming its weights before the previous piece has left the GPU, while each skinny GEMM starts under its
+predecessor.
 
 precision="fp32" is the exactness mode: the same weights (bf16) with fp32 activations, fp32 KV caches
 and no rounding of any intermediate to bf16, kernel by kernel (skinny GEMMs read x as fp32, the glue
@@ -77,10 +79,12 @@ class BolmoDecoder:
     def __init__(self, device: torch.device | str = "cuda", seed: int = 0, d: int = 2048, vocab: int = 512,
                  local_heads: int = 4, local_dh: int = 512, local_ffn: int = 2816, global_layers: int = 16,
                  global_heads: int = 16, global_ffn: int = 8192, max_patches: int = 1024,
-                 rope_theta: float = 500000.0, fused_glob: bool = True, fused_local: bool = False,
+                 rope_theta: float = 500000.0, fused_glob: bool = True, fused_local: bool | str = "enc",
                  precision: str = "bf16"):
         if precision not in ("bf16", "fp32"):
             raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
+        if fused_local not in (False, True, "enc", "dec"):
+            raise ValueError(f"fused_local must be False, True, 'enc' or 'dec', got {fused_local!r}")
         act = torch.bfloat16 if precision == "bf16" else torch.float32
         if act == torch.float32:  # the persistent kernels run bf16 activations only
             fused_glob = fused_local = False
@@ -115,13 +119,14 @@ class BolmoDecoder:
         self.patches = 0  # patch positions used (host count)
         self._pin_byte = torch.zeros(1, dtype=torch.long).pin_memory()
         self._pin_out = torch.zeros(2, dtype=torch.long).pin_memory()
+        self._byte_np, self._out_np = self._pin_byte.numpy(), self._pin_out.numpy()  # host views, no torch ops
         # the global step as one persistent kernel, or kernel by kernel (GlobalBlock.step)
         self.fused_glob = fused_glob
         self.glob_kernel = GlobStep(self.blocks, self.dec_in_norm, self.cos, self.sin, max_patches, EPS) \
             if fused_glob else None
         # the local steps as one persistent kernel each, or kernel by kernel (LocalLayer.step)
-        self.enc_kernel = LocStep(self.enc) if fused_local else None
-        self.dec_kernel = LocStep(self.dec) if fused_local else None
+        self.enc_kernel = LocStep(self.enc) if fused_local in (True, "enc") else None
+        self.dec_kernel = LocStep(self.dec) if fused_local in (True, "dec") else None
 
     def weights(self) -> dict[str, torch.Tensor]:
         """Every parameter by name (the CPU oracle rebuilds the model from these)."""
@@ -187,14 +192,17 @@ class BolmoDecoder:
                 ("dec0", lambda: self.dec_step(0)), ("dec1", lambda: self.dec_step(1)))
 
     def _bytes(self):
-        """The whole work of one byte as one piece, per state parity: encoder and decoder, or encoder, global
-        step and decoder when the byte opens a patch (one graph launch per byte, no gaps between graphs)."""
+        """The whole work of one byte as one piece, per state parity: the byte's copy in from pinned memory,
+        encoder and decoder, or encoder, global step and decoder when the byte opens a patch, and the copy
+        of (token, boundary flag) out to pinned memory (one graph launch per byte, no gaps between graphs)."""
         def one(p: int, patch: bool):
             def fn():
+                self.byte.copy_(self._pin_byte, non_blocking=True)
                 self.enc_step(p)
                 if patch:
                     self.glob_step()
                 self.dec_step(p)
+                self._pin_out.copy_(self.out, non_blocking=True)
             return fn
         return tuple((f"{'patch' if patch else 'byte'}{p}", one(p, patch)) for p in (0, 1) for patch in (False, True))
 
@@ -217,32 +225,34 @@ class BolmoDecoder:
         self.reset()
 
     def launch(self, b: int, new_patch: bool) -> None:
-        """Queue one byte (encoder, the global model if a patch starts here, decoder); no sync."""
+        """Queue one byte (encoder, the global model if a patch starts here, decoder); no sync. The byte goes
+        through one pinned host word that the queued work reads when it runs, so synchronise (as `feed` does)
+        before the next launch."""
         if not 0 <= b < self.vocab:
             raise ValueError(f"byte id {b} outside the vocabulary")
         if new_patch and self.patches >= self.max_patches:
             raise RuntimeError(f"more than {self.max_patches} patches: the static KV cache is full")
         p = self.parity
-        self._pin_byte[0] = b
-        self.byte.copy_(self._pin_byte, non_blocking=True)
+        self._byte_np[0] = b
         whole = self.graphs.get(f"{'patch' if new_patch else 'byte'}{p}")
         if whole is not None:
-            whole.replay()
+            whole.replay()  # copies the byte in and (token, flag) out itself
         else:
+            self.byte.copy_(self._pin_byte, non_blocking=True)
             self.enc_step(p)
             if new_patch:
                 self.glob_step()
             self.dec_step(p)
+            self._pin_out.copy_(self.out, non_blocking=True)
         if new_patch:
             self.patches += 1
-        self._pin_out.copy_(self.out, non_blocking=True)
         self.parity = 1 - p
 
     def feed(self, b: int, new_patch: bool) -> tuple[int, bool]:
         """One byte, then the step's single synchronisation; returns (greedy token, boundary flag)."""
         self.launch(b, new_patch)
         torch.cuda.current_stream().synchronize()
-        return int(self._pin_out[0]), bool(self._pin_out[1])
+        return int(self._out_np[0]), bool(self._out_np[1])
 
     @torch.no_grad()
     def generate(self, prompt: list[int], n_new: int) -> tuple[list[int], list[bool]]:

@@ -38,8 +38,12 @@ def _restore(layer, snap):
         t.copy_(v)
 
 
+def _np(t):
+    return to_np(t) if torch.is_tensor(t) else np.asarray(t)
+
+
 def _stats(a, b):
-    a, b = to_np(a).ravel().astype(np.float64), to_np(b).ravel().astype(np.float64)
+    a, b = _np(a).ravel().astype(np.float64), _np(b).ravel().astype(np.float64)
     err = float(np.abs(a - b).max() / np.abs(b).max())
     corr = float(np.corrcoef(a, b)[0, 1])
     return err, corr
@@ -133,3 +137,56 @@ def test_a_byte_outside_the_vocabulary_writes_nan_and_leaves_the_state():
     assert torch.isnan(m.e.float()).all() and torch.isnan(m.patch.float()).all()
     assert torch.isnan(m.boundary_logit).all()
     assert all(torch.equal(a, b) for a, b in zip((*m.enc.state, *m.enc.nm[1]), snap))
+
+
+def _oracle_layer(m, layer, name):
+    from oracle import bolmo_ref
+    w = {k: to_np(v) for k, v in m.weights().items()}
+    ref = bolmo_ref.LocalLayer(w, name, layer.nh, layer.dh, layer.ffn)
+    c, n, mm = layer.current_state(0)
+    ref.state = (to_np(c[0]), to_np(n[0]), to_np(mm[0, :, 0]))
+    return w, ref
+
+
+@pytest.mark.parametrize("byte", [3, 200])
+def test_both_encoder_steps_against_the_oracle(byte):
+    """The persistent encoder step and the kernel-by-kernel one against the numpy oracle from the same weights
+    and state: the persistent kernel is no farther from the oracle than the kernel-by-kernel step (both differ
+    from it only in summation orders), on the outputs and on the new state."""
+    from oracle import bolmo_ref
+    m = _model(13)
+    w, ref = _oracle_layer(m, m.enc, "enc")
+    h = w["embed"][byte][None, :]
+    _, e = ref.step(h, bolmo_ref.rmsnorm(h, ref.w["norm1"], 1e-6), out_norm=w["enc_norm"])
+    want = {"e": e, "patch": bolmo_ref.linear(e, w["w_patch"]), "C": ref.state[0]}
+    snap = _snap(m.enc)
+    m.byte.fill_(byte)
+    got = {}
+    for fused in (False, True):
+        _restore(m.enc, snap)
+        _run(m, "enc", fused)
+        got[fused] = {"e": m.e.clone(), "patch": m.patch.clone(), "C": m.enc.state[0][0].clone()}
+    stats = {k: (_stats(got[False][k], want[k]), _stats(got[True][k], want[k])) for k in want}
+    print(byte, stats)
+    for k, ((e_kbk, c_kbk), (e_f, c_f)) in stats.items():
+        assert e_f <= max(1.5 * e_kbk, 0.01) and c_f >= min(c_kbk - 0.002, 0.999), (k, stats[k])
+
+
+def test_both_decoder_steps_against_the_oracle():
+    from oracle import bolmo_ref
+    m = _model(17)
+    w, ref = _oracle_layer(m, m.dec, "dec")
+    e, value = to_np(m.e), to_np(m.value)
+    hd, x = bolmo_ref.norm_add(bolmo_ref.linear(e, w["w_in"]), value, ref.w["norm1"], 1e-6)
+    _, xf = ref.step(hd, x, out_norm=w["final_norm"])
+    want = {"logits": bolmo_ref.linear(xf, w["lm_head"], bf16_out=False), "C": ref.state[0]}
+    snap = _snap(m.dec)
+    got = {}
+    for fused in (False, True):
+        _restore(m.dec, snap)
+        _run(m, "dec", fused)
+        got[fused] = {"logits": m.logits.clone(), "C": m.dec.state[0][0].clone()}
+    stats = {k: (_stats(got[False][k], want[k]), _stats(got[True][k], want[k])) for k in want}
+    print(stats)
+    for k, ((e_kbk, c_kbk), (e_f, c_f)) in stats.items():
+        assert e_f <= max(1.5 * e_kbk, 0.01) and c_f >= min(c_kbk - 0.002, 0.999), (k, stats[k])
