@@ -62,15 +62,116 @@ struct Args {
   const float* cos_t;
   const float* sin_t;
   float eps, scale;
-  __nv_bfloat16* y;     // [3d]
-  float* part;          // [nh][kChunks][kPart]
-  __nv_bfloat16* o;     // [d]
-  __nv_bfloat16* a;     // [ffn]
-  __nv_bfloat16* dn;    // [d]
-  __nv_bfloat16* xres;  // [2][d]: block input x, by block parity
-  __nv_bfloat16* hres;  // [2][d]: h, by block parity
-  unsigned* sync;       // [0] barrier arrivals (grows during a launch), [2] abort
+  uint32_t* y;     // [3d] tagged (see st_tagged)
+  float* part;     // [nh][kChunks][kPart]
+  uint32_t* o;     // [d] tagged
+  uint32_t* a;     // [ffn] tagged
+  uint32_t* dn;    // [d] tagged
+  unsigned* sync;  // [0] barrier arrivals (grows during a launch), [2] abort, [8] launch number (kept)
 };
+
+// ---- tagged hand-offs ------------------------------------------------------------------------------
+// The outputs of the matrix-vector phases (y, o, a, dn) go to global memory as 32-bit words, the bf16 value
+// in the low half and a 16-bit tag naming the write (launch number and hand-off) in the high half, each
+// written by one relaxed store. The grid barrier between the phases is then only a wake-up signal (no
+// release fence: it waited 1.2-1.7 us for the SM's bulk copies in flight, measured with per-CTA stamps), and
+// a reader takes a word once it carries the expected tag, polling again in the rare case that the signal
+// overtook the data. (Polling the words alone, without the signal, was slower: 256 threads per SM spinning on
+// L2 loads delayed everything else.) Two writes to one word are at most a few hand-offs or one launch
+// apart, so their tags always differ, and a zero-filled workspace never holds a valid tag.
+__device__ __forceinline__ uint32_t hand_tag(unsigned seq, int t) { return 1u + (seq * 128u + t) % 65535u; }
+
+__device__ __forceinline__ void st_tagged(uint32_t* p, float v, uint32_t tag) {
+  const uint32_t w = (tag << 16) | static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
+  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
+}
+
+__device__ __forceinline__ uint4 ld_relaxed16(const uint32_t* p) {
+  uint4 r;
+  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p)
+               : "memory");
+  return r;
+}
+
+__device__ __forceinline__ uint32_t ld_relaxed4(const uint32_t* p) {
+  uint32_t r;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
+  return r;
+}
+
+// A failed tag wait: stop the grid (abort word; the device error flag when the wait timed out).
+__device__ __forceinline__ bool tag_wait_gives_up(unsigned* sync, unsigned long long t0) {
+  if (*reinterpret_cast<volatile unsigned*>(sync + 2) != 0u) return true;
+  if (globaltimer() - t0 > kWaitLimitNs) {
+    atomicExch(sync + 2, 1u);
+    atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
+    return true;
+  }
+  return false;
+}
+
+// The 8 tagged words at p (16-byte aligned), loaded already as u, v (so that a thread's loads are all in
+// flight at once), once all carry `tag`, as floats (loading them again while one is stale); false when the
+// step stops.
+__device__ bool take_tagged8(uint4 u, uint4 v, const uint32_t* p, uint32_t tag, float (&f)[8], unsigned* sync) {
+  auto ready = [&]() {
+    return ((u.x >> 16) == tag) & ((u.y >> 16) == tag) & ((u.z >> 16) == tag) & ((u.w >> 16) == tag) &
+           ((v.x >> 16) == tag) & ((v.y >> 16) == tag) & ((v.z >> 16) == tag) & ((v.w >> 16) == tag);
+  };
+  bool ok = true;
+  if (!ready()) {
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+      u = ld_relaxed16(p);
+      v = ld_relaxed16(p + 4);
+      if (ready()) break;
+      if ((it & 31u) == 0 && tag_wait_gives_up(sync, t0)) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  f[0] = __uint_as_float(u.x << 16); f[1] = __uint_as_float(u.y << 16);
+  f[2] = __uint_as_float(u.z << 16); f[3] = __uint_as_float(u.w << 16);
+  f[4] = __uint_as_float(v.x << 16); f[5] = __uint_as_float(v.y << 16);
+  f[6] = __uint_as_float(v.z << 16); f[7] = __uint_as_float(v.w << 16);
+  return ok;
+}
+
+__device__ __forceinline__ bool ld_tagged8(const uint32_t* p, uint32_t tag, float (&f)[8], unsigned* sync) {
+  return take_tagged8(ld_relaxed16(p), ld_relaxed16(p + 4), p, tag, f, sync);
+}
+
+// One tagged word (loaded already as u) as a float, once it carries `tag`; false when the step stops.
+__device__ bool take_tagged1(uint32_t u, const uint32_t* p, uint32_t tag, float& f, unsigned* sync) {
+  bool ok = true;
+  if ((u >> 16) != tag) {
+    const unsigned long long t0 = globaltimer();
+    for (uint32_t it = 1;; ++it) {
+      u = ld_relaxed4(p);
+      if ((u >> 16) == tag) break;
+      if ((it & 31u) == 0 && tag_wait_gives_up(sync, t0)) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  f = __uint_as_float(u << 16);
+  return ok;
+}
+
+// Consumer barrier that stops the CTA when any consumer's wait failed (`bad`) or the ring stopped; a stop
+// also stops this CTA's producer and tells the other CTAs (the grid's abort word).
+__device__ __forceinline__ bool consumers_stop_if(Ring& r, unsigned* sync, bool bad) {
+  const bool stop = named_barrier_or(1, kConsumers, bad || r.abort != 0);
+  if (stop && threadIdx.x == 0) {
+    r.abort = 1;
+    atomicExch(sync + 2, 1u);
+  }
+  return stop;
+}
 
 struct Smem {
   Ring r;
@@ -84,24 +185,23 @@ struct Smem {
 };
 
 // out[e] = bf16(res[e] + bf16(src[e] * inv * w[e])) for this thread's 8 elements e = 8 t .. 8 t + 7 of a
-// d-vector, inv from the sum of squares of src (decode.cu's BP_NORM_ADD_AFTER with a 256-thread team).
-// src and res are read through L2 (written by other CTAs); the result goes to shared memory.
-__device__ void add_norm_vec(const __nv_bfloat16* src, const __nv_bfloat16* res, const __nv_bfloat16* w, float eps,
-                             Smem& s, float* red, bool res_global) {
+// d-vector, inv from the sum of squares of src (decode.cu's BP_NORM_ADD_AFTER with a 256-thread team). src
+// is a tagged hand-off, res this thread's 8 values; the result goes to shared memory and to `out`. Every
+// consumer reaches the CTA barrier inside, whether its wait succeeded or not; false when the step stops.
+__device__ bool add_norm_tagged(const uint32_t* src, uint32_t tag, const float (&res)[8], const __nv_bfloat16* w,
+                                float eps, Smem& s, float* red, unsigned* sync, float (&out)[8]) {
   const int e = threadIdx.x * 8;
-  float f[8], r[8], wv[8];
-  unpack8(ldcg16(src + e), f);
+  float f[8], wv[8];
+  const bool ok = ld_tagged8(src + e, tag, f, sync);
   float ss = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
   const float inv = inv_rms(consumer_sum(ss, red), kD, eps);
-  unpack8(res_global ? ldcg16(res + e) : *reinterpret_cast<const uint4*>(res + e), r);
   unpack8(ldg16(w + e), wv);
-  float o[8];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) o[j] = __fadd_rn(r[j], round_bf16(__fmul_rn(__fmul_rn(f[j], inv), wv[j])));
-  *reinterpret_cast<uint4*>(&s.vec[e]) =
-      make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  for (int j = 0; j < 8; ++j) out[j] = round_bf16(__fadd_rn(res[j], round_bf16(__fmul_rn(__fmul_rn(f[j], inv), wv[j]))));
+  *reinterpret_cast<uint4*>(&s.vec[e]) = pack8(out);
+  return ok;
 }
 
 // Row . vec for a bf16 row of 8192 in shared memory against the 8192-vector in s.vec.
@@ -123,9 +223,9 @@ __device__ __forceinline__ float dot8192(const uint8_t* row, const Smem& s) {
 }
 
 // Rows [r0, r1) of a K = 2048 weight, in 4-row ring chunks from chunk j0: warp w takes the chunks w,
-// w + 8, ... whole (one reader per chunk); out[row] = bf16(row . x). The warps run independently; a warp
-// whose wait fails (the CTA stops) leaves, and the end of the phase tells the others.
-__device__ uint32_t gemv2048(Smem& s, uint32_t j0, int r0, int r1, const float (&xr)[64], __nv_bfloat16* out) {
+// w + 8, ... whole (one reader per chunk); out[row] = bf16(row . x), tagged. The warps run independently; a
+// warp whose wait fails (the CTA stops) leaves, and the end of the phase tells the others.
+__device__ uint32_t gemv2048(Smem& s, uint32_t j0, int r0, int r1, const float (&xr)[64], uint32_t* out, uint32_t tag) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = (r1 - r0 + kRows2048 - 1) / kRows2048;
   for (int ch = warp; ch < nch; ch += kConsumerWarps) {
@@ -134,8 +234,7 @@ __device__ uint32_t gemv2048(Smem& s, uint32_t j0, int r0, int r1, const float (
     float v[kRows2048];
     dot4x2048(slot, xr, v);
     release(s.r, j0 + ch, 1);
-    if (lane < kRows2048 && r0 + ch * kRows2048 + lane < r1)
-      out[r0 + ch * kRows2048 + lane] = __float2bfloat16_rn(lane_row(v));
+    if (lane < kRows2048 && r0 + ch * kRows2048 + lane < r1) st_tagged(out + r0 + ch * kRows2048 + lane, lane_row(v), tag);
   }
   return j0 + nch;
 }
@@ -191,14 +290,17 @@ struct StreamSrc {
 };
 
 // ---- phase 2: one (head, chunk) unit of the attention ---------------------------------------------------
-__device__ void attention_unit(const Args& a, Smem& s, const Layer& L, int h, int chunk, long long p) {
+// q, k, v come from the tagged hand-off y (tag `tag`); false when the step stops (every consumer still
+// reaches the CTA barriers inside).
+__device__ bool attention_unit(const Args& a, Smem& s, const Layer& L, int h, int chunk, long long p, uint32_t tag) {
   constexpr int kHalf = kHd / 2;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int rounds = static_cast<int>(p / kRound) + 1;
   const bool own = static_cast<int>((p % kRound) / kSpan) == chunk;
-  const __nv_bfloat16* q = a.y;
-  const __nv_bfloat16* k = a.y + kD;
-  const __nv_bfloat16* v = a.y + 2 * kD;
+  const uint32_t* q = a.y;
+  const uint32_t* k = a.y + kD;
+  const uint32_t* v = a.y + 2 * kD;
+  bool ok = true;
   auto load_rows = [&](long long base, uint2 (&kk)[kPerWarp], uint2 (&vv)[kPerWarp]) {
 #pragma unroll
     for (int j = 0; j < kPerWarp; ++j) {
@@ -216,27 +318,44 @@ __device__ void attention_unit(const Args& a, Smem& s, const Layer& L, int h, in
   const int hi = h * kHd + (tid % kHalf);
   float cs = 0.0f, sn = 0.0f, qa = 0.0f, qb = 0.0f, qwa = 0.0f, qwb = 0.0f, ka = 0.0f, kb = 0.0f, kwa = 0.0f, kwb = 0.0f;
   float va = 0.0f, vb = 0.0f;
-  if (tid < kHalf) {
+  // every load of y this thread needs in flight at once, then the tag checks: this thread's 8 values of q
+  // and k (for the norms over d), and its rotary pair of q, k and its v pair of this head
+  const uint4 q0 = ld_relaxed16(q + tid * 8), q1 = ld_relaxed16(q + tid * 8 + 4);
+  const uint4 k0 = ld_relaxed16(k + tid * 8), k1 = ld_relaxed16(k + tid * 8 + 4);
+  const int vj = h * kHd + (tid - kHalf) * 2;
+  const bool rot = tid < kHalf, vown = !rot && own && tid < kHd;
+  uint32_t w0 = 0, w1 = 0, w2 = 0, w3 = 0;
+  if (rot) {
+    w0 = ld_relaxed4(q + hi);
+    w1 = ld_relaxed4(q + hi + kHalf);
+    if (own) {
+      w2 = ld_relaxed4(k + hi);
+      w3 = ld_relaxed4(k + hi + kHalf);
+    }
+  } else if (vown) {
+    w0 = ld_relaxed4(v + vj);
+    w1 = ld_relaxed4(v + vj + 1);
+  }
+  float fq[8], fk[8];
+  ok &= take_tagged8(q0, q1, q + tid * 8, tag, fq, a.sync);
+  ok &= take_tagged8(k0, k1, k + tid * 8, tag, fk, a.sync);
+  if (rot) {
     cs = a.cos_t[p * kHalf + tid];
     sn = a.sin_t[p * kHalf + tid];
-    qa = __bfloat162float(__ldcg(q + hi));
-    qb = __bfloat162float(__ldcg(q + hi + kHalf));
+    ok &= take_tagged1(w0, q + hi, tag, qa, a.sync);
+    ok &= take_tagged1(w1, q + hi + kHalf, tag, qb, a.sync);
     qwa = __bfloat162float(L.q_norm[hi]);
     qwb = __bfloat162float(L.q_norm[hi + kHalf]);
     if (own) {
-      ka = __bfloat162float(__ldcg(k + hi));
-      kb = __bfloat162float(__ldcg(k + hi + kHalf));
+      ok &= take_tagged1(w2, k + hi, tag, ka, a.sync);
+      ok &= take_tagged1(w3, k + hi + kHalf, tag, kb, a.sync);
       kwa = __bfloat162float(L.k_norm[hi]);
       kwb = __bfloat162float(L.k_norm[hi + kHalf]);
     }
-  } else if (own && tid < kHd) {
-    const int j = (tid - kHalf) * 2;
-    va = __bfloat162float(__ldcg(v + h * kHd + j));
-    vb = __bfloat162float(__ldcg(v + h * kHd + j + 1));
+  } else if (vown) {
+    ok &= take_tagged1(w0, v + vj, tag, va, a.sync);
+    ok &= take_tagged1(w1, v + vj + 1, tag, vb, a.sync);
   }
-  float fq[8], fk[8];
-  unpack8(ldcg16(q + tid * 8), fq);
-  unpack8(ldcg16(k + tid * 8), fk);
   float sq = 0.0f, sk = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
@@ -370,33 +489,45 @@ __device__ void attention_unit(const Args& a, Smem& s, const Layer& L, int h, in
     }
   }
   consumer_sync();  // shared scratch is reused by the next unit
+  return ok;
 }
 
 // ---- the consumers --------------------------------------------------------------------------------------
-__device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
+// Hand-offs of block l (tags hand_tag(seq, 4 l + i)): i = 0 y (qkv -> attention), 1 o (-> gate/up),
+// 2 a (-> down), 3 dn (-> the next block's qkv, or the final norm), each after a grid barrier without fence.
+// The partials of the attention go to the o phase through an ordered grid barrier (its fence is cheap
+// there: the ring is full and no copy is in flight).
+// Every CTA computes the block input x and the residual h itself and keeps its 8 values per thread.
+__device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, unsigned seq) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   unsigned epoch = 0;  // grid barriers passed (thread 0)
   uint32_t j = 0;  // ring chunk counter, in the producer's order
   float xr[64];
+  float xreg[8], hreg[8];  // x and h at elements 8 tid .. 8 tid + 7
   for (int l = 0; l < a.n_layers; ++l) {
     const Layer& L = a.L[l];
-    __nv_bfloat16* xres = a.xres + (l & 1) * kD;
+    const uint32_t tag_y = hand_tag(seq, 4 * l), tag_o = hand_tag(seq, 4 * l + 1), tag_a = hand_tag(seq, 4 * l + 2),
+                   tag_dn = hand_tag(seq, 4 * l + 3);
     // ---- 1: x and y = W_qkv x
+    bool ok = true;
     if (l == 0) {
-      *reinterpret_cast<uint4*>(&s.vec[tid * 8]) = ldg16(a.x_in + tid * 8);
+      const uint4 xv = ldg16(a.x_in + tid * 8);
+      unpack8(xv, xreg);
+      *reinterpret_cast<uint4*>(&s.vec[tid * 8]) = xv;
     } else {
-      add_norm_vec(a.dn, a.hres + ((l - 1) & 1) * kD, a.L[l - 1].mlp_norm, a.eps, s, s.r.red[0], true);
+      ok = add_norm_tagged(a.dn, hand_tag(seq, 4 * l - 1), hreg, a.L[l - 1].mlp_norm, a.eps, s, s.r.red[0], a.sync,
+                           xreg);
     }
-    consumer_sync();
-    if (c == 0) *reinterpret_cast<uint4*>(xres + tid * 8) = *reinterpret_cast<const uint4*>(&s.vec[tid * 8]);
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;  // also the CTA barrier after s.vec
     load_lane_x(s.vec, xr);
     int r0, r1;
     split(kQkvRows, G, c, r0, r1);
-    j = gemv2048(s, j, r0, r1, xr, a.y);
-    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch)) return;
+    j = gemv2048(s, j, r0, r1, xr, a.y, tag_y);
+    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch, false)) return;
     // ---- 2: attention
-    for (int u = c; u < kNH * kChunks; u += G) attention_unit(a, s, L, u / kChunks, u % kChunks, p);
-    if (!grid_sync(s.r, a.sync, epoch)) return;
+    ok = true;
+    for (int u = c; u < kNH * kChunks; u += G) ok &= attention_unit(a, s, L, u / kChunks, u % kChunks, p, tag_y);
+    if (consumers_stop_if(s.r, a.sync, !ok) || !grid_sync(s.r, a.sync, epoch)) return;
     // ---- 3: att (merge of the partials) and o = W_o att
     {
       const int e = tid * 8, h = e / kHd, dd = e % kHd;
@@ -427,12 +558,11 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
     consumer_sync();
     load_lane_x(s.vec, xr);
     split(kD, G, c, r0, r1);
-    j = gemv2048(s, j, r0, r1, xr, a.o);
-    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch)) return;
+    j = gemv2048(s, j, r0, r1, xr, a.o, tag_o);
+    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch, false)) return;
     // ---- 4: h = x + rmsnorm(o) * attn_norm; a = silu(W_gate h) * (W_up h)
-    add_norm_vec(a.o, xres, L.attn_norm, a.eps, s, s.r.red[0], true);
-    consumer_sync();
-    if (c == 0) *reinterpret_cast<uint4*>(a.hres + (l & 1) * kD + tid * 8) = *reinterpret_cast<const uint4*>(&s.vec[tid * 8]);
+    ok = add_norm_tagged(a.o, tag_o, xreg, L.attn_norm, a.eps, s, s.r.red[0], a.sync, hreg);
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;
     load_lane_x(s.vec, xr);
     split(kFfn, G, c, r0, r1);
     {
@@ -454,43 +584,58 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p) {
     for (int rl = tid; rl < r1 - r0; rl += kConsumers) {
       const float g = round_bf16(s.gbuf[rl]), up = round_bf16(s.ubuf[rl]);
       const float sl = round_bf16(static_cast<float>(g / (1.0 + exp(-static_cast<double>(g)))));
-      a.a[r0 + rl] = __float2bfloat16_rn(__fmul_rn(sl, up));
+      st_tagged(a.a + r0 + rl, __fmul_rn(sl, up), tag_a);
     }
-    if (!grid_sync(s.r, a.sync, epoch)) return;
+    if (!grid_sync(s.r, a.sync, epoch, false)) return;
     // ---- 5: dn = W_down a
+    ok = true;
+    {
+      constexpr int kGroups = kFfn / (kConsumers * 8);
+      uint4 ua[kGroups][2];  // all loads in flight, then the tag checks
 #pragma unroll
-    for (int i = 0; i < kFfn / (kConsumers * 8); ++i)
-      *reinterpret_cast<uint4*>(&s.vec[(i * kConsumers + tid) * 8]) = ldcg16(a.a + (i * kConsumers + tid) * 8);
-    consumer_sync();
+      for (int i = 0; i < kGroups; ++i) {
+        const uint32_t* pa = a.a + (i * kConsumers + tid) * 8;
+        ua[i][0] = ld_relaxed16(pa);
+        ua[i][1] = ld_relaxed16(pa + 4);
+      }
+#pragma unroll
+      for (int i = 0; i < kGroups; ++i) {
+        const int e = (i * kConsumers + tid) * 8;
+        float f[8];
+        ok &= take_tagged8(ua[i][0], ua[i][1], a.a + e, tag_a, f, a.sync);
+        *reinterpret_cast<uint4*>(&s.vec[e]) = pack8(f);
+      }
+    }
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;
     split(kD, G, c, r0, r1);
     for (int q = warp; q < r1 - r0; q += kConsumerWarps) {  // one row per chunk, one reader warp
       const uint8_t* slot = acquire(s.r, j + q);
       if (slot == nullptr) break;
       const float v = dot8192(slot, s);
-      if (lane == 0) a.dn[r0 + q] = __float2bfloat16_rn(v);
+      if (lane == 0) st_tagged(a.dn + r0 + q, v, tag_dn);
       release(s.r, j + q, 1);
     }
     j += r1 - r0;
-    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch)) return;
+    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch, false)) return;
   }
   // ---- value = rmsnorm(x_L) * out_norm, x_L = h + rmsnorm(dn) * mlp_norm of the last block
   if (c != 0) return;
   const int last = a.n_layers - 1;
-  add_norm_vec(a.dn, a.hres + (last & 1) * kD, a.L[last].mlp_norm, a.eps, s, s.r.red[0], true);
-  consumer_sync();
+  float xl[8];
+  const bool ok = add_norm_tagged(a.dn, hand_tag(seq, 4 * last + 3), hreg, a.L[last].mlp_norm, a.eps, s, s.r.red[0],
+                                  a.sync, xl);
+  if (consumers_stop_if(s.r, a.sync, !ok)) return;
   const int e = tid * 8;
-  float f[8], wv[8];
-  unpack8(*reinterpret_cast<const uint4*>(&s.vec[e]), f);
+  float wv[8];
   float ss = 0.0f;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+  for (int i = 0; i < 8; ++i) ss = fmaf(xl[i], xl[i], ss);
   const float inv = inv_rms(consumer_sum(ss, s.r.red[1]), kD, a.eps);
   unpack8(ldg16(a.out_norm + e), wv);
   float o[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(f[i], inv), wv[i]);
-  *reinterpret_cast<uint4*>(a.value_out + e) =
-      make_uint4(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]), pack_bf16x2(o[4], o[5]), pack_bf16x2(o[6], o[7]));
+  for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(xl[i], inv), wv[i]);
+  *reinterpret_cast<uint4*>(a.value_out + e) = pack8(o);
   if (tid == 0) *a.pos = p + 1;
 }
 
@@ -516,17 +661,18 @@ __global__ void __launch_bounds__(kThreads, 1) glob_step_kernel(Args a) {
     }
     return;
   }
-  consumers(a, s, c, G, p);
+  const unsigned seq = *reinterpret_cast<volatile unsigned*>(a.sync + 8);  // this launch's number (tags)
+  consumers(a, s, c, G, p, seq);
+  // CTA 0 finishes last (it reads every CTA's last output); every CTA read the number at its start
+  if (c == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.sync + 8) = seq + 1;
 }
 
-constexpr size_t kWsY = 0;
-constexpr size_t kWsPart = kWsY + 3 * kD * 2;
+constexpr size_t kWsY = 0;  // tagged hand-offs: 4 bytes per value
+constexpr size_t kWsPart = kWsY + 3 * kD * 4;
 constexpr size_t kWsO = kWsPart + static_cast<size_t>(kNH) * kChunks * kPart * 4;
-constexpr size_t kWsA = kWsO + kD * 2;
-constexpr size_t kWsDn = kWsA + kFfn * 2;
-constexpr size_t kWsX = kWsDn + kD * 2;
-constexpr size_t kWsH = kWsX + 2 * kD * 2;
-constexpr size_t kWsSync = kWsH + 2 * kD * 2;
+constexpr size_t kWsA = kWsO + kD * 4;
+constexpr size_t kWsDn = kWsA + kFfn * 4;
+constexpr size_t kWsSync = kWsDn + kD * 4;
 constexpr size_t kWsBytes = kWsSync + 256;
 
 }  // namespace
@@ -576,13 +722,11 @@ extern "C" int bp_glob_step(const bp_glob_layer* layers, int n_layers, const voi
   a.eps = eps;
   a.scale = 1.0f / sqrtf(static_cast<float>(kHd));
   char* ws = static_cast<char*>(workspace);
-  a.y = reinterpret_cast<__nv_bfloat16*>(ws + kWsY);
+  a.y = reinterpret_cast<uint32_t*>(ws + kWsY);
   a.part = reinterpret_cast<float*>(ws + kWsPart);
-  a.o = reinterpret_cast<__nv_bfloat16*>(ws + kWsO);
-  a.a = reinterpret_cast<__nv_bfloat16*>(ws + kWsA);
-  a.dn = reinterpret_cast<__nv_bfloat16*>(ws + kWsDn);
-  a.xres = reinterpret_cast<__nv_bfloat16*>(ws + kWsX);
-  a.hres = reinterpret_cast<__nv_bfloat16*>(ws + kWsH);
+  a.o = reinterpret_cast<uint32_t*>(ws + kWsO);
+  a.a = reinterpret_cast<uint32_t*>(ws + kWsA);
+  a.dn = reinterpret_cast<uint32_t*>(ws + kWsDn);
   a.sync = reinterpret_cast<unsigned*>(ws + kWsSync);
   int st = require_sm100();
   if (st != BP_OK) return st;
@@ -595,7 +739,7 @@ extern "C" int bp_glob_step(const bp_glob_layer* layers, int n_layers, const voi
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, glob_step_kernel, kThreads, smem);
   if (e != cudaSuccess || per_sm < 1) return fail(BP_ERR_CUDA, "glob_step does not fit on an SM");
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
-  e = cudaMemsetAsync(a.sync, 0, 16, s);  // arrival counter, abort word
+  e = cudaMemsetAsync(a.sync, 0, 16, s);  // arrival counter, abort word (the launch number stays)
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "glob_step sync reset: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sms);  // one CTA per SM, all resident (cooperative launch)

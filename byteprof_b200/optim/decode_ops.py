@@ -227,7 +227,8 @@ class GlobStep:
             self.layers[i] = _GlobLayer(*(t.data_ptr() for t in ts))
         self.out_norm, self.cos, self.sin, self.max_pos, self.eps = out_norm, cos, sin, max_pos, eps
         dev = out_norm.device
-        self.workspace = torch.empty(int(_lib.lib().bp_glob_step_workspace_bytes()), dtype=torch.uint8, device=dev)
+        # zero-filled once: it carries the kernel's launch number from one launch to the next
+        self.workspace = torch.zeros(int(_lib.lib().bp_glob_step_workspace_bytes()), dtype=torch.uint8, device=dev)
 
     def __call__(self, x: torch.Tensor, value_out: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         _bf16(x, value_out)

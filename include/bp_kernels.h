@@ -230,7 +230,9 @@ int bp_decode_attention(const void* qkv, const void* q_norm_w, const void* k_nor
  * Per layer: w_qkv [3d, d], q_norm [d], k_norm [d], w_o [d, d], attn_norm [d], w_gu [2 ffn, d] (gate rows,
  * then up rows), w_down [d, ffn], mlp_norm [d], k_cache / v_cache [max_pos, 16, 128]; all bf16, 16-byte
  * aligned. cos_t / sin_t fp32 [max_pos, 64]. workspace: the size bp_glob_step_workspace_bytes returns,
- * 16-byte aligned, no initial content. Results equal the kernel-by-kernel path (bp_skinny_mm, bp_decode_attention,
+ * 16-byte aligned, zero-filled before its first launch and not written by anything else afterwards (it
+ * carries a launch number from one launch to the next; ABI version 202 added this requirement). Calls
+ * sharing a workspace must not overlap. Results equal the kernel-by-kernel path (bp_skinny_mm, bp_decode_attention,
  * bp_rmsnorm_ex, bp_swiglu) up to the summation order of the matrix-vector products. Not capturable
  * together with other work that needs the SMs meanwhile (one CTA per SM, all resident). Replaces
  * GlobalStep.step (byteprof/optim/bolmo.py:100-136).
