@@ -241,8 +241,8 @@ __device__ uint32_t gemv2048(Smem& s, uint32_t j0, int r0, int r1, const float (
 
 // ---- the producer: this CTA's weight slices, in the consumers' order --------------------------------
 // Chunk k of this CTA's stream (the same sequence for every block): the qkv rows in 4-row chunks, the o
-// rows in 4-row chunks, then for each 4 gate rows the chunk of gate rows and the chunk of the same up
-// rows, then the down rows one per chunk.
+// rows in 4-row chunks, the gate rows in 4-row chunks, the same up rows in 4-row chunks (two contiguous
+// runs: 574 us per step against 585 with gate and up chunks alternating), then the down rows one per chunk.
 struct Stream {
   int q0, q1, o0, o1, g0, g1, d0, d1;  // this CTA's row ranges
   int nq, no, ng, nd, per_layer;       // chunks per segment and per block
@@ -273,9 +273,10 @@ struct Stream {
     }
     i -= no;
     if (i < ng) {
-      const int r = g0 + (i / 2) * kRows2048;
+      const int up = i >= ng / 2 ? 1 : 0;
+      const int r = g0 + (i - up * (ng / 2)) * kRows2048;
       bytes = min(kRows2048, g1 - r) * kD * 2;
-      return L.w_gu + static_cast<size_t>((i & 1) * kFfn + r) * kD;
+      return L.w_gu + static_cast<size_t>(up * kFfn + r) * kD;
     }
     i -= ng;
     bytes = kFfn * 2;
@@ -566,8 +567,8 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
     load_lane_x(s.vec, xr);
     split(kFfn, G, c, r0, r1);
     {
-      // chunk 2m: gate rows r0 + 4m .., chunk 2m + 1: the same up rows; warp w takes the chunks w,
-      // w + 8, ... whole
+      // chunk m < npairs: gate rows r0 + 4m .., chunk npairs + m: the same up rows; warp w takes the
+      // chunks w, w + 8, ... whole
       const int npairs = (r1 - r0 + kRows2048 - 1) / kRows2048;
       for (int ch = warp; ch < 2 * npairs; ch += kConsumerWarps) {
         const uint8_t* slot = acquire(s.r, j + ch);
@@ -575,8 +576,9 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
         float v[kRows2048];
         dot4x2048(slot, xr, v);
         release(s.r, j + ch, 1);
-        const int rl = (ch / 2) * kRows2048 + lane;
-        if (lane < kRows2048 && r0 + rl < r1) ((ch & 1) ? s.ubuf : s.gbuf)[rl] = lane_row(v);
+        const bool up = ch >= npairs;
+        const int rl = (up ? ch - npairs : ch) * kRows2048 + lane;
+        if (lane < kRows2048 && r0 + rl < r1) (up ? s.ubuf : s.gbuf)[rl] = lane_row(v);
       }
       j += 2 * npairs;
     }

@@ -189,17 +189,18 @@ __device__ __forceinline__ bool grid_sync(Ring& r, unsigned* sync, unsigned& epo
 // The producer: chunk k of `src` (src.chunk(k, bytes) -> global address) into the ring, k = 0 .. total-1;
 // then waits for every copy in flight. No L2 prefetch ahead of the copies: with one prefetch per chunk the
 // producer issued a chunk every 0.54 us instead of 0.32 (per-CTA stamps), which bounded the global step
-// (682 against 621 us). Copying two contiguous chunks into neighbouring slots as one 32 KB operation did
-// not help either (634 us).
+// (682 against 621 us). Measured and not kept either: copying two contiguous chunks into neighbouring
+// slots as one 32 KB operation (634 us), and requesting up to 12-48 chunks into L2 while the ring is full
+// (614-640 us, against 575).
 template <typename Src>
 __device__ void produce(Ring& r, const Src& src, int total) {
   const uint64_t pol = l2_evict_first_policy();
   uint32_t i = 0;
   for (int k = 0; k < total; ++k) {
     const uint32_t s = i % kSlots, use = i / kSlots;
-    if (use > 0 && !mbar_wait(&r.empty[s], (use - 1) & 1u, &r.abort)) break;
     uint32_t bytes;
-    const void* p = src.chunk(k, bytes);
+    const void* p = src.chunk(k, bytes);  // before the wait: the copy leaves as soon as the slot is free
+    if (use > 0 && !mbar_wait(&r.empty[s], (use - 1) & 1u, &r.abort)) break;
     mbar_arrive_expect_tx(&r.full[s], bytes);
     bulk_load(r.slot[s], p, bytes, &r.full[s], pol);
     *reinterpret_cast<volatile int*>(&r.issued[s]) = k;  // after the copy is on its way (see acquire)
