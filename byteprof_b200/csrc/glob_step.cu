@@ -35,6 +35,9 @@ namespace {
 
 using namespace persist;
 
+constexpr int kProducers = 1;
+constexpr int kThreads = threads_for(kProducers);
+
 constexpr int kD = 2048, kNH = 16, kHd = 128, kFfn = 8192;
 constexpr int kQkvRows = 3 * kD;
 constexpr int kChunks = 8;                        // attention position chunks per head
@@ -650,9 +653,9 @@ __global__ void __launch_bounds__(kThreads, 1) glob_step_kernel(Args a) {
   if (threadIdx.x == 0) ring_init(s.r);
   __syncthreads();
   if (threadIdx.x >= kConsumers) {
-    if (threadIdx.x == kConsumers) {
+    if ((threadIdx.x & 31) == 0) {
       const StreamSrc src{a, Stream(c, G)};
-      produce(s.r, src, valid ? src.st.per_layer * a.n_layers : 0);
+      produce<kProducers>(s.r, src, valid ? src.st.per_layer * a.n_layers : 0, (threadIdx.x - kConsumers) / 32);
     }
     return;
   }

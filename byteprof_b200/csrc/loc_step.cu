@@ -29,6 +29,9 @@ namespace {
 
 using namespace persist;
 
+constexpr int kProducers = 2;
+constexpr int kThreads = threads_for(kProducers);
+
 constexpr int kD = 2048, kNH = 4, kDh = 512, kFfn = 2816, kVocab = 512;
 constexpr int kQkvoRows = 4 * kD;
 constexpr int kCols = 16;                 // value columns per mLSTM unit
@@ -526,7 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1) loc_step_kernel(Args a) {
   if (threadIdx.x == 0) ring_init(s.r);
   __syncthreads();
   if (threadIdx.x >= kConsumers) {
-    if (threadIdx.x == kConsumers) produce(s.r, pl, valid ? pl.total() : 0);
+    if ((threadIdx.x & 31) == 0) produce<kProducers>(s.r, pl, valid ? pl.total() : 0, (threadIdx.x - kConsumers) / 32);
     return;
   }
   if (!valid) {  // host checks keep the byte in range; never index with a bad one

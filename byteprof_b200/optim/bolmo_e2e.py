@@ -17,11 +17,8 @@ Each byte is one CUDA graph launch (encoder + decoder, or encoder + global step 
 the fused scan, and the glue between them is the fused kernels of `decode_ops`. By default the global
 step is one persistent kernel (decode_ops.GlobStep, csrc/glob_step.cu); fused_glob=False runs it kernel
 by kernel (GlobalBlock.step). fused_local chooses which local steps run as one persistent kernel
-(decode_ops.LocStep, csrc/loc_step.cu): "enc" (the default: the encoder step, 52 us against 57 kernel by
-kernel on B200), "dec", True (both) or False (neither). The decoder step stays kernel by kernel by
-default: its persistent form measures slower (62 us against 60), as a persistent kernel cannot start
-streaming its weights before the previous piece has left the GPU, while each skinny GEMM starts under its
-predecessor.
+(decode_ops.LocStep, csrc/loc_step.cu): True (the default: both; on B200 the encoder step takes 46 us
+against 57 kernel by kernel, the decoder step 54 against 61), "enc", "dec" or False (neither).
 
 precision="fp32" is the exactness mode: the same weights (bf16) with fp32 activations, fp32 KV caches
 and no rounding of any intermediate to bf16, kernel by kernel (skinny GEMMs read x as fp32, the glue
@@ -79,7 +76,7 @@ class BolmoDecoder:
     def __init__(self, device: torch.device | str = "cuda", seed: int = 0, d: int = 2048, vocab: int = 512,
                  local_heads: int = 4, local_dh: int = 512, local_ffn: int = 2816, global_layers: int = 16,
                  global_heads: int = 16, global_ffn: int = 8192, max_patches: int = 1024,
-                 rope_theta: float = 500000.0, fused_glob: bool = True, fused_local: bool | str = "enc",
+                 rope_theta: float = 500000.0, fused_glob: bool = True, fused_local: bool | str = True,
                  precision: str = "bf16"):
         if precision not in ("bf16", "fp32"):
             raise ValueError(f"precision must be 'bf16' or 'fp32', got {precision!r}")
