@@ -294,6 +294,29 @@ struct StreamSrc {
 };
 
 // ---- phase 2: one (head, chunk) unit of the attention ---------------------------------------------------
+// A (head, chunk) unit has work when one of its positions is at most p: chunk c covers the positions
+// c kSpan + r kRound + [0, kSpan) of rounds r = 0 .. p / kRound. Units without any (c kSpan > p < kRound)
+// neither run nor write a partial; the merge skips their chunks (a partial of no position contributed
+// exactly nothing: m = -inf, weight 0).
+__device__ __forceinline__ bool chunk_active(int chunk, long long p) {
+  return p >= kRound || static_cast<long long>(chunk) * kSpan <= p;
+}
+
+// Requests into L2 the cache rows (k and v, head h) that unit (h, chunk) will read: the positions below p,
+// written by earlier steps, so the request can go out at the start of the block.
+__device__ void prefetch_unit_rows(const Layer& L, int h, int chunk, long long p) {
+  const int tid = threadIdx.x;
+  const int rounds = static_cast<int>(p / kRound) + 1;
+  for (int r = 0; r < rounds; ++r) {
+    const long long pos = static_cast<long long>(r) * kRound + chunk * kSpan + (tid >> 1);
+    if (tid < 2 * kSpan && pos < p) {
+      const long long off = (pos * kNH + h) * kHd + (tid & 1) * (kHd / 2);  // one 128-byte half of the row
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(L.kc + off));
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(L.vc + off));
+    }
+  }
+}
+
 // q, k, v come from the tagged hand-off y (tag `tag`); false when the step stops (every consumer still
 // reaches the CTA barriers inside).
 __device__ bool attention_unit(const Args& a, Smem& s, const Layer& L, int h, int chunk, long long p, uint32_t tag) {
@@ -322,8 +345,19 @@ __device__ bool attention_unit(const Args& a, Smem& s, const Layer& L, int h, in
   const int hi = h * kHd + (tid % kHalf);
   float cs = 0.0f, sn = 0.0f, qa = 0.0f, qb = 0.0f, qwa = 0.0f, qwb = 0.0f, ka = 0.0f, kb = 0.0f, kwa = 0.0f, kwb = 0.0f;
   float va = 0.0f, vb = 0.0f;
-  // every load of y this thread needs in flight at once, then the tag checks: this thread's 8 values of q
-  // and k (for the norms over d), and its rotary pair of q, k and its v pair of this head
+  // the rotary factors and norm weights first (they do not wait for y), then every load of y this thread
+  // needs in flight at once, then the tag checks: this thread's 8 values of q and k (for the norms over d),
+  // and its rotary pair of q, k and its v pair of this head
+  if (tid < kHalf) {
+    cs = a.cos_t[p * kHalf + tid];
+    sn = a.sin_t[p * kHalf + tid];
+    qwa = __bfloat162float(L.q_norm[hi]);
+    qwb = __bfloat162float(L.q_norm[hi + kHalf]);
+    if (own) {
+      kwa = __bfloat162float(L.k_norm[hi]);
+      kwb = __bfloat162float(L.k_norm[hi + kHalf]);
+    }
+  }
   const uint4 q0 = ld_relaxed16(q + tid * 8), q1 = ld_relaxed16(q + tid * 8 + 4);
   const uint4 k0 = ld_relaxed16(k + tid * 8), k1 = ld_relaxed16(k + tid * 8 + 4);
   const int vj = h * kHd + (tid - kHalf) * 2;
@@ -344,17 +378,11 @@ __device__ bool attention_unit(const Args& a, Smem& s, const Layer& L, int h, in
   ok &= take_tagged8(q0, q1, q + tid * 8, tag, fq, a.sync);
   ok &= take_tagged8(k0, k1, k + tid * 8, tag, fk, a.sync);
   if (rot) {
-    cs = a.cos_t[p * kHalf + tid];
-    sn = a.sin_t[p * kHalf + tid];
     ok &= take_tagged1(w0, q + hi, tag, qa, a.sync);
     ok &= take_tagged1(w1, q + hi + kHalf, tag, qb, a.sync);
-    qwa = __bfloat162float(L.q_norm[hi]);
-    qwb = __bfloat162float(L.q_norm[hi + kHalf]);
     if (own) {
       ok &= take_tagged1(w2, k + hi, tag, ka, a.sync);
       ok &= take_tagged1(w3, k + hi + kHalf, tag, kb, a.sync);
-      kwa = __bfloat162float(L.k_norm[hi]);
-      kwb = __bfloat162float(L.k_norm[hi + kHalf]);
     }
   } else if (vown) {
     ok &= take_tagged1(w0, v + vj, tag, va, a.sync);
@@ -523,6 +551,8 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
                            xreg);
     }
     if (consumers_stop_if(s.r, a.sync, !ok)) return;  // also the CTA barrier after s.vec
+    for (int u = c; u < kNH * kChunks; u += G)
+      if (chunk_active(u % kChunks, p)) prefetch_unit_rows(L, u / kChunks, u % kChunks, p);
     load_lane_x(s.vec, xr);
     int r0, r1;
     split(kQkvRows, G, c, r0, r1);
@@ -530,7 +560,8 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
     if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch, false)) return;
     // ---- 2: attention
     ok = true;
-    for (int u = c; u < kNH * kChunks; u += G) ok &= attention_unit(a, s, L, u / kChunks, u % kChunks, p, tag_y);
+    for (int u = c; u < kNH * kChunks; u += G)
+      if (chunk_active(u % kChunks, p)) ok &= attention_unit(a, s, L, u / kChunks, u % kChunks, p, tag_y);
     if (consumers_stop_if(s.r, a.sync, !ok) || !grid_sync(s.r, a.sync, epoch)) return;
     // ---- 3: att (merge of the partials) and o = W_o att
     {
@@ -539,12 +570,13 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
       float mc[kChunks], mg = -INFINITY;
 #pragma unroll
       for (int ch = 0; ch < kChunks; ++ch) {
-        mc[ch] = __ldcg(ph + ch * kPart);
+        mc[ch] = chunk_active(ch, p) ? __ldcg(ph + ch * kPart) : -INFINITY;
         mg = fmaxf(mg, mc[ch]);
       }
       float lg = 0.0f, og[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int ch = 0; ch < kChunks; ++ch) {
+        if (!chunk_active(ch, p)) continue;
         const float f = mc[ch] == -INFINITY ? 0.0f : expf(__fsub_rn(mc[ch], mg));
         lg = fmaf(__ldcg(ph + ch * kPart + 1), f, lg);
         const float4 o0 = __ldcg(reinterpret_cast<const float4*>(ph + ch * kPart + kPartO + dd));
