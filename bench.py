@@ -34,6 +34,7 @@ import time
 from datetime import timedelta
 from pathlib import Path
 
+import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parent
@@ -506,41 +507,75 @@ class TorchDecoder:
         torch.cuda.current_stream().synchronize()
         return int(self._out_np[0]), bool(self._out_np[1])
 
+    def steps(self, n, bytes_=None, patches=None, first_byte=0, first_patch=True):
+        """The same native per-byte loop as BolmoDecoder.steps, over this arm's two graphs."""
+        from byteprof_b200.optim.bolmo_e2e import native_steps
+
+        bytes_ = None if bytes_ is None else np.ascontiguousarray(bytes_, dtype=np.int64)
+        patches = None if patches is None else np.ascontiguousarray(patches, dtype=np.int32)
+        execs = [self.graphs[k].raw_cuda_graph_exec() for k in ("byte", "patch", "byte", "patch")]
+        tokens, flags, wall = native_steps(execs, self._pin_byte, self._pin_out, n, bytes_, patches, first_byte,
+                                           first_patch, 0, self.dev)
+        opened = patches.astype(bool).tolist() if patches is not None else \
+            ([bool(first_patch)] + [bool(f) for f in flags[:n - 1]])[:n]
+        self.patches += sum(opened)
+        return tokens.tolist(), [bool(f) for f in flags], opened, wall
+
 
 def _time_decode(m, seed: int, reps: int, replay: list | None = None, gaps: bool = False) -> dict:
     """Prompt of 256 random bytes fed byte by byte, then 511 greedy steps timed on the wall clock (each
     step ends with its host synchronisation); then (reps > 0) each graph replayed alone for its device time.
     `replay` = a (byte, opens a patch) sequence to feed instead of this model's own greedy choices, so that
     two implementations do exactly the same work; the model's own choice at every step is still recorded.
-    gaps: also the top-2 logit gap of every step that chose a generated byte (outside the timed loop's
-    numbers: it adds a read per step)."""
+    The steps run in the native per-byte loop (`steps`: bp_decode_loop). gaps: the loop in Python instead,
+    reading the top-2 logit gap of every step that chose a generated byte (that run is not timed)."""
     prompt = torch.randint(0, 256, (DECODE_PROMPT,), generator=torch.Generator().manual_seed(seed)).tolist()
     m.reset()
-    tok, new_patch, fed, gap = 0, True, [], []
+    gap = []
+    if gaps:
+        tok, new_patch, fed = 0, True, []
 
-    def top2():
-        if gaps:
+        def top2():
             top = torch.topk(m.logits[0], 2).values
             gap.append(float(top[0] - top[1]))
 
-    for i, b in enumerate(prompt):
-        if replay is not None:
-            b, new_patch = replay[i]
-        fed.append((b, new_patch))
-        tok, new_patch = m.feed(b, new_patch)
-    top2()
-    prompt_patches = m.patches
-    torch.cuda.synchronize()
-    gen = [tok]
-    t0 = time.perf_counter()
-    for i in range(DECODE_NEW - 1):
-        if replay is not None:
-            tok, new_patch = replay[DECODE_PROMPT + i]
-        fed.append((tok, new_patch))
-        tok, new_patch = m.feed(tok, new_patch)
-        gen.append(tok)
+        for i, b in enumerate(prompt):
+            if replay is not None:
+                b, new_patch = replay[i]
+            fed.append((b, new_patch))
+            tok, new_patch = m.feed(b, new_patch)
         top2()
-    wall = time.perf_counter() - t0
+        prompt_patches = m.patches
+        gen = [tok]
+        t0 = time.perf_counter()
+        for i in range(DECODE_NEW - 1):
+            if replay is not None:
+                tok, new_patch = replay[DECODE_PROMPT + i]
+            fed.append((tok, new_patch))
+            tok, new_patch = m.feed(tok, new_patch)
+            gen.append(tok)
+            top2()
+        wall = time.perf_counter() - t0
+    elif replay is not None:
+        fb = [b for b, _ in replay[:DECODE_PROMPT + DECODE_NEW - 1]]
+        fp = [p for _, p in replay[:DECODE_PROMPT + DECODE_NEW - 1]]
+        toks, _, _, _ = m.steps(DECODE_PROMPT, bytes_=fb[:DECODE_PROMPT], patches=fp[:DECODE_PROMPT])
+        prompt_patches = m.patches
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        tk, _, _, _ = m.steps(DECODE_NEW - 1, bytes_=fb[DECODE_PROMPT:], patches=fp[DECODE_PROMPT:])
+        wall = time.perf_counter() - t0
+        gen = [toks[-1]] + tk
+        fed = list(zip(fb, fp))
+    else:
+        toks, flags, opened, _ = m.steps(DECODE_PROMPT, bytes_=prompt, first_patch=True)
+        prompt_patches = m.patches
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        tk, _, op2, _ = m.steps(DECODE_NEW - 1, first_byte=toks[-1], first_patch=flags[-1])
+        wall = time.perf_counter() - t0
+        gen = [toks[-1]] + tk
+        fed = list(zip(prompt, opened)) + list(zip(gen[:-1], op2))
     per = {}
     if reps > 0:
         for name in ("enc0", "dec0", "glob"):
@@ -612,7 +647,8 @@ def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 2
         "work": ("the exactness mode's greedy bytes and patch starts (float64-equivalent), fed to both arms; "
                  "the model's own greedy choice is read at every step"),
         "graphs_per_byte": ("one graph per byte: byte copy in, enc + dec (or enc + glob + dec on a patch start), "
-                            "result copy out; one host sync per byte; the torch arm runs the same loop"),
+                            "result copy out; one host sync per byte in a native loop (bp_decode_loop); "
+                            "the torch arm runs the same loop over its own graphs"),
         "free_running": {"bytes_per_s": round(steps / free["wall"], 1),
                          "patches_in_timed_steps": free["gen_patches"],
                          "what": "the bf16 decoder's own greedy bytes and patch decisions"},

@@ -39,6 +39,8 @@ _SIGNATURES = {
     "bp_rmsnorm": (c_int, [c_void_p, c_longlong, c_void_p, c_void_p, c_longlong, c_int, c_int, c_float, c_void_p]),
     "bp_rmsnorm_ex": (c_int, [c_void_p, c_longlong, c_void_p, c_int, c_void_p, c_longlong, c_void_p, c_longlong,
                               c_void_p, c_longlong, c_int, c_int, c_float, c_int, c_int, c_void_p]),
+    "bp_decode_loop": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_longlong, c_int, c_int,
+                               c_void_p, c_void_p, c_void_p, c_void_p]),
     "bp_embed_rmsnorm": (c_int, [c_void_p, c_longlong, c_longlong, c_void_p, c_void_p, c_void_p, c_longlong,
                                  c_void_p, c_longlong, c_int, c_int, c_float, c_void_p]),
     "bp_swiglu": (c_int, [c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int, c_int, c_void_p]),

@@ -28,7 +28,12 @@ weights decodes, so it pins the whole model end to end; the default "bf16" mode 
 
 from __future__ import annotations
 
+import ctypes
+
+import numpy as np
 import torch
+
+from .. import _lib
 
 from .bolmo_local import LocalLayer, rmsnorm
 from .decode_ops import (DecodeAttention, GlobStep, LocStep, add_norm, decode_finish, embed_rmsnorm, norm_add,
@@ -251,18 +256,76 @@ class BolmoDecoder:
         torch.cuda.current_stream().synchronize()
         return int(self._out_np[0]), bool(self._out_np[1])
 
+    def steps(self, n: int, bytes_=None, patches=None, first_byte: int = 0, first_patch: bool = True):
+        """n bytes through the captured per-byte graphs in the native loop (bp_decode_loop), one synchronisation
+        per byte. Step i feeds bytes_[i] (or first_byte, then the previous step's greedy token) and opens a
+        patch when patches[i] (or first_patch, then the previous step's boundary flag). Returns (tokens,
+        boundary flags, patch starts fed, wall seconds of the loop)."""
+        if not self.graphs:
+            raise RuntimeError("steps() runs the captured graphs: call capture() first")
+        if bytes_ is not None:
+            bytes_ = np.ascontiguousarray(bytes_, dtype=np.int64)
+            if bytes_.shape != (n,) or (n and (bytes_.min() < 0 or bytes_.max() >= self.vocab)):
+                raise ValueError(f"bytes_ must hold n byte ids in [0, {self.vocab})")
+        elif not 0 <= first_byte < self.vocab:
+            raise ValueError(f"byte id {first_byte} outside the vocabulary")
+        if patches is not None:
+            patches = np.ascontiguousarray(patches, dtype=np.int32)
+            if patches.shape != (n,):
+                raise ValueError("patches must hold n flags")
+            need = int(patches.astype(bool).sum())
+        else:
+            need = n  # at most one patch per byte
+        if self.patches + need > self.max_patches:
+            raise RuntimeError(f"up to {self.patches + need} patches: more than the static KV cache's {self.max_patches}")
+        execs = [self.graphs[f"{kind}{p}"].raw_cuda_graph_exec() for p in (0, 1) for kind in ("byte", "patch")]
+        tokens, flags, wall = native_steps(execs, self._pin_byte, self._pin_out, n, bytes_, patches, first_byte,
+                                           first_patch, self.parity, self.device)
+        opened = patches.astype(bool).tolist() if patches is not None else \
+            ([bool(first_patch)] + [bool(f) for f in flags[:n - 1]])[:n]
+        self.patches += sum(opened)
+        self.parity ^= n & 1
+        return tokens.tolist(), [bool(f) for f in flags], opened, wall
+
     @torch.no_grad()
     def generate(self, prompt: list[int], n_new: int) -> tuple[list[int], list[bool]]:
         """Greedy decoding from the current state: the prompt bytes in order, then each predicted byte.
-        Returns the n_new generated bytes and, for every byte fed, whether it opened a patch."""
-        new_patch, opened, tok = True, [], 0
-        for b in prompt:
-            opened.append(new_patch)
-            tok, new_patch = self.feed(b, new_patch)
-        out = []
-        for i in range(n_new):
-            out.append(tok)
-            if i + 1 < n_new:
+        Returns the n_new generated bytes and, for every byte fed, whether it opened a patch. Runs the
+        captured graphs in the native loop when present, else byte by byte."""
+        if not self.graphs:
+            new_patch, opened, tok = True, [], 0
+            for b in prompt:
                 opened.append(new_patch)
-                tok, new_patch = self.feed(tok, new_patch)
+                tok, new_patch = self.feed(b, new_patch)
+            out = []
+            for i in range(n_new):
+                out.append(tok)
+                if i + 1 < n_new:
+                    opened.append(new_patch)
+                    tok, new_patch = self.feed(tok, new_patch)
+            return out, opened
+        toks, flags, opened, _ = self.steps(len(prompt), bytes_=prompt, first_patch=True)
+        if n_new <= 0:
+            return [], opened
+        out = [toks[-1]]
+        if n_new > 1:
+            gen, _, op2, _ = self.steps(n_new - 1, first_byte=toks[-1], first_patch=flags[-1])
+            out += gen
+            opened += op2
         return out, opened
+
+
+def native_steps(execs, pin_byte: torch.Tensor, pin_out: torch.Tensor, n: int, bytes_, patches, first_byte: int,
+                 first_patch: bool, parity: int, device) -> tuple[np.ndarray, np.ndarray, float]:
+    """bp_decode_loop over four graph execs (index 2 * parity + patch) whose first node copies the pinned
+    byte word in and whose last copies (token, flag) to the pinned pair. Returns (tokens, flags, wall s)."""
+    arr = (ctypes.c_void_p * 4)(*execs)
+    tokens = np.zeros(max(n, 1), np.int64)
+    flags = np.zeros(max(n, 1), np.int32)
+    wall = ctypes.c_double(0.0)
+    with torch.cuda.device(device):
+        _lib.call("bp_decode_loop", arr, pin_byte.data_ptr(), pin_out.data_ptr(),
+                  None if bytes_ is None else bytes_.ctypes.data, None if patches is None else patches.ctypes.data,
+                  n, int(first_byte), int(bool(first_patch)), int(parity), tokens.ctypes.data, flags.ctypes.data,
+                  torch.cuda.current_stream(device).cuda_stream, ctypes.byref(wall))
+    return tokens[:n], flags[:n], wall.value

@@ -249,6 +249,20 @@ typedef struct bp_glob_layer {
   void* k_cache;
   void* v_cache;
 } bp_glob_layer;
+/*
+ * The per-byte host loop of the byte decoder (no reference counterpart in C: byteprof/optim/bolmo_loop.py:
+ * 182-207 runs it in Python). graph_execs: four cudaGraphExec_t, index 2 * parity + patch, each running one
+ * whole byte: copy *byte_host in, the steps, copy (token, boundary flag) to out_host[0..1]. Step i feeds
+ * bytes[i] (or, when bytes is NULL, first_byte at step 0 and then the previous step's token) with patch
+ * start patches[i] (or first_patch, then the previous step's flag), launches the graph on `stream`, waits
+ * for it and stores the token and flag in tokens_out[i], flags_out[i]; parity alternates from `parity`.
+ * byte_host and out_host are pinned host memory; wall_seconds (may be NULL) gets the loop's wall time.
+ * Added with ABI version 203.
+ */
+int bp_decode_loop(void* const* graph_execs, int64_t* byte_host, const int64_t* out_host, const int64_t* bytes,
+                   const int32_t* patches, int n, int64_t first_byte, int32_t first_patch, int parity,
+                   int64_t* tokens_out, int32_t* flags_out, void* stream, double* wall_seconds);
+
 size_t bp_glob_step_workspace_bytes(void);
 int bp_glob_step(const bp_glob_layer* layers, int n_layers, const void* x_in, const void* out_norm, void* value_out,
                  int64_t* pos, const float* cos_t, const float* sin_t, int max_pos, float eps, void* workspace,

@@ -124,3 +124,33 @@ def test_benchmark_configuration_decode_tracks_the_oracle(model, ref):
     gen, opened = model.generate(prompt, 512)
     assert gen == fed[256:] + [rows[-1][0]]  # the free-running decode is the teacher-forced one
     assert sum(opened) == stats["patches"]
+
+
+def test_native_loop_equals_feeding_byte_by_byte():
+    """BolmoDecoder.steps (the per-byte loop in C++, bp_decode_loop) gives the tokens, flags and patch starts
+    of feed() byte by byte, from the same state, with given bytes and patches and with the model's own."""
+    m = BolmoDecoder(seed=3)
+    m.capture()
+    prompt = [int(b) for b in torch.randint(0, 256, (40,), generator=torch.Generator().manual_seed(4))]
+    m.reset()
+    want_tok, want_flag, opened, new_patch = [], [], [], True
+    for b in prompt:
+        opened.append(new_patch)
+        tok, new_patch = m.feed(b, new_patch)
+        want_tok.append(tok)
+        want_flag.append(new_patch)
+    for _ in range(20):  # greedy continuation
+        opened.append(new_patch)
+        tok, new_patch = m.feed(want_tok[-1], new_patch)
+        want_tok.append(tok)
+        want_flag.append(new_patch)
+    m.reset()
+    t1, f1, o1, _ = m.steps(len(prompt), bytes_=prompt, first_patch=True)
+    t2, f2, o2, _ = m.steps(20, first_byte=t1[-1], first_patch=f1[-1])
+    assert t1 + t2 == want_tok and f1 + f2 == want_flag and o1 + o2 == opened
+    assert m.patches == sum(opened)
+    # forced bytes and patches: the same run again
+    m.reset()
+    fed = prompt + want_tok[len(prompt) - 1:-1]
+    t3, f3, o3, _ = m.steps(len(fed), bytes_=fed, patches=[int(x) for x in opened])
+    assert t3 == want_tok and f3 == want_flag and o3 == opened
