@@ -526,7 +526,9 @@ __device__ bool attention_unit(const Args& a, Smem& s, const Layer& L, int h, in
 
 // ---- the consumers --------------------------------------------------------------------------------------
 // Hand-offs of block l (tags hand_tag(seq, 4 l + i)): i = 0 y (qkv -> attention), 1 o (-> gate/up),
-// 2 a (-> down), 3 dn (-> the next block's qkv, or the final norm), each after a grid barrier without fence.
+// 2 a (-> down), 3 dn (-> the next block's qkv, or the final norm), each after a grid barrier without fence,
+// except y: only the (at most 128) active attention units read it, and they poll its words directly (557
+// against 571 us per step with the signal).
 // The partials of the attention go to the o phase through an ordered grid barrier (its fence is cheap
 // there: the ring is full and no copy is in flight).
 // Every CTA computes the block input x and the residual h itself and keeps its 8 values per thread.
@@ -557,8 +559,8 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
     int r0, r1;
     split(kQkvRows, G, c, r0, r1);
     j = gemv2048(s, j, r0, r1, xr, a.y, tag_y);
-    if (consumers_stop(s.r, a.sync) || !grid_sync(s.r, a.sync, epoch, false)) return;
-    // ---- 2: attention
+    if (consumers_stop(s.r, a.sync)) return;
+    // ---- 2: attention (the active units wait for y word by word: no signal)
     ok = true;
     for (int u = c; u < kNH * kChunks; u += G)
       if (chunk_active(u % kChunks, p)) ok &= attention_unit(a, s, L, u / kChunks, u % kChunks, p, tag_y);
