@@ -99,11 +99,14 @@ struct Seg {
 
 enum SegId { kSegIn, kSegQkvo, kSegIf, kSegOut, kSegGu, kSegDown, kSegHead, kSegBnd, kSegCount };
 
-// This CTA's segments, in stream order (the producer's order and the consumers').
+// This CTA's segments, in stream order (the producer's order and the consumers'). One copy per CTA in shared
+// memory, built by one thread: built by every thread it went to local memory (320 copies), which the small
+// L1 left beside this kernel's shared memory pushed out to L2, and the first weight copy left ~5 us after the
+// kernel started.
 struct Plan {
   Seg seg[kSegCount];
   int order[kSegCount], n;
-  __device__ Plan(const Args& a, int c, int G) {
+  __device__ void init(const Args& a, int c, int G) {
     auto rows = [&](int id, const __nv_bfloat16* w, int nrows, int row_bytes, int rpc, int pair_off) {
       Seg& s = seg[id];
       s.w = w;
@@ -139,19 +142,17 @@ struct Plan {
     order[n++] = kSegDown;
     order[n++] = kSegHead;
     if (!a.decoder) order[n++] = kSegBnd;
+    index();
   }
-  __device__ int total() const {
-    int t = 0;
-    for (int i = 0; i < n; ++i) t += seg[order[i]].chunks();
-    return t;
+  int first[kSegCount + 1];  // chunk number of the first chunk of stream segment i (i in stream order)
+  __device__ void index() {    // once, after the segments are set: no division per chunk lookup
+    first[0] = 0;
+    for (int i = 0; i < n; ++i) first[i + 1] = first[i] + seg[order[i]].chunks();
   }
+  __device__ int total() const { return first[n]; }
   __device__ const void* chunk(int k, uint32_t& bytes) const {
-    for (int i = 0; i < n; ++i) {
-      const Seg& s = seg[order[i]];
-      const int m = s.chunks();
-      if (k < m) return s.chunk(k, bytes);
-      k -= m;
-    }
+    for (int i = 0; i < n; ++i)
+      if (k < first[i + 1]) return seg[order[i]].chunk(k - first[i], bytes);
     bytes = 0;
     return nullptr;
   }
@@ -159,6 +160,7 @@ struct Plan {
 
 struct Smem {
   Ring r;
+  Plan plan;
   alignas(16) __nv_bfloat16 vec[kD > kFfn ? kD : kFfn];  // the phase's input vector
   alignas(16) float part[kConsumerWarps][kCols];          // per-warp column sums (mLSTM unit)
   float gbuf[kMaxGuRows], ubuf[kMaxGuRows];
@@ -525,9 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1) loc_step_kernel(Args a) {
     byte = *a.byte;
     valid = byte >= 0 && byte < kVocab;  // the same answer in every CTA
   }
-  const Plan pl(a, c, G);
-  if (threadIdx.x == 0) ring_init(s.r);
+  if (threadIdx.x == 0) {
+    s.plan.init(a, c, G);
+    ring_init(s.r);
+  }
   __syncthreads();
+  const Plan& pl = s.plan;
   if (threadIdx.x >= kConsumers) {
     if ((threadIdx.x & 31) == 0) produce<kProducers>(s.r, pl, valid ? pl.total() : 0, (threadIdx.x - kConsumers) / 32);
     return;
