@@ -73,109 +73,6 @@ struct Args {
   unsigned* sync;  // [0] barrier arrivals (grows during a launch), [2] abort, [8] launch number (kept)
 };
 
-// ---- tagged hand-offs ------------------------------------------------------------------------------
-// The outputs of the matrix-vector phases (y, o, a, dn) go to global memory as 32-bit words, the bf16 value
-// in the low half and a 16-bit tag naming the write (launch number and hand-off) in the high half, each
-// written by one relaxed store. The grid barrier between the phases is then only a wake-up signal (no
-// release fence: it waited 1.2-1.7 us for the SM's bulk copies in flight, measured with per-CTA stamps), and
-// a reader takes a word once it carries the expected tag, polling again in the rare case that the signal
-// overtook the data. (Polling the words alone, without the signal, was slower: 256 threads per SM spinning on
-// L2 loads delayed everything else.) Two writes to one word are at most a few hand-offs or one launch
-// apart, so their tags always differ, and a zero-filled workspace never holds a valid tag.
-__device__ __forceinline__ uint32_t hand_tag(unsigned seq, int t) { return 1u + (seq * 128u + t) % 65535u; }
-
-__device__ __forceinline__ void st_tagged(uint32_t* p, float v, uint32_t tag) {
-  const uint32_t w = (tag << 16) | static_cast<uint32_t>(__bfloat16_as_ushort(__float2bfloat16_rn(v)));
-  asm volatile("st.relaxed.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(w) : "memory");
-}
-
-__device__ __forceinline__ uint4 ld_relaxed16(const uint32_t* p) {
-  uint4 r;
-  asm volatile("ld.relaxed.gpu.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p)
-               : "memory");
-  return r;
-}
-
-__device__ __forceinline__ uint32_t ld_relaxed4(const uint32_t* p) {
-  uint32_t r;
-  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(r) : "l"(p) : "memory");
-  return r;
-}
-
-// A failed tag wait: stop the grid (abort word; the device error flag when the wait timed out).
-__device__ __forceinline__ bool tag_wait_gives_up(unsigned* sync, unsigned long long t0) {
-  if (*reinterpret_cast<volatile unsigned*>(sync + 2) != 0u) return true;
-  if (globaltimer() - t0 > kWaitLimitNs) {
-    atomicExch(sync + 2, 1u);
-    atomicOr(&g_bp_device_errors, BP_DEVERR_TIMEOUT);
-    return true;
-  }
-  return false;
-}
-
-// The 8 tagged words at p (16-byte aligned), loaded already as u, v (so that a thread's loads are all in
-// flight at once), once all carry `tag`, as floats (loading them again while one is stale); false when the
-// step stops.
-__device__ bool take_tagged8(uint4 u, uint4 v, const uint32_t* p, uint32_t tag, float (&f)[8], unsigned* sync) {
-  auto ready = [&]() {
-    return ((u.x >> 16) == tag) & ((u.y >> 16) == tag) & ((u.z >> 16) == tag) & ((u.w >> 16) == tag) &
-           ((v.x >> 16) == tag) & ((v.y >> 16) == tag) & ((v.z >> 16) == tag) & ((v.w >> 16) == tag);
-  };
-  bool ok = true;
-  if (!ready()) {
-    const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 1;; ++it) {
-      u = ld_relaxed16(p);
-      v = ld_relaxed16(p + 4);
-      if (ready()) break;
-      if ((it & 31u) == 0 && tag_wait_gives_up(sync, t0)) {
-        ok = false;
-        break;
-      }
-    }
-  }
-  f[0] = __uint_as_float(u.x << 16); f[1] = __uint_as_float(u.y << 16);
-  f[2] = __uint_as_float(u.z << 16); f[3] = __uint_as_float(u.w << 16);
-  f[4] = __uint_as_float(v.x << 16); f[5] = __uint_as_float(v.y << 16);
-  f[6] = __uint_as_float(v.z << 16); f[7] = __uint_as_float(v.w << 16);
-  return ok;
-}
-
-__device__ __forceinline__ bool ld_tagged8(const uint32_t* p, uint32_t tag, float (&f)[8], unsigned* sync) {
-  return take_tagged8(ld_relaxed16(p), ld_relaxed16(p + 4), p, tag, f, sync);
-}
-
-// One tagged word (loaded already as u) as a float, once it carries `tag`; false when the step stops.
-__device__ bool take_tagged1(uint32_t u, const uint32_t* p, uint32_t tag, float& f, unsigned* sync) {
-  bool ok = true;
-  if ((u >> 16) != tag) {
-    const unsigned long long t0 = globaltimer();
-    for (uint32_t it = 1;; ++it) {
-      u = ld_relaxed4(p);
-      if ((u >> 16) == tag) break;
-      if ((it & 31u) == 0 && tag_wait_gives_up(sync, t0)) {
-        ok = false;
-        break;
-      }
-    }
-  }
-  f = __uint_as_float(u << 16);
-  return ok;
-}
-
-// Consumer barrier that stops the CTA when any consumer's wait failed (`bad`) or the ring stopped; a stop
-// also stops this CTA's producer and tells the other CTAs (the grid's abort word).
-__device__ __forceinline__ bool consumers_stop_if(Ring& r, unsigned* sync, bool bad) {
-  const bool stop = named_barrier_or(1, kConsumers, bad || r.abort != 0);
-  if (stop && threadIdx.x == 0) {
-    r.abort = 1;
-    atomicExch(sync + 2, 1u);
-  }
-  return stop;
-}
-
 struct Smem {
   Ring r;
   alignas(16) __nv_bfloat16 vec[kFfn];  // the phase's input vector

@@ -68,15 +68,24 @@ struct Args {
   long long* out;
   float* boundary_logit;  // encoder: written; decoder: read
   float eps, cap, mlstm_eps, qk_scale;
-  // workspace
-  __nv_bfloat16* t;   // [d] decoder: W_in e
-  __nv_bfloat16* y;   // [4d] q | k | v | o
-  float* g;           // [2 nh] gate pre-activations (after the soft cap)
-  __nv_bfloat16* hm;  // [d] mLSTM output
-  __nv_bfloat16* wo;  // [d] W_out z
-  __nv_bfloat16* a;   // [ffn]
-  __nv_bfloat16* dn;  // [d]
-  unsigned* sync;     // [0] barrier arrivals, [2] abort
+  // workspace: the hand-offs between phases as tagged words (persist.cuh: st_tagged, st_tagged_f32)
+  uint32_t* t;     // [d] decoder: W_in e
+  uint32_t* y;     // [4d] q | k | v | o
+  uint64_t* g;     // [2 nh] gate pre-activations (after the soft cap), fp32
+  uint32_t* hm;    // [d] mLSTM output
+  uint32_t* wo;    // [d] W_out z
+  uint32_t* a;     // [ffn]
+  uint32_t* dn;    // [d]
+  uint64_t* lg;    // [vocab] decoder: the logits again, for the argmax, fp32
+  unsigned* sync;  // [0] barrier arrivals, [2] abort, [8] launch number (kept)
+};
+
+// The tags of one launch's hand-offs (hand_tag(launch number, i)); y and the gates share one.
+struct Tags {
+  uint32_t t, y, hm, wo, a, dn, lg;
+  __device__ explicit Tags(unsigned seq)
+      : t(hand_tag(seq, 0)), y(hand_tag(seq, 1)), hm(hand_tag(seq, 2)), wo(hand_tag(seq, 3)), a(hand_tag(seq, 4)),
+        dn(hand_tag(seq, 5)), lg(hand_tag(seq, 6)) {}
 };
 
 // A run of this CTA's weight rows: chunks of `rpc` rows of `row_bytes` bytes; with pair_off > 0 the chunks
@@ -185,27 +194,31 @@ __device__ void norm_into_vec(Smem& s, const float (&f)[8], const __nv_bfloat16*
   *reinterpret_cast<uint4*>(&s.vec[e]) = pack8(o);
 }
 
-// The layer input h (8 values of this thread): the embedding row (encoder) or bf16(W_in e + value).
-__device__ void layer_input(const Args& a, float (&h)[8], long long byte) {
+// The layer input h (8 values of this thread): the embedding row (encoder) or bf16(W_in e + value); false
+// when the step stops.
+__device__ bool layer_input(const Args& a, const Tags& tg, unsigned* sy, float (&h)[8], long long byte) {
   const int e = threadIdx.x * 8;
   if (!a.decoder) {
     unpack8(ldg16(a.embed + byte * kD + e), h);
-  } else {
-    float t[8], v[8];
-    unpack8(ldcg16(a.t + e), t);
-    unpack8(ldg16(a.value + e), v);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) h[j] = round_bf16(__fadd_rn(t[j], v[j]));
+    return true;
   }
+  float t[8], v[8];
+  unpack8(ldg16(a.value + e), v);
+  const bool ok = ld_tagged8(a.t + e, tg.t, t, sy);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) h[j] = round_bf16(__fadd_rn(t[j], v[j]));
+  return ok;
 }
 
-// h2 = bf16(h + W_out z) for this thread's 8 values.
-__device__ void layer_h2(const Args& a, float (&h2)[8], long long byte) {
+// h2 = bf16(h + W_out z) for this thread's 8 values; false when the step stops.
+__device__ bool layer_h2(const Args& a, const Tags& tg, unsigned* sy, float (&h2)[8], long long byte) {
   float h[8], w[8];
-  layer_input(a, h, byte);
-  unpack8(ldcg16(a.wo + threadIdx.x * 8), w);
+  const uint4 w0 = ld_relaxed16(a.wo + threadIdx.x * 8), w1 = ld_relaxed16(a.wo + threadIdx.x * 8 + 4);
+  bool ok = layer_input(a, tg, sy, h, byte);
+  ok &= take_tagged8(w0, w1, a.wo + threadIdx.x * 8, tg.wo, w, sy);
 #pragma unroll
   for (int j = 0; j < 8; ++j) h2[j] = round_bf16(__fadd_rn(h[j], w[j]));
+  return ok;
 }
 
 // sigmoid evaluated in double precision and rounded once (decode.cu's sigmoid_d).
@@ -215,20 +228,25 @@ __device__ __forceinline__ float sigmoid_d(float v) {
 
 // ---- GEMV phases --------------------------------------------------------------------------------------
 // Output of row `row` of segment `id`: a bf16 vector, fp32 logits, a soft-capped gate or the boundary logit.
-__device__ void store_row(const Args& a, int id, int row, float v) {
+__device__ void store_row(const Args& a, const Tags& tg, int id, int row, float v) {
   switch (id) {
-    case kSegIn: a.t[row] = __float2bfloat16_rn(v); break;
-    case kSegQkvo: a.y[row] = __float2bfloat16_rn(v); break;
+    case kSegIn: st_tagged(a.t + row, v, tg.t); break;
+    case kSegQkvo: st_tagged(a.y + row, v, tg.y); break;
     case kSegIf: {
       const float t = __fadd_rn(v, a.L.b_if[row]);
-      a.g[row] = __fmul_rn(a.cap, static_cast<float>(tanh(static_cast<double>(__fdiv_rn(t, a.cap)))));
+      st_tagged_f32(a.g + row, __fmul_rn(a.cap, static_cast<float>(tanh(static_cast<double>(__fdiv_rn(t, a.cap))))),
+                    tg.y);
       break;
     }
-    case kSegOut: a.wo[row] = __float2bfloat16_rn(v); break;
-    case kSegDown: a.dn[row] = __float2bfloat16_rn(v); break;
+    case kSegOut: st_tagged(a.wo + row, v, tg.wo); break;
+    case kSegDown: st_tagged(a.dn + row, v, tg.dn); break;
     case kSegHead:
-      if (a.decoder) a.logits[row] = v;
-      else a.patch_out[row] = __float2bfloat16_rn(v);
+      if (a.decoder) {
+        a.logits[row] = v;
+        st_tagged_f32(a.lg + row, v, tg.lg);
+      } else {
+        a.patch_out[row] = __float2bfloat16_rn(v);
+      }
       break;
     case kSegBnd: *a.boundary_logit = v; break;
     default: break;
@@ -238,7 +256,7 @@ __device__ void store_row(const Args& a, int id, int row, float v) {
 // A K = 2048 segment whose first chunk is number `off` of its phase: warp w takes the phase's chunks w,
 // w + 8, ... whole (4 rows at once), so that the striding the ring waits rely on runs across the segments
 // of a phase (see persist.cuh, acquire); returns the next chunk.
-__device__ uint32_t gemv_seg(const Args& a, Smem& s, const Seg& sg, int id, uint32_t j0, const float (&xr)[64],
+__device__ uint32_t gemv_seg(const Args& a, const Tags& tg, Smem& s, const Seg& sg, int id, uint32_t j0, const float (&xr)[64],
                              int off = 0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = sg.chunks();
@@ -253,14 +271,14 @@ __device__ uint32_t gemv_seg(const Args& a, Smem& s, const Seg& sg, int id, uint
       if (lane < 4 && sg.r0 + rl < sg.r1) ((ch & 1) ? s.ubuf : s.gbuf)[rl] = lane_row(v);
     } else {
       const int row = sg.r0 + ch * sg.rpc + lane;
-      if (lane < sg.rpc && lane < 4 && row < sg.r1) store_row(a, id, row, lane_row(v));
+      if (lane < sg.rpc && lane < 4 && row < sg.r1) store_row(a, tg, id, row, lane_row(v));
     }
   }
   return j0 + nch;
 }
 
 // The down segment: K = 2816, 2 rows per chunk, x in s.vec; warp w takes the chunks w, w + 8, ...
-__device__ uint32_t gemv_down(const Args& a, Smem& s, const Seg& sg, uint32_t j0) {
+__device__ uint32_t gemv_down(const Args& a, const Tags& tg, Smem& s, const Seg& sg, uint32_t j0) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nch = sg.chunks();
   for (int ch = warp; ch < nch; ch += kConsumerWarps) {
@@ -286,7 +304,7 @@ __device__ uint32_t gemv_down(const Args& a, Smem& s, const Seg& sg, uint32_t j0
 #pragma unroll
       for (int r = 0; r < 2; ++r) v[r] += __shfl_xor_sync(kFull, v[r], o);
     const int row = sg.r0 + ch * 2 + lane;
-    if (lane < 2 && row < sg.r1) a.dn[row] = __float2bfloat16_rn(lane == 0 ? v[0] : v[1]);
+    if (lane < 2 && row < sg.r1) st_tagged(a.dn + row, lane == 0 ? v[0] : v[1], tg.dn);
   }
   return j0 + nch;
 }
@@ -294,14 +312,31 @@ __device__ uint32_t gemv_down(const Args& a, Smem& s, const Seg& sg, uint32_t j0
 // ---- the mLSTM step of one unit (head hd, value columns c0 .. c0 + 15) -------------------------------------
 // Thread t owns the column pair cp = t % 8 (columns c0 + 2 cp, + 1) and the rows t / 8 + 32 i (i < 16) of
 // the tile, and the two n rows 2 t, 2 t + 1.
-__device__ void mlstm_unit(const Args& a, Smem& s, int hd, int c0) {
+// q, k, v and the gates come from the tagged hand-off of the qkvo phase; false when the step stops (every
+// consumer still reaches the CTA barriers inside).
+__device__ bool mlstm_unit(const Args& a, const Tags& tg, unsigned* sy, Smem& s, int hd, int c0) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const Layer& L = a.L;
-  const __nv_bfloat16* q = a.y + hd * kDh;
-  const __nv_bfloat16* k = a.y + kD + hd * kDh;
-  const __nv_bfloat16* v = a.y + 2 * kD + hd * kDh + c0;
+  const uint32_t* q = a.y + hd * kDh;
+  const uint32_t* k = a.y + kD + hd * kDh;
+  const uint32_t* v = a.y + 2 * kD + hd * kDh + c0;
+  const int r = 2 * tid, cp = tid % 8, rb = tid / 8;
+  // every hand-off load of this thread in flight at once, then the tag checks: the gates, its q and k pair,
+  // its v pair
+  const uint64_t gi = ld_relaxed8(a.g + hd), gf = ld_relaxed8(a.g + kNH + hd);
+  const uint32_t wk0 = ld_relaxed4(k + r), wk1 = ld_relaxed4(k + r + 1), wq0 = ld_relaxed4(q + r),
+                 wq1 = ld_relaxed4(q + r + 1), wv0 = ld_relaxed4(v + 2 * cp), wv1 = ld_relaxed4(v + 2 * cp + 1);
+  float iv, fv, k0, k1, q0, q1, va, vb;
+  bool ok = take_tagged_f32(gi, a.g + hd, tg.y, iv, sy);
+  ok &= take_tagged_f32(gf, a.g + kNH + hd, tg.y, fv, sy);
+  ok &= take_tagged1(wk0, k + r, tg.y, k0, sy);
+  ok &= take_tagged1(wk1, k + r + 1, tg.y, k1, sy);
+  ok &= take_tagged1(wq0, q + r, tg.y, q0, sy);
+  ok &= take_tagged1(wq1, q + r + 1, tg.y, q1, sy);
+  ok &= take_tagged1(wv0, v + 2 * cp, tg.y, va, sy);
+  ok &= take_tagged1(wv1, v + 2 * cp + 1, tg.y, vb, sy);
   // gates (every thread; the scan kernel's gate_chunk for one position)
-  const float iv = __ldcg(a.g + hd), fv = __ldcg(a.g + kNH + hd), m_old = L.m_cur[hd];
+  const float m_old = L.m_cur[hd];
   const float ex = static_cast<float>(exp(-static_cast<double>(fv)));
   const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
   const float fl = static_cast<float>(log(static_cast<double>(sig)));
@@ -314,12 +349,7 @@ __device__ void mlstm_unit(const Args& a, Smem& s, int hd, int c0) {
   // n rows 2 t, 2 t + 1 and their part of q . n
   float qn = 0.0f;
   {
-    const int r = 2 * tid;
-    const __nv_bfloat162 k2 = __ldcg(reinterpret_cast<const __nv_bfloat162*>(k + r));
-    const __nv_bfloat162 q2 = __ldcg(reinterpret_cast<const __nv_bfloat162*>(q + r));
     const float2 n2 = *reinterpret_cast<const float2*>(L.n_cur + hd * kDh + r);
-    float k0, k1, q0, q1;
-    k0 = __low2float(k2); k1 = __high2float(k2); q0 = __low2float(q2); q1 = __high2float(q2);
     const float n0 = fmaf(fa, n2.x, round_bf16(__fmul_rn(ia, k0)));
     const float n1 = fmaf(fa, n2.y, round_bf16(__fmul_rn(ia, k1)));
     if (c0 == 0) *reinterpret_cast<float2*>(L.n_next + hd * kDh + r) = make_float2(n0, n1);
@@ -335,9 +365,6 @@ __device__ void mlstm_unit(const Args& a, Smem& s, int hd, int c0) {
   qn = consumer_sum(qn, s.r.red[1]);  // also makes s.kf, s.qsv visible
   if (c0 == 0 && tid == 0) L.m_next[hd] = mn;
   // the C tile
-  const int cp = tid % 8, rb = tid / 8;
-  const __nv_bfloat162 v2 = __ldcg(reinterpret_cast<const __nv_bfloat162*>(v + 2 * cp));
-  const float va = __low2float(v2), vb = __high2float(v2);
   float* cbase = L.c + static_cast<size_t>(hd) * kDh * kDh + c0 + 2 * cp;
   constexpr int kRowsPerThread = kDh / 32;
   float2 cv[kRowsPerThread];  // all 16 loads in flight before the first store
@@ -372,45 +399,55 @@ __device__ void mlstm_unit(const Args& a, Smem& s, int hd, int c0) {
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) hs += s.part[w][tid];
     const float den = __fadd_rn(fmaxf(fabsf(qn), g_mx), a.mlstm_eps);
-    a.hm[hd * kDh + c0 + tid] = __float2bfloat16_rn(__fdiv_rn(hs, den));
+    st_tagged(a.hm + hd * kDh + c0 + tid, __fdiv_rn(hs, den), tg.hm);
   }
   consumer_sync();  // s.part and s.r.red are reused by the next unit
+  return ok;
 }
 
 // ---- the consumers ----------------------------------------------------------------------------------------
-__device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, long long byte) {
+// Hand-offs between the phases go through tagged words (persist.cuh) behind grid barriers without fence: the
+// ordered barrier's release fence waited for the SM's bulk copies in flight.
+__device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, long long byte, const Tags& tg) {
   const int tid = threadIdx.x, e = tid * 8;
   unsigned epoch = 0;
   uint32_t j = 0;
   float xr[64];
   auto stop = [&]() { return consumers_stop(s.r, a.sync); };
+  auto signal = [&]() { return grid_sync(s.r, a.sync, epoch, false); };
   // decoder: t = W_in e
   if (a.decoder) {
     *reinterpret_cast<uint4*>(&s.vec[e]) = ldg16(a.e_in + e);
     consumer_sync();
     load_lane_x(s.vec, xr);
-    j = gemv_seg(a, s, pl.seg[kSegIn], kSegIn, j, xr);
-    if (stop() || !grid_sync(s.r, a.sync, epoch)) return;
+    j = gemv_seg(a, tg, s, pl.seg[kSegIn], kSegIn, j, xr);
+    if (stop() || !signal()) return;
   }
   // x = rmsnorm(h) * norm1; y = W_qkvo x; g = soft-capped gates
   {
     float h[8];
-    layer_input(a, h, byte);
+    const bool ok = layer_input(a, tg, a.sync, h, byte);
     norm_into_vec(s, h, a.L.norm1, a.eps);
-    consumer_sync();
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;  // also the CTA barrier after s.vec
     load_lane_x(s.vec, xr);
-    j = gemv_seg(a, s, pl.seg[kSegQkvo], kSegQkvo, j, xr);
-    j = gemv_seg(a, s, pl.seg[kSegIf], kSegIf, j, xr, pl.seg[kSegQkvo].chunks());
-    if (stop() || !grid_sync(s.r, a.sync, epoch)) return;
+    j = gemv_seg(a, tg, s, pl.seg[kSegQkvo], kSegQkvo, j, xr);
+    j = gemv_seg(a, tg, s, pl.seg[kSegIf], kSegIf, j, xr, pl.seg[kSegQkvo].chunks());
+    if (stop() || !signal()) return;
   }
   // the mLSTM step
-  for (int u = c; u < kUnits; u += G) mlstm_unit(a, s, u / (kDh / kCols), (u % (kDh / kCols)) * kCols);
-  if (!grid_sync(s.r, a.sync, epoch)) return;
+  {
+    bool ok = true;
+    for (int u = c; u < kUnits; u += G) ok &= mlstm_unit(a, tg, a.sync, s, u / (kDh / kCols), (u % (kDh / kCols)) * kCols);
+    if (consumers_stop_if(s.r, a.sync, !ok) || !signal()) return;
+  }
   // z = bf16(bf16(sigmoid(o)) * bf16(rmsnorm_head(hm) * mh_norm)); wo = W_out z
   {
     const int hd = e / kDh;  // 64 threads (2 warps) per head
-    float f[8];
-    unpack8(ldcg16(a.hm + e), f);
+    const uint4 h0 = ld_relaxed16(a.hm + e), h1 = ld_relaxed16(a.hm + e + 4);
+    const uint4 o0 = ld_relaxed16(a.y + 3 * kD + e), o1 = ld_relaxed16(a.y + 3 * kD + e + 4);
+    float f[8], ov[8];
+    bool ok = take_tagged8(h0, h1, a.hm + e, tg.hm, f, a.sync);
+    ok &= take_tagged8(o0, o1, a.y + 3 * kD + e, tg.y, ov, a.sync);
     float ss = 0.0f;
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) ss = fmaf(f[jj], f[jj], ss);
@@ -419,60 +456,78 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
     if ((tid & 31) == 0) s.head_red[hd][(tid >> 5) & 1] = ss;
     consumer_sync();
     const float inv = inv_rms(s.head_red[hd][0] + s.head_red[hd][1], kDh, a.eps);
-    float wv[8], ov[8], z[8];
+    float wv[8], z[8];
     unpack8(ldg16(a.L.mh_norm + e), wv);
-    unpack8(ldcg16(a.y + 3 * kD + e), ov);
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj)
       z[jj] = __fmul_rn(round_bf16(sigmoid_d(ov[jj])), round_bf16(__fmul_rn(__fmul_rn(f[jj], inv), wv[jj])));
     *reinterpret_cast<uint4*>(&s.vec[e]) = pack8(z);
-    consumer_sync();
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;  // also the CTA barrier after s.vec
     load_lane_x(s.vec, xr);
-    j = gemv_seg(a, s, pl.seg[kSegOut], kSegOut, j, xr);
-    if (stop() || !grid_sync(s.r, a.sync, epoch)) return;
+    j = gemv_seg(a, tg, s, pl.seg[kSegOut], kSegOut, j, xr);
+    if (stop() || !signal()) return;
   }
   // x2 = rmsnorm(h2) * norm2; a = silu(W_gate x2) * (W_up x2)
   {
     float h2[8];
-    layer_h2(a, h2, byte);
+    const bool ok = layer_h2(a, tg, a.sync, h2, byte);
     norm_into_vec(s, h2, a.L.norm2, a.eps);
-    consumer_sync();
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;
     load_lane_x(s.vec, xr);
     const Seg& sg = pl.seg[kSegGu];
-    j = gemv_seg(a, s, sg, kSegGu, j, xr);
+    j = gemv_seg(a, tg, s, sg, kSegGu, j, xr);
     if (stop()) return;
     for (int rl = tid; rl < sg.r1 - sg.r0; rl += kConsumers) {
       const float gv = round_bf16(s.gbuf[rl]), up = round_bf16(s.ubuf[rl]);
       const float sl = round_bf16(static_cast<float>(gv / (1.0 + exp(-static_cast<double>(gv)))));
-      a.a[sg.r0 + rl] = __float2bfloat16_rn(__fmul_rn(sl, up));
+      st_tagged(a.a + sg.r0 + rl, __fmul_rn(sl, up), tg.a);
     }
-    if (!grid_sync(s.r, a.sync, epoch)) return;
+    if (!signal()) return;
   }
   // dn = W_down a
   {
-    for (int i = tid; i < kFfn / 8; i += kConsumers)
-      *reinterpret_cast<uint4*>(&s.vec[i * 8]) = ldcg16(a.a + i * 8);
-    consumer_sync();
-    j = gemv_down(a, s, pl.seg[kSegDown], j);
-    if (stop() || !grid_sync(s.r, a.sync, epoch)) return;
+    constexpr int kGroups = (kFfn / 8 + kConsumers - 1) / kConsumers;  // 8-value groups per thread (2)
+    uint4 ua[kGroups][2];  // all loads in flight, then the tag checks
+#pragma unroll
+    for (int q = 0; q < kGroups; ++q) {
+      const int i = tid + q * kConsumers;
+      if (i < kFfn / 8) {
+        ua[q][0] = ld_relaxed16(a.a + i * 8);
+        ua[q][1] = ld_relaxed16(a.a + i * 8 + 4);
+      }
+    }
+    bool ok = true;
+#pragma unroll
+    for (int q = 0; q < kGroups; ++q) {
+      const int i = tid + q * kConsumers;
+      if (i < kFfn / 8) {
+        float f[8];
+        ok &= take_tagged8(ua[q][0], ua[q][1], a.a + i * 8, tg.a, f, a.sync);
+        *reinterpret_cast<uint4*>(&s.vec[i * 8]) = pack8(f);
+      }
+    }
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;
+    j = gemv_down(a, tg, s, pl.seg[kSegDown], j);
+    if (stop() || !signal()) return;
   }
   // the layer output, its norm, and the head (patch + boundary, or the LM head)
   {
     float h2[8], d[8], out[8];
-    layer_h2(a, h2, byte);
-    unpack8(ldcg16(a.dn + e), d);
+    const uint4 d0 = ld_relaxed16(a.dn + e), d1 = ld_relaxed16(a.dn + e + 4);
+    bool ok = layer_h2(a, tg, a.sync, h2, byte);
+    ok &= take_tagged8(d0, d1, a.dn + e, tg.dn, d, a.sync);
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) out[jj] = round_bf16(__fadd_rn(h2[jj], d[jj]));
     norm_into_vec(s, out, a.decoder ? a.final_norm : a.enc_norm, a.eps);
-    consumer_sync();
+    if (consumers_stop_if(s.r, a.sync, !ok)) return;
     if (!a.decoder && c == 0) *reinterpret_cast<uint4*>(a.e_out + e) = *reinterpret_cast<const uint4*>(&s.vec[e]);
     load_lane_x(s.vec, xr);
-    j = gemv_seg(a, s, pl.seg[kSegHead], kSegHead, j, xr);
-    if (!a.decoder) j = gemv_seg(a, s, pl.seg[kSegBnd], kSegBnd, j, xr, pl.seg[kSegHead].chunks());
+    j = gemv_seg(a, tg, s, pl.seg[kSegHead], kSegHead, j, xr);
+    if (!a.decoder) j = gemv_seg(a, tg, s, pl.seg[kSegBnd], kSegBnd, j, xr, pl.seg[kSegHead].chunks());
     if (stop()) return;
   }
   if (!a.decoder) return;
-  if (!grid_sync(s.r, a.sync, epoch)) return;
+  if (!signal()) return;
   // decoder: out = [argmax(logits) (torch order: NaN largest, lowest index on ties), boundary flag]
   if (c != 0) return;
   float best = -INFINITY;
@@ -482,8 +537,18 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
     if (nx || ny) return nx && (!ny || ix < iy);
     return x > y || (x == y && ix < iy);
   };
-  for (int i = tid; i < kVocab; i += kConsumers) {
-    const float x = __ldcg(a.logits + i);
+  constexpr int kPer = (kVocab + kConsumers - 1) / kConsumers;  // logits per thread (2)
+  uint64_t wl[kPer];
+#pragma unroll
+  for (int q = 0; q < kPer; ++q)
+    if (tid + q * kConsumers < kVocab) wl[q] = ld_relaxed8(a.lg + tid + q * kConsumers);
+  bool lok = true;
+#pragma unroll
+  for (int q = 0; q < kPer; ++q) {
+    const int i = tid + q * kConsumers;
+    if (i >= kVocab) continue;
+    float x;
+    lok &= take_tagged_f32(wl[q], a.lg + i, tg.lg, x, a.sync);
     if (better(x, i, best, idx)) {
       best = x;
       idx = i;
@@ -502,8 +567,8 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
     s.part[tid >> 5][0] = best;
     s.part[tid >> 5][1] = __int_as_float(idx);
   }
-  consumer_sync();
-  if (tid == 0) {
+  const bool bad = named_barrier_or(1, kConsumers, !lok);  // a failed wait leaves out alone
+  if (tid == 0 && !bad) {
     for (int w = 1; w < kConsumerWarps; ++w) {
       const float ob = s.part[w][0];
       const int oi = __float_as_int(s.part[w][1]);
@@ -546,17 +611,21 @@ __global__ void __launch_bounds__(kThreads, 1) loc_step_kernel(Args a) {
     }
     return;
   }
-  consumers(a, s, pl, c, G, byte);
+  const unsigned seq = *reinterpret_cast<volatile unsigned*>(a.sync + 8);  // this launch's number (tags)
+  consumers(a, s, pl, c, G, byte, Tags(seq));
+  // CTA 0 finishes after every CTA has read the number (they read it at their start)
+  if (c == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.sync + 8) = seq + 1;
 }
 
-constexpr size_t kWsT = 0;
-constexpr size_t kWsY = kWsT + kD * 2;
-constexpr size_t kWsG = kWsY + 4 * kD * 2;
+constexpr size_t kWsT = 0;  // tagged hand-offs: 4 bytes per bf16 value, 8 per fp32 value
+constexpr size_t kWsY = kWsT + kD * 4;
+constexpr size_t kWsG = kWsY + 4 * kD * 4;
 constexpr size_t kWsHm = kWsG + 256;
-constexpr size_t kWsWo = kWsHm + kD * 2;
-constexpr size_t kWsA = kWsWo + kD * 2;
-constexpr size_t kWsDn = kWsA + kFfn * 2;
-constexpr size_t kWsSync = kWsDn + kD * 2;
+constexpr size_t kWsWo = kWsHm + kD * 4;
+constexpr size_t kWsA = kWsWo + kD * 4;
+constexpr size_t kWsDn = kWsA + kFfn * 4;
+constexpr size_t kWsLg = kWsDn + kD * 4;
+constexpr size_t kWsSync = kWsLg + kVocab * 8;
 constexpr size_t kWsBytes = kWsSync + 256;
 
 int launch_loc(Args& a, void* workspace, size_t workspace_bytes, cudaStream_t s) {
@@ -564,13 +633,14 @@ int launch_loc(Args& a, void* workspace, size_t workspace_bytes, cudaStream_t s)
     return fail(BP_ERR_INVALID_ARGUMENT, "workspace NULL or too small (%zu < %zu bytes)", workspace_bytes, kWsBytes);
   if ((reinterpret_cast<uintptr_t>(workspace) & 15u) != 0) return fail(BP_ERR_MISALIGNED, "workspace must be 16-byte aligned");
   char* ws = static_cast<char*>(workspace);
-  a.t = reinterpret_cast<__nv_bfloat16*>(ws + kWsT);
-  a.y = reinterpret_cast<__nv_bfloat16*>(ws + kWsY);
-  a.g = reinterpret_cast<float*>(ws + kWsG);
-  a.hm = reinterpret_cast<__nv_bfloat16*>(ws + kWsHm);
-  a.wo = reinterpret_cast<__nv_bfloat16*>(ws + kWsWo);
-  a.a = reinterpret_cast<__nv_bfloat16*>(ws + kWsA);
-  a.dn = reinterpret_cast<__nv_bfloat16*>(ws + kWsDn);
+  a.t = reinterpret_cast<uint32_t*>(ws + kWsT);
+  a.y = reinterpret_cast<uint32_t*>(ws + kWsY);
+  a.g = reinterpret_cast<uint64_t*>(ws + kWsG);
+  a.hm = reinterpret_cast<uint32_t*>(ws + kWsHm);
+  a.wo = reinterpret_cast<uint32_t*>(ws + kWsWo);
+  a.a = reinterpret_cast<uint32_t*>(ws + kWsA);
+  a.dn = reinterpret_cast<uint32_t*>(ws + kWsDn);
+  a.lg = reinterpret_cast<uint64_t*>(ws + kWsLg);
   a.sync = reinterpret_cast<unsigned*>(ws + kWsSync);
   a.qk_scale = 1.0f / sqrtf(static_cast<float>(kDh));
   int st = require_sm100();
@@ -583,7 +653,7 @@ int launch_loc(Args& a, void* workspace, size_t workspace_bytes, cudaStream_t s)
   int per_sm = 0;
   e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, loc_step_kernel, kThreads, smem);
   if (e != cudaSuccess || per_sm < 1) return fail(BP_ERR_CUDA, "loc_step does not fit on an SM");
-  e = cudaMemsetAsync(a.sync, 0, 16, s);  // arrival counter, abort word
+  e = cudaMemsetAsync(a.sync, 0, 16, s);  // arrival counter, abort word (the launch number stays)
   if (e != cudaSuccess) return fail(BP_ERR_CUDA, "loc_step sync reset: %s", cudaGetErrorString(e));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(sms);  // one CTA per SM, all resident (cooperative launch)

@@ -268,7 +268,8 @@ class LocStep:
             n_next, m_next = layer.nm[1 - parity]
             self.tables.append(_LocLayer(*(t.data_ptr() for t in w), c.data_ptr(), n_cur.data_ptr(), m_cur.data_ptr(),
                                          n_next.data_ptr(), m_next.data_ptr()))
-        self.workspace = torch.empty(int(_lib.lib().bp_loc_step_workspace_bytes()), dtype=torch.uint8, device=c.device)
+        # zero-filled once: it carries the kernel's launch number from one launch to the next
+        self.workspace = torch.zeros(int(_lib.lib().bp_loc_step_workspace_bytes()), dtype=torch.uint8, device=c.device)
 
     def _common(self, parity: int):
         layer = self.layer

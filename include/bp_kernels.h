@@ -276,8 +276,9 @@ int bp_glob_step(const bp_glob_layer* layers, int n_layers, const void* x_in, co
  * n_cur / m_cur, written to n_next / m_next); z = sigmoid(o) * rmsnorm_head(h_mlstm) * mh_norm [NH, 512];
  * h2 = h + w_out z; output = h2 + w_down (silu(W_gate x2) * W_up x2), x2 = rmsnorm(h2) * norm2, w_gu
  * [2 * 2816, d] (gate rows, then up rows), w_down [d, 2816]. All weights bf16, 16-byte aligned. Each
- * call needs the workspace size bp_loc_step_workspace_bytes returns (16-byte aligned, no initial
- * content) and the whole GPU while it runs.
+ * call needs the workspace size bp_loc_step_workspace_bytes returns (16-byte aligned, zero-filled before
+ * its first launch and then left to the kernel: it carries the launch number from one call to the next)
+ * and the whole GPU while it runs. Changed with ABI version 204 (the workspace was scratch before).
  *   bp_loc_enc_step: h = embed[*byte] (embed [512, d]); e_out = rmsnorm(output) * enc_norm; patch_out =
  *     w_patch e (bf16 [d]); *boundary_logit = w_boundary . e (fp32; w_boundary [1, d]). A byte outside
  *     [0, 512) writes NaN and leaves the state alone.
