@@ -92,12 +92,13 @@ __device__ bool add_norm_tagged(const uint32_t* src, uint32_t tag, const float (
                                 float eps, Smem& s, float* red, unsigned* sync, float (&out)[8]) {
   const int e = threadIdx.x * 8;
   float f[8], wv[8];
+  const uint4 wraw = ldg16(w + e);  // in flight during the wait (the barriers below keep later loads behind)
   const bool ok = ld_tagged8(src + e, tag, f, sync);
   float ss = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
   const float inv = inv_rms(consumer_sum(ss, red), kD, eps);
-  unpack8(ldg16(w + e), wv);
+  unpack8(wraw, wv);
 #pragma unroll
   for (int j = 0; j < 8; ++j) out[j] = round_bf16(__fadd_rn(res[j], round_bf16(__fmul_rn(__fmul_rn(f[j], inv), wv[j]))));
   *reinterpret_cast<uint4*>(&s.vec[e]) = pack8(out);
@@ -557,6 +558,7 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
   // ---- value = rmsnorm(x_L) * out_norm, x_L = h + rmsnorm(dn) * mlp_norm of the last block
   if (c != 0) return;
   const int last = a.n_layers - 1;
+  const uint4 onw = ldg16(a.out_norm + tid * 8);  // before the waits
   float xl[8];
   const bool ok = add_norm_tagged(a.dn, hand_tag(seq, 4 * last + 3), hreg, a.L[last].mlp_norm, a.eps, s, s.r.red[0],
                                   a.sync, xl);
@@ -567,7 +569,7 @@ __device__ void consumers(const Args& a, Smem& s, int c, int G, long long p, uns
 #pragma unroll
   for (int i = 0; i < 8; ++i) ss = fmaf(xl[i], xl[i], ss);
   const float inv = inv_rms(consumer_sum(ss, s.r.red[1]), kD, a.eps);
-  unpack8(ldg16(a.out_norm + e), wv);
+  unpack8(onw, wv);
   float o[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i] = __fmul_rn(__fmul_rn(xl[i], inv), wv[i]);

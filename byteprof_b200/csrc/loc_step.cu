@@ -180,15 +180,32 @@ struct Smem {
 
 // ---- vector builders (all 256 consumer threads; each owns 8 elements e = 8 t .. 8 t + 7) ------------------
 
-// vec = bf16(rmsnorm(src) * w) where src is a d-vector (bf16, global through L2, or given values).
-__device__ void norm_into_vec(Smem& s, const float (&f)[8], const __nv_bfloat16* w, float eps) {
+// This thread's 8 elements of the vectors every phase input needs that no phase writes: the norm weights
+// and the layer input's own part (the embedding row, or the decoder's value and its input e), loaded at the
+// start of the kernel so that no phase waits for them.
+struct Pre {
+  uint4 n1, n2, mh, on, h, x0;
+  __device__ void load(const Args& a, long long byte) {
+    const int e = threadIdx.x * 8;
+    n1 = ldg16(a.L.norm1 + e);
+    n2 = ldg16(a.L.norm2 + e);
+    mh = ldg16(a.L.mh_norm + e);
+    on = ldg16((a.decoder ? a.final_norm : a.enc_norm) + e);
+    h = a.decoder ? ldg16(a.value + e) : ldg16(a.embed + byte * kD + e);
+    if (a.decoder) x0 = ldg16(a.e_in + e);
+  }
+};
+
+// vec = bf16(rmsnorm(src) * w) where src is a d-vector (bf16, global through L2, or given values) and w
+// this thread's 8 norm weights.
+__device__ void norm_into_vec(Smem& s, const float (&f)[8], uint4 w, float eps) {
   const int e = threadIdx.x * 8;
   float ss = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) ss = fmaf(f[j], f[j], ss);
   const float inv = inv_rms(consumer_sum(ss, s.r.red[0]), kD, eps);
   float wv[8], o[8];
-  unpack8(ldg16(w + e), wv);
+  unpack8(w, wv);
 #pragma unroll
   for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(__fmul_rn(f[j], inv), wv[j]);
   *reinterpret_cast<uint4*>(&s.vec[e]) = pack8(o);
@@ -196,14 +213,14 @@ __device__ void norm_into_vec(Smem& s, const float (&f)[8], const __nv_bfloat16*
 
 // The layer input h (8 values of this thread): the embedding row (encoder) or bf16(W_in e + value); false
 // when the step stops.
-__device__ bool layer_input(const Args& a, const Tags& tg, unsigned* sy, float (&h)[8], long long byte) {
+__device__ bool layer_input(const Args& a, const Tags& tg, unsigned* sy, float (&h)[8], const Pre& pre) {
   const int e = threadIdx.x * 8;
   if (!a.decoder) {
-    unpack8(ldg16(a.embed + byte * kD + e), h);
+    unpack8(pre.h, h);
     return true;
   }
   float t[8], v[8];
-  unpack8(ldg16(a.value + e), v);
+  unpack8(pre.h, v);
   const bool ok = ld_tagged8(a.t + e, tg.t, t, sy);
 #pragma unroll
   for (int j = 0; j < 8; ++j) h[j] = round_bf16(__fadd_rn(t[j], v[j]));
@@ -211,10 +228,10 @@ __device__ bool layer_input(const Args& a, const Tags& tg, unsigned* sy, float (
 }
 
 // h2 = bf16(h + W_out z) for this thread's 8 values; false when the step stops.
-__device__ bool layer_h2(const Args& a, const Tags& tg, unsigned* sy, float (&h2)[8], long long byte) {
+__device__ bool layer_h2(const Args& a, const Tags& tg, unsigned* sy, float (&h2)[8], const Pre& pre) {
   float h[8], w[8];
   const uint4 w0 = ld_relaxed16(a.wo + threadIdx.x * 8), w1 = ld_relaxed16(a.wo + threadIdx.x * 8 + 4);
-  bool ok = layer_input(a, tg, sy, h, byte);
+  bool ok = layer_input(a, tg, sy, h, pre);
   ok &= take_tagged8(w0, w1, a.wo + threadIdx.x * 8, tg.wo, w, sy);
 #pragma unroll
   for (int j = 0; j < 8; ++j) h2[j] = round_bf16(__fadd_rn(h[j], w[j]));
@@ -321,6 +338,14 @@ __device__ bool mlstm_unit(const Args& a, const Tags& tg, unsigned* sy, Smem& s,
   const uint32_t* k = a.y + kD + hd * kDh;
   const uint32_t* v = a.y + 2 * kD + hd * kDh + c0;
   const int r = 2 * tid, cp = tid % 8, rb = tid / 8;
+  // the state first (it does not wait for the hand-off)
+  float* cbase = L.c + static_cast<size_t>(hd) * kDh * kDh + c0 + 2 * cp;
+  constexpr int kRowsPerThread = kDh / 32;
+  float2 cv[kRowsPerThread];  // all 16 loads in flight before the first store
+#pragma unroll
+  for (int i = 0; i < kRowsPerThread; ++i) cv[i] = *reinterpret_cast<const float2*>(cbase + static_cast<size_t>(rb + 32 * i) * kDh);
+  const float2 n2 = *reinterpret_cast<const float2*>(L.n_cur + hd * kDh + r);
+  const float m_old = L.m_cur[hd];
   // every hand-off load of this thread in flight at once, then the tag checks: the gates, its q and k pair,
   // its v pair
   const uint64_t gi = ld_relaxed8(a.g + hd), gf = ld_relaxed8(a.g + kNH + hd);
@@ -336,7 +361,6 @@ __device__ bool mlstm_unit(const Args& a, const Tags& tg, unsigned* sy, Smem& s,
   ok &= take_tagged1(wv0, v + 2 * cp, tg.y, va, sy);
   ok &= take_tagged1(wv1, v + 2 * cp + 1, tg.y, vb, sy);
   // gates (every thread; the scan kernel's gate_chunk for one position)
-  const float m_old = L.m_cur[hd];
   const float ex = static_cast<float>(exp(-static_cast<double>(fv)));
   const float sig = __fdiv_rn(1.0f, __fadd_rn(1.0f, ex));
   const float fl = static_cast<float>(log(static_cast<double>(sig)));
@@ -349,7 +373,6 @@ __device__ bool mlstm_unit(const Args& a, const Tags& tg, unsigned* sy, Smem& s,
   // n rows 2 t, 2 t + 1 and their part of q . n
   float qn = 0.0f;
   {
-    const float2 n2 = *reinterpret_cast<const float2*>(L.n_cur + hd * kDh + r);
     const float n0 = fmaf(fa, n2.x, round_bf16(__fmul_rn(ia, k0)));
     const float n1 = fmaf(fa, n2.y, round_bf16(__fmul_rn(ia, k1)));
     if (c0 == 0) *reinterpret_cast<float2*>(L.n_next + hd * kDh + r) = make_float2(n0, n1);
@@ -365,11 +388,6 @@ __device__ bool mlstm_unit(const Args& a, const Tags& tg, unsigned* sy, Smem& s,
   qn = consumer_sum(qn, s.r.red[1]);  // also makes s.kf, s.qsv visible
   if (c0 == 0 && tid == 0) L.m_next[hd] = mn;
   // the C tile
-  float* cbase = L.c + static_cast<size_t>(hd) * kDh * kDh + c0 + 2 * cp;
-  constexpr int kRowsPerThread = kDh / 32;
-  float2 cv[kRowsPerThread];  // all 16 loads in flight before the first store
-#pragma unroll
-  for (int i = 0; i < kRowsPerThread; ++i) cv[i] = *reinterpret_cast<const float2*>(cbase + static_cast<size_t>(rb + 32 * i) * kDh);
   float ha = 0.0f, hb = 0.0f;
 #pragma unroll
   for (int i = 0; i < kRowsPerThread; ++i) {
@@ -408,7 +426,7 @@ __device__ bool mlstm_unit(const Args& a, const Tags& tg, unsigned* sy, Smem& s,
 // ---- the consumers ----------------------------------------------------------------------------------------
 // Hand-offs between the phases go through tagged words (persist.cuh) behind grid barriers without fence: the
 // ordered barrier's release fence waited for the SM's bulk copies in flight.
-__device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, long long byte, const Tags& tg) {
+__device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, const Pre& pre, const Tags& tg) {
   const int tid = threadIdx.x, e = tid * 8;
   unsigned epoch = 0;
   uint32_t j = 0;
@@ -417,7 +435,7 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
   auto signal = [&]() { return grid_sync(s.r, a.sync, epoch, false); };
   // decoder: t = W_in e
   if (a.decoder) {
-    *reinterpret_cast<uint4*>(&s.vec[e]) = ldg16(a.e_in + e);
+    *reinterpret_cast<uint4*>(&s.vec[e]) = pre.x0;
     consumer_sync();
     load_lane_x(s.vec, xr);
     j = gemv_seg(a, tg, s, pl.seg[kSegIn], kSegIn, j, xr);
@@ -426,8 +444,8 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
   // x = rmsnorm(h) * norm1; y = W_qkvo x; g = soft-capped gates
   {
     float h[8];
-    const bool ok = layer_input(a, tg, a.sync, h, byte);
-    norm_into_vec(s, h, a.L.norm1, a.eps);
+    const bool ok = layer_input(a, tg, a.sync, h, pre);
+    norm_into_vec(s, h, pre.n1, a.eps);
     if (consumers_stop_if(s.r, a.sync, !ok)) return;  // also the CTA barrier after s.vec
     load_lane_x(s.vec, xr);
     j = gemv_seg(a, tg, s, pl.seg[kSegQkvo], kSegQkvo, j, xr);
@@ -457,7 +475,7 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
     consumer_sync();
     const float inv = inv_rms(s.head_red[hd][0] + s.head_red[hd][1], kDh, a.eps);
     float wv[8], z[8];
-    unpack8(ldg16(a.L.mh_norm + e), wv);
+    unpack8(pre.mh, wv);
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj)
       z[jj] = __fmul_rn(round_bf16(sigmoid_d(ov[jj])), round_bf16(__fmul_rn(__fmul_rn(f[jj], inv), wv[jj])));
@@ -470,8 +488,8 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
   // x2 = rmsnorm(h2) * norm2; a = silu(W_gate x2) * (W_up x2)
   {
     float h2[8];
-    const bool ok = layer_h2(a, tg, a.sync, h2, byte);
-    norm_into_vec(s, h2, a.L.norm2, a.eps);
+    const bool ok = layer_h2(a, tg, a.sync, h2, pre);
+    norm_into_vec(s, h2, pre.n2, a.eps);
     if (consumers_stop_if(s.r, a.sync, !ok)) return;
     load_lane_x(s.vec, xr);
     const Seg& sg = pl.seg[kSegGu];
@@ -514,11 +532,11 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
   {
     float h2[8], d[8], out[8];
     const uint4 d0 = ld_relaxed16(a.dn + e), d1 = ld_relaxed16(a.dn + e + 4);
-    bool ok = layer_h2(a, tg, a.sync, h2, byte);
+    bool ok = layer_h2(a, tg, a.sync, h2, pre);
     ok &= take_tagged8(d0, d1, a.dn + e, tg.dn, d, a.sync);
 #pragma unroll
     for (int jj = 0; jj < 8; ++jj) out[jj] = round_bf16(__fadd_rn(h2[jj], d[jj]));
-    norm_into_vec(s, out, a.decoder ? a.final_norm : a.enc_norm, a.eps);
+    norm_into_vec(s, out, pre.on, a.eps);
     if (consumers_stop_if(s.r, a.sync, !ok)) return;
     if (!a.decoder && c == 0) *reinterpret_cast<uint4*>(a.e_out + e) = *reinterpret_cast<const uint4*>(&s.vec[e]);
     load_lane_x(s.vec, xr);
@@ -592,7 +610,13 @@ __global__ void __launch_bounds__(kThreads, 1) loc_step_kernel(Args a) {
     byte = *a.byte;
     valid = byte >= 0 && byte < kVocab;  // the same answer in every CTA
   }
-  if (threadIdx.x == 0) {
+  // the consumers' loads that no phase waits for go out while the first producer thread builds the plan
+  const unsigned seq = *reinterpret_cast<volatile unsigned*>(a.sync + 8);  // this launch's number (tags)
+  Pre pre{};
+  if (threadIdx.x < kConsumers && valid) {
+    pre.load(a, byte);
+  }
+  if (threadIdx.x == kConsumers) {
     s.plan.init(a, c, G);
     ring_init(s.r);
   }
@@ -611,8 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1) loc_step_kernel(Args a) {
     }
     return;
   }
-  const unsigned seq = *reinterpret_cast<volatile unsigned*>(a.sync + 8);  // this launch's number (tags)
-  consumers(a, s, pl, c, G, byte, Tags(seq));
+  consumers(a, s, pl, c, G, pre, Tags(seq));
   // CTA 0 finishes after every CTA has read the number (they read it at their start)
   if (c == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.sync + 8) = seq + 1;
 }
