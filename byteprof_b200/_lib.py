@@ -55,6 +55,7 @@ _SIGNATURES = {
                                 c_float, c_float, c_float, c_void_p, c_size_t, c_void_p]),
     "bp_loc_dec_step": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_float, c_float, c_float, c_void_p, c_size_t, c_void_p]),
+    "bp_loc_encdec_step": (c_int, [c_void_p] * 16 + [c_float, c_float, c_float, c_void_p, c_size_t, c_void_p]),
     "bp_glob_step": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_float,
                              c_void_p, c_size_t, c_void_p]),
     "bp_mlstm_scan": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

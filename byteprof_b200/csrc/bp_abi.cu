@@ -55,7 +55,7 @@ int require_sm100() {
 
 extern "C" {
 
-int bp_abi_version(void) { return 204; }
+int bp_abi_version(void) { return 205; }
 
 const char* bp_status_string(int status) {
   switch (status) {

@@ -50,6 +50,9 @@ struct Layer {
 struct Args {
   Layer L;
   int decoder;
+  // fused: this launch runs the encoder step (L) and then the decoder step (L2) of the same byte
+  int fused;
+  Layer L2;
   // encoder
   const __nv_bfloat16* embed;
   const long long* byte;
@@ -78,14 +81,16 @@ struct Args {
   uint32_t* dn;    // [d]
   uint64_t* lg;    // [vocab] decoder: the logits again, for the argmax, fp32
   unsigned* sync;  // [0] barrier arrivals, [2] abort, [8] launch number (kept)
+  uint64_t* bnd;   // fused: the boundary logit, tagged, for the decoder part's decision (in the sync words)
 };
 
-// The tags of one launch's hand-offs (hand_tag(launch number, i)); y and the gates share one.
+// The tags of one launch's hand-offs (hand_tag(launch number, i)); y and the gates share one. A fused launch
+// numbers its decoder part's hand-offs from 8; the boundary logit's hand-off is number 16 in either part.
 struct Tags {
-  uint32_t t, y, hm, wo, a, dn, lg;
-  __device__ explicit Tags(unsigned seq)
-      : t(hand_tag(seq, 0)), y(hand_tag(seq, 1)), hm(hand_tag(seq, 2)), wo(hand_tag(seq, 3)), a(hand_tag(seq, 4)),
-        dn(hand_tag(seq, 5)), lg(hand_tag(seq, 6)) {}
+  uint32_t t, y, hm, wo, a, dn, lg, bnd;
+  __device__ Tags(unsigned seq, int base)
+      : t(hand_tag(seq, base)), y(hand_tag(seq, base + 1)), hm(hand_tag(seq, base + 2)), wo(hand_tag(seq, base + 3)),
+        a(hand_tag(seq, base + 4)), dn(hand_tag(seq, base + 5)), lg(hand_tag(seq, base + 6)), bnd(hand_tag(seq, 16)) {}
 };
 
 // A run of this CTA's weight rows: chunks of `rpc` rows of `row_bytes` bytes; with pair_off > 0 the chunks
@@ -167,9 +172,21 @@ struct Plan {
   }
 };
 
+// The producer's stream: the plan's chunks, then (fused launch) the decoder part's.
+struct Stream2 {
+  const Plan& p0;
+  const Plan* p1;
+  __device__ int total() const { return p0.total() + (p1 != nullptr ? p1->total() : 0); }
+  __device__ const void* chunk(int k, uint32_t& bytes) const {
+    const int t0 = p0.total();
+    return k < t0 ? p0.chunk(k, bytes) : p1->chunk(k - t0, bytes);
+  }
+};
+
 struct Smem {
   Ring r;
-  Plan plan;
+  Plan plan, plan1;  // plan1, part1: a fused launch's decoder part
+  Args part1;
   alignas(16) __nv_bfloat16 vec[kD > kFfn ? kD : kFfn];  // the phase's input vector
   alignas(16) float part[kConsumerWarps][kCols];          // per-warp column sums (mLSTM unit)
   float gbuf[kMaxGuRows], ubuf[kMaxGuRows];
@@ -265,7 +282,10 @@ __device__ void store_row(const Args& a, const Tags& tg, int id, int row, float 
         a.patch_out[row] = __float2bfloat16_rn(v);
       }
       break;
-    case kSegBnd: *a.boundary_logit = v; break;
+    case kSegBnd:
+      *a.boundary_logit = v;
+      if (a.fused) st_tagged_f32(a.bnd, v, tg.bnd);  // read by this launch's decoder part
+      break;
     default: break;
   }
 }
@@ -426,10 +446,11 @@ __device__ bool mlstm_unit(const Args& a, const Tags& tg, unsigned* sy, Smem& s,
 // ---- the consumers ----------------------------------------------------------------------------------------
 // Hand-offs between the phases go through tagged words (persist.cuh) behind grid barriers without fence: the
 // ordered barrier's release fence waited for the SM's bulk copies in flight.
-__device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, const Pre& pre, const Tags& tg) {
+// j: the ring chunk counter, epoch: the grid barriers passed (both carried from a fused launch's encoder part
+// into its decoder part).
+__device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, const Pre& pre, const Tags& tg,
+                          uint32_t& j, unsigned& epoch) {
   const int tid = threadIdx.x, e = tid * 8;
-  unsigned epoch = 0;
-  uint32_t j = 0;
   float xr[64];
   auto stop = [&]() { return consumers_stop(s.r, a.sync); };
   auto signal = [&]() { return grid_sync(s.r, a.sync, epoch, false); };
@@ -595,8 +616,10 @@ __device__ void consumers(const Args& a, Smem& s, const Plan& pl, int c, int G, 
         idx = oi;
       }
     }
+    float bl = *a.boundary_logit;
+    if (a.fused && !take_tagged_f32(ld_relaxed8(a.bnd), a.bnd, tg.bnd, bl, a.sync)) return;
     a.out[0] = idx;
-    a.out[1] = sigmoid_d(*a.boundary_logit) >= 0.5f ? 1 : 0;
+    a.out[1] = sigmoid_d(bl) >= 0.5f ? 1 : 0;
   }
 }
 
@@ -618,12 +641,21 @@ __global__ void __launch_bounds__(kThreads, 1) loc_step_kernel(Args a) {
   }
   if (threadIdx.x == kConsumers) {
     s.plan.init(a, c, G);
+    if (a.fused) {  // the decoder part: the same arguments with its layer
+      s.part1 = a;
+      s.part1.L = a.L2;
+      s.part1.decoder = 1;
+      s.plan1.init(s.part1, c, G);
+    }
     ring_init(s.r);
   }
   __syncthreads();
   const Plan& pl = s.plan;
   if (threadIdx.x >= kConsumers) {
-    if ((threadIdx.x & 31) == 0) produce<kProducers>(s.r, pl, valid ? pl.total() : 0, (threadIdx.x - kConsumers) / 32);
+    if ((threadIdx.x & 31) == 0) {
+      const Stream2 src{pl, a.fused ? &s.plan1 : nullptr};
+      produce<kProducers>(s.r, src, valid ? src.total() : 0, (threadIdx.x - kConsumers) / 32);
+    }
     return;
   }
   if (!valid) {  // host checks keep the byte in range; never index with a bad one
@@ -635,7 +667,18 @@ __global__ void __launch_bounds__(kThreads, 1) loc_step_kernel(Args a) {
     }
     return;
   }
-  consumers(a, s, pl, c, G, pre, Tags(seq));
+  uint32_t j = 0;
+  unsigned epoch = 0;
+  consumers(a, s, pl, c, G, pre, Tags(seq, 0), j, epoch);
+  const bool stopped = named_barrier_or(1, kConsumers, s.r.abort != 0);  // one answer for every consumer
+  if (a.fused && !stopped) {
+    // the decoder part, in the same ring and barrier sequence; its input e is this CTA's s.vec (the encoder
+    // part's normalised output, also in e_out)
+    Pre pd{};
+    pd.load(s.part1, 0);
+    pd.x0 = *reinterpret_cast<const uint4*>(&s.vec[threadIdx.x * 8]);
+    consumers(s.part1, s, s.plan1, c, G, pd, Tags(seq, 8), j, epoch);
+  }
   // CTA 0 finishes after every CTA has read the number (they read it at their start)
   if (c == 0 && threadIdx.x == 0) *reinterpret_cast<volatile unsigned*>(a.sync + 8) = seq + 1;
 }
@@ -665,6 +708,7 @@ int launch_loc(Args& a, void* workspace, size_t workspace_bytes, cudaStream_t s)
   a.dn = reinterpret_cast<uint32_t*>(ws + kWsDn);
   a.lg = reinterpret_cast<uint64_t*>(ws + kWsLg);
   a.sync = reinterpret_cast<unsigned*>(ws + kWsSync);
+  a.bnd = reinterpret_cast<uint64_t*>(ws + kWsSync + 64);  // kept (tagged), not cleared per launch
   a.qk_scale = 1.0f / sqrtf(static_cast<float>(kDh));
   int st = require_sm100();
   if (st != BP_OK) return st;
@@ -765,6 +809,48 @@ extern "C" int bp_loc_dec_step(const bp_loc_layer* layer, const void* e_in, cons
   a.final_norm = static_cast<const __nv_bfloat16*>(final_norm);
   a.lm_head = static_cast<const __nv_bfloat16*>(lm_head);
   a.boundary_logit = const_cast<float*>(boundary_logit);
+  a.logits = logits;
+  a.out = reinterpret_cast<long long*>(out);
+  a.eps = eps;
+  a.cap = gate_cap;
+  a.mlstm_eps = mlstm_eps;
+  return launch_loc(a, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bp_loc_encdec_step(const bp_loc_layer* enc_layer, const bp_loc_layer* dec_layer, const void* embed,
+                                  const int64_t* byte, const void* enc_norm, const void* w_patch,
+                                  const void* w_boundary, void* e_out, void* patch_out, float* boundary_logit,
+                                  const void* value, const void* w_in, const void* final_norm, const void* lm_head,
+                                  float* logits, int64_t* out, float eps, float gate_cap, float mlstm_eps,
+                                  void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace bp;
+  clear_error();
+  Args a{};
+  int st = fill_layer(enc_layer, a.L);
+  if (st != BP_OK) return st;
+  st = fill_layer(dec_layer, a.L2);
+  if (st != BP_OK) return st;
+  if (a.L.c == a.L2.c || a.L.n_next == a.L2.n_next || a.L.m_next == a.L2.m_next)
+    return fail(BP_ERR_INVALID_ARGUMENT, "the encoder and decoder layers must have their own state");
+  if (!a16(embed) || byte == nullptr || !a16(enc_norm) || !a16(w_patch) || !a16(w_boundary) || !a16(e_out) ||
+      !a16(patch_out) || boundary_logit == nullptr || !a16(value) || !a16(w_in) || !a16(final_norm) ||
+      !a16(lm_head) || logits == nullptr || out == nullptr)
+    return fail(BP_ERR_MISALIGNED, "a pointer is NULL or not 16-byte aligned");
+  a.decoder = 0;
+  a.fused = 1;
+  a.embed = static_cast<const __nv_bfloat16*>(embed);
+  a.byte = reinterpret_cast<const long long*>(byte);
+  a.enc_norm = static_cast<const __nv_bfloat16*>(enc_norm);
+  a.w_patch = static_cast<const __nv_bfloat16*>(w_patch);
+  a.w_boundary = static_cast<const __nv_bfloat16*>(w_boundary);
+  a.e_out = static_cast<__nv_bfloat16*>(e_out);
+  a.patch_out = static_cast<__nv_bfloat16*>(patch_out);
+  a.boundary_logit = boundary_logit;
+  a.e_in = static_cast<const __nv_bfloat16*>(e_out);  // the decoder part takes e from shared memory
+  a.value = static_cast<const __nv_bfloat16*>(value);
+  a.w_in = static_cast<const __nv_bfloat16*>(w_in);
+  a.final_norm = static_cast<const __nv_bfloat16*>(final_norm);
+  a.lm_head = static_cast<const __nv_bfloat16*>(lm_head);
   a.logits = logits;
   a.out = reinterpret_cast<long long*>(out);
   a.eps = eps;

@@ -158,6 +158,13 @@ class BolmoDecoder:
         skinny_mm(self.e, self.w_patch, out=self.patch)
         skinny_mm(self.e, self.w_boundary, out=self.boundary_logit)
 
+    def encdec_step(self, parity: int) -> None:
+        """enc_step and dec_step of a byte that opens no patch as one launch (the persistent local steps only);
+        the same results as the two, bit for bit."""
+        self.enc_kernel.encdec(self.dec_kernel, parity, self.embed, self.byte, self.enc_norm, self.w_patch,
+                               self.w_boundary, self.e, self.patch, self.boundary_logit, self.value, self.w_in,
+                               self.final_norm, self.lm_head, self.logits, self.out)
+
     def glob_step(self) -> None:
         if self.glob_kernel is not None:
             self.glob_kernel(self.patch, self.value, self.pos)  # writes value, advances pos
@@ -200,6 +207,10 @@ class BolmoDecoder:
         def one(p: int, patch: bool):
             def fn():
                 self.byte.copy_(self._pin_byte, non_blocking=True)
+                if not patch and self.enc_kernel is not None and self.dec_kernel is not None:
+                    self.encdec_step(p)  # no global step between them: one launch for both
+                    self._pin_out.copy_(self.out, non_blocking=True)
+                    return
                 self.enc_step(p)
                 if patch:
                     self.glob_step()

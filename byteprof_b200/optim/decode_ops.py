@@ -282,6 +282,20 @@ class LocStep:
                       enc_norm.data_ptr(), w_patch.data_ptr(), w_boundary.data_ptr(), e_out.data_ptr(),
                       patch_out.data_ptr(), boundary_logit.data_ptr(), *self._common(parity))
 
+    def encdec(self, dec: "LocStep", parity: int, embed, byte, enc_norm, w_patch, w_boundary, e_out, patch_out,
+               boundary_logit, value, w_in, final_norm, lm_head, logits, out) -> None:
+        """This (encoder) step and then `dec`'s decoder step of the same byte in one launch
+        (bp_loc_encdec_step), for a byte that opens no patch; this step's workspace."""
+        a, b = self.layer, dec.layer
+        if (a.norm_eps, a.gate_cap, a.mlstm_eps) != (b.norm_eps, b.gate_cap, b.mlstm_eps):
+            raise ValueError("the fused local step needs the encoder and decoder layers' eps and gate cap to agree")
+        with _lib.on_device(embed):
+            _lib.call("bp_loc_encdec_step", ctypes.addressof(self.tables[parity]), ctypes.addressof(dec.tables[parity]),
+                      embed.data_ptr(), byte.data_ptr(), enc_norm.data_ptr(), w_patch.data_ptr(), w_boundary.data_ptr(),
+                      e_out.data_ptr(), patch_out.data_ptr(), boundary_logit.data_ptr(), value.data_ptr(),
+                      w_in.data_ptr(), final_norm.data_ptr(), lm_head.data_ptr(), logits.data_ptr(), out.data_ptr(),
+                      *self._common(parity))
+
     def dec(self, parity: int, e_in, value, w_in, final_norm, lm_head, boundary_logit, logits, out) -> None:
         with _lib.on_device(e_in):
             _lib.call("bp_loc_dec_step", ctypes.addressof(self.tables[parity]), e_in.data_ptr(), value.data_ptr(),

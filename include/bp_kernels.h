@@ -19,7 +19,7 @@
  *   bp_mlstm_accept     byteprof/optim/mlstm_multistep.py:136-146 accept_kernel
  *   bp_mlstm_commit_state byteprof/optim/draft_core.py:92-111  commit_state (+ draft_kernels.py commit_kernel)
  *   bp_rmsnorm_ex, bp_embed_rmsnorm, bp_swiglu, bp_gate_softcap, bp_decode_attention, bp_decode_finish, bp_glob_step,
- *   bp_loc_enc_step, bp_loc_dec_step
+ *   bp_loc_enc_step, bp_loc_dec_step, bp_loc_encdec_step
  *                       the per-byte pieces of the minimal Bolmo loop: byteprof/optim/bolmo.py:32-136
  *                       (_layer_step, LocalLoop.enc_step / dec_step, GlobalStep.step) and
  *                       byteprof/optim/bolmo_loop.py:36-64 (MinimalPieces: norm, lm_head, argmax)
@@ -312,6 +312,19 @@ int bp_loc_dec_step(const bp_loc_layer* layer, const void* e_in, const void* val
                     const void* final_norm, const void* lm_head, const float* boundary_logit, float* logits,
                     int64_t* out, float eps, float gate_cap, float mlstm_eps, void* workspace, size_t workspace_bytes,
                     void* stream);
+/*
+ * bp_loc_encdec_step: bp_loc_enc_step and then bp_loc_dec_step of the same byte (e_in = e_out, the encoder's
+ * boundary logit for the decision) in one persistent launch, for a byte that opens no patch (the global
+ * step does not run between them): the decoder's weights stream into the ring while the encoder finishes,
+ * and one launch boundary goes. Results equal the two launches bit for bit. The workspace is the encoder's
+ * (its own launch numbers); eps, gate_cap and mlstm_eps are the two layers' common values. A byte outside
+ * [0, 512) writes the encoder's NaN outputs and runs neither layer. Added with ABI version 205.
+ */
+int bp_loc_encdec_step(const bp_loc_layer* enc_layer, const bp_loc_layer* dec_layer, const void* embed,
+                       const int64_t* byte, const void* enc_norm, const void* w_patch, const void* w_boundary,
+                       void* e_out, void* patch_out, float* boundary_logit, const void* value, const void* w_in,
+                       const void* final_norm, const void* lm_head, float* logits, int64_t* out, float eps,
+                       float gate_cap, float mlstm_eps, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
  * End of a decode step: out[0] = argmax(logits[0:n]) (torch.argmax order: NaN largest, lowest index on

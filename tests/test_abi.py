@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_version_and_status_strings():
     L = _lib.lib()
-    assert L.bp_abi_version() == 204
+    assert L.bp_abi_version() == 205
     assert L.bp_status_string(0) == b"ok"
     assert L.bp_status_string(3) == b"misaligned"
     assert L.bp_status_string(99) == b"unknown status"

@@ -190,3 +190,47 @@ def test_both_decoder_steps_against_the_oracle():
     print(stats)
     for k, ((e_kbk, c_kbk), (e_f, c_f)) in stats.items():
         assert e_f <= max(1.5 * e_kbk, 0.01) and c_f >= min(c_kbk - 0.002, 0.999), (k, stats[k])
+
+
+def _everything(m):
+    return [m.e, m.patch, m.boundary_logit, m.logits, m.out, *m.enc.state, *m.enc.nm[1], *m.dec.state, *m.dec.nm[1]]
+
+
+def test_one_launch_for_both_steps_equals_the_two_launches_bit_for_bit():
+    """bp_loc_encdec_step (a byte that opens no patch: encoder then decoder in one persistent launch) gives
+    the outputs and new states of bp_loc_enc_step followed by bp_loc_dec_step exactly, launch after launch."""
+    m = _model(9)
+    snap_e, snap_d = _snap(m.enc), _snap(m.dec)
+    for byte in (97, 3, 500):
+        _restore(m.enc, snap_e)
+        _restore(m.dec, snap_d)
+        m.byte.fill_(byte)
+        m.enc_step(0)
+        m.dec_step(0)
+        torch.cuda.synchronize()
+        want = [t.clone() for t in _everything(m)]
+        _restore(m.enc, snap_e)
+        _restore(m.dec, snap_d)
+        m.logits.zero_()
+        m.out.zero_()
+        m.e.zero_()
+        m.encdec_step(0)
+        torch.cuda.synchronize()
+        got = _everything(m)
+        bad = [i for i, (a, b) in enumerate(zip(got, want)) if not torch.equal(a, b)]
+        assert not bad, (byte, bad)
+
+
+def test_one_launch_for_both_steps_with_a_byte_outside_the_vocabulary_runs_neither_layer():
+    m = _model(13)
+    snap_e, snap_d = _snap(m.enc), _snap(m.dec)
+    m.logits.fill_(1.0)
+    m.out.fill_(7)
+    m.byte.fill_(512)
+    m.encdec_step(0)
+    torch.cuda.synchronize()
+    assert torch.isnan(m.e.float()).all() and torch.isnan(m.patch.float()).all()
+    assert torch.isnan(m.boundary_logit).all()
+    assert all(torch.equal(a, b) for a, b in zip((*m.enc.state, *m.enc.nm[1]), snap_e))
+    assert all(torch.equal(a, b) for a, b in zip((*m.dec.state, *m.dec.nm[1]), snap_d))
+    assert bool((m.logits == 1.0).all()) and bool((m.out == 7).all())
