@@ -646,8 +646,8 @@ def decode_cells(device: torch.device, peak: float, seed: int = 0, reps: int = 2
         "frac": round(streamed / ours["wall"] / 1e9 / peak, 4),
         "work": ("the exactness mode's greedy bytes and patch starts (float64-equivalent), fed to both arms; "
                  "the model's own greedy choice is read at every step"),
-        "graphs_per_byte": ("one graph per byte: byte copy in, enc + dec (or enc + glob + dec on a patch start), "
-                            "result copy out; one host sync per byte in a native loop (bp_decode_loop); "
+        "graphs_per_byte": ("one graph per byte: byte copy in, enc + dec as one launch (or enc, glob, dec on a "
+                            "patch start), result copy out; one host sync per byte in a native loop (bp_decode_loop); "
                             "the torch arm runs the same loop over its own graphs"),
         "free_running": {"bytes_per_s": round(steps / free["wall"], 1),
                          "patches_in_timed_steps": free["gen_patches"],
