@@ -4,6 +4,8 @@
 //            patch = W_patch e; boundary logit = w_boundary . e (fp32)
 //   decoder: h = W_in e + value; one mLSTM layer; logits = LM head (rmsnorm(layer output) * final_norm)
 //            (fp32); out = [argmax(logits), sigmoid(boundary logit) >= 0.5]
+//   both (a byte that opens no patch): the encoder step, then the decoder step on its e and boundary logit,
+//            in one launch: one ring stream and one barrier sequence over both parts
 // The layer: x = rmsnorm(h) * norm1; y = W_qkvo x (q | k | v | o), g = cap * tanh((W_if x + b_if) / cap);
 // the mLSTM step (state C in place, n / m from buffer `cur` to buffer `next`); z = sigmoid(o) *
 // rmsnorm_head(h_mlstm) * mh_norm; h2 = h + W_out z; a = silu(W_gate x2) * (W_up x2) with
